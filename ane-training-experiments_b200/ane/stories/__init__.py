@@ -1,0 +1,456 @@
+"""Host-side mirror of the reference's `ane/stories` package over the CUDA C ABI.
+
+Go reference (tmc/ane-training-experiments):
+  ane/stories/config.go:3-28     model constants, Llama2Config
+  ane/stories/weights.go:13-122  LayerWeights / ModelWeights / NewModelWeights / LoadPretrained
+  ane/stories/infer.go:15-202    DecodeOptions / DecodeResult / Decoder (NewDecoder, Decode,
+                                 EvalNextLogits, ResetCache)
+  ane/stories/tokenizer.go:16-69 Tokenizer / LoadTokenizer / Decode
+
+Names, argument meaning and error texts follow the Go package; the Decoder runs on the
+B200 through lib/libllm_cuda.so (no CPU fallback).  Additions beyond the Go API are the
+runtime ModelConfig (Stories110M and Qwen3-0.6B presets), the dtype/device arguments of
+NewDecoder, and the batched DecodeBatch.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import struct
+from dataclasses import dataclass, field
+from typing import List, Optional
+
+import numpy as np
+
+from .. import _abi
+from .._abi import LLMError
+
+# ane/stories/config.go:3-10
+Dim = 768
+Hidden = 2048
+Heads = 12
+SeqDefault = 256
+NLayers = 12
+Vocab = 32000
+
+BOS = 1  # ane/stories/infer.go:10
+EOS = 2  # ane/stories/infer.go:11
+
+
+@dataclass(frozen=True)
+class ModelConfig:
+    """Runtime model description (the Go code hard-codes Stories110M in config.go)."""
+
+    dim: int
+    hidden: int
+    n_layers: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    vocab: int
+    max_seq: int = SeqDefault
+    qk_norm: bool = False
+    tied_embed: bool = True
+    norm_eps: float = 1e-5
+    rope_theta: float = 10000.0
+    name: str = "custom"
+
+    @property
+    def q_dim(self) -> int:
+        return self.n_heads * self.head_dim
+
+    @property
+    def kv_dim(self) -> int:
+        return self.n_kv_heads * self.head_dim
+
+    def with_max_seq(self, max_seq: int) -> "ModelConfig":
+        return ModelConfig(**{**self.__dict__, "max_seq": max_seq})
+
+    def c_struct(self) -> _abi.llm_model_config:
+        return _abi.llm_model_config(
+            self.dim, self.hidden, self.n_layers, self.n_heads, self.n_kv_heads, self.head_dim, self.vocab,
+            self.max_seq, int(self.qk_norm), int(self.tied_embed), float(self.norm_eps), float(self.rope_theta))
+
+    def oracle_dict(self) -> dict:
+        return dict(dim=self.dim, hidden=self.hidden, n_layers=self.n_layers, n_heads=self.n_heads,
+                    n_kv_heads=self.n_kv_heads, head_dim=self.head_dim, vocab=self.vocab, max_seq=self.max_seq,
+                    qk_norm=int(self.qk_norm), norm_eps=self.norm_eps, rope_theta=self.rope_theta)
+
+
+# ane/stories/config.go:3-10, ane/stories/infer.go:102,307
+STORIES_110M = ModelConfig(Dim, Hidden, NLayers, Heads, Heads, Dim // Heads, Vocab, SeqDefault,
+                           qk_norm=False, tied_embed=True, norm_eps=1e-5, rope_theta=10000.0, name="stories110m")
+# training/training_dynamic/models/qwen3_06b.h:6-16 plus the Qwen3 features of the spec
+# (per-head QK RMSNorm, theta 1e6, eps 1e-6, tied 151936 vocab)
+QWEN3_0_6B = ModelConfig(1024, 3072, 28, 16, 8, 128, 151936, 4096, qk_norm=True, tied_embed=True,
+                         norm_eps=1e-6, rope_theta=1e6, name="qwen3-0.6b")
+
+PRESETS = {"stories110m": STORIES_110M, "qwen3-0.6b": QWEN3_0_6B}
+
+
+@dataclass
+class LayerWeights:
+    """ane/stories/weights.go:13-17 (fp32, row-major [out, in]) plus Qwen3 q/k norms."""
+
+    Wq: np.ndarray
+    Wk: np.ndarray
+    Wv: np.ndarray
+    Wo: np.ndarray
+    W1: np.ndarray
+    W2: np.ndarray
+    W3: np.ndarray
+    RMSAtt: np.ndarray
+    RMSFFN: np.ndarray
+    QNorm: Optional[np.ndarray] = None
+    KNorm: Optional[np.ndarray] = None
+
+
+@dataclass
+class ModelWeights:
+    """ane/stories/weights.go:19-24."""
+
+    Layers: List[LayerWeights]
+    RMSFinal: np.ndarray
+    Embed: np.ndarray  # [vocab, dim]
+    SharedCL: bool = True
+    LMHead: Optional[np.ndarray] = None  # only when not SharedCL
+    Config: ModelConfig = STORIES_110M
+
+    def c_struct(self):
+        """ctypes view (keeps the numpy arrays referenced by the returned tuple)."""
+        layers = (_abi.llm_layer_weights_f32 * len(self.Layers))()
+        keep = []
+        for i, L in enumerate(self.Layers):
+            for name, arr in (("wq", L.Wq), ("wk", L.Wk), ("wv", L.Wv), ("wo", L.Wo), ("w1", L.W1), ("w2", L.W2),
+                              ("w3", L.W3), ("rms_att", L.RMSAtt), ("rms_ffn", L.RMSFFN), ("q_norm", L.QNorm),
+                              ("k_norm", L.KNorm)):
+                if arr is not None:
+                    a = _abi.f32(arr)
+                    keep.append(a)
+                    setattr(layers[i], name, _abi.ptr(a))
+        emb = _abi.f32(self.Embed)
+        fin = _abi.f32(self.RMSFinal)
+        keep += [emb, fin, layers]
+        lm = None
+        if not self.SharedCL:
+            lm = _abi.f32(self.LMHead)
+            keep.append(lm)
+        w = _abi.llm_model_weights_f32(_abi.ptr(emb), _abi.ptr(fin), _abi.ptr(lm), layers)
+        return w, keep
+
+
+def NewModelWeights(vocab: int = Vocab, cfg: ModelConfig = STORIES_110M) -> ModelWeights:
+    """ane/stories/weights.go:26-47: zeroed weights of the given config."""
+    D, F, Q, KV, hd = cfg.dim, cfg.hidden, cfg.q_dim, cfg.kv_dim, cfg.head_dim
+    z = lambda *s: np.zeros(s, dtype=np.float32)  # noqa: E731
+    layers = [LayerWeights(z(Q, D), z(KV, D), z(KV, D), z(D, Q), z(F, D), z(D, F), z(F, D), z(D), z(D),
+                           z(hd) if cfg.qk_norm else None, z(hd) if cfg.qk_norm else None) for _ in range(cfg.n_layers)]
+    return ModelWeights(layers, z(D), z(vocab, D), True, None, cfg)
+
+
+def SyntheticWeights(cfg: ModelConfig, seed: int = 1234, out_proj_scale: float = 1.0,
+                     stddev: float = 0.02) -> ModelWeights:
+    """Seeded N(0, stddev) weights from the library's counter-based generator (with the
+    default 0.02 these are the values llm_load_weights_synthetic uploads); Wo and W2 also
+    x out_proj_scale; norms = 1."""
+    D, F, Q, KV, hd = cfg.dim, cfg.hidden, cfg.q_dim, cfg.kv_dim, cfg.head_dim
+    g = lambda n, l, k, s=1.0: _abi.synth_normal(n, seed, _abi.synth_stream(l, k), stddev, s)  # noqa: E731
+    layers = []
+    for l in range(cfg.n_layers):
+        layers.append(LayerWeights(
+            g(Q * D, l, 0).reshape(Q, D), g(KV * D, l, 1).reshape(KV, D), g(KV * D, l, 2).reshape(KV, D),
+            g(D * Q, l, 3, out_proj_scale).reshape(D, Q), g(F * D, l, 4).reshape(F, D),
+            g(D * F, l, 5, out_proj_scale).reshape(D, F), g(F * D, l, 6).reshape(F, D),
+            np.ones(D, np.float32), np.ones(D, np.float32),
+            np.ones(hd, np.float32) if cfg.qk_norm else None, np.ones(hd, np.float32) if cfg.qk_norm else None))
+    emb = g(cfg.vocab * D, 0, 7).reshape(cfg.vocab, D)
+    lm = None if cfg.tied_embed else g(cfg.vocab * D, 0, 8).reshape(cfg.vocab, D)
+    return ModelWeights(layers, np.ones(D, np.float32), emb, cfg.tied_embed, lm, cfg)
+
+
+def LoadPretrained(path: str, cfg: Optional[ModelConfig] = None):
+    """ane/stories/weights.go:49-122: llama2.c .bin reader (header of 7 int32, then embed,
+    rms_att[L], wq[L], wk[L], wv[L], wo[L], rms_ffn[L], w1[L], w2[L], w3[L], rms_final;
+    vocab < 0 means an unshared classifier follows... the Go loader only records SharedCL)."""
+    with open(path, "rb") as f:
+        hdr = f.read(28)
+        if len(hdr) != 28:
+            raise ValueError("read config: unexpected EOF")
+        dim, hidden, n_layers, n_heads, n_kv, vocab, seq = struct.unpack("<7i", hdr)
+        cfg = cfg or STORIES_110M
+        if dim != cfg.dim or hidden != cfg.hidden or n_layers != cfg.n_layers:
+            raise ValueError(f"config mismatch: got dim={dim} hidden={hidden} layers={n_layers}")
+        shared = vocab > 0
+        vocab = abs(vocab)
+        mw = NewModelWeights(vocab, cfg)
+        mw.SharedCL = shared
+
+        def rd(arr, what):
+            b = f.read(arr.nbytes)
+            if len(b) != arr.nbytes:
+                raise ValueError(f"read {what}: unexpected EOF")
+            arr[...] = np.frombuffer(b, dtype="<f4").reshape(arr.shape)
+
+        rd(mw.Embed, "embed")
+        for name, attr in (("rms_att", "RMSAtt"), ("wq", "Wq"), ("wk", "Wk"), ("wv", "Wv"), ("wo", "Wo"),
+                           ("rms_ffn", "RMSFFN"), ("w1", "W1"), ("w2", "W2"), ("w3", "W3")):
+            for i, L in enumerate(mw.Layers):
+                rd(getattr(L, attr), f"{name}[{i}]")
+        rd(mw.RMSFinal, "rms_final")
+    return mw, dict(Dim=dim, HiddenDim=hidden, NLayers=n_layers, NHeads=n_heads, NKVHeads=n_kv,
+                    VocabSize=vocab if shared else -vocab, SeqLen=seq)
+
+
+class Tokenizer:
+    """ane/stories/tokenizer.go:11-69 (decode only)."""
+
+    def __init__(self, vocab: List[str]):
+        self.vocab = vocab
+
+    def Decode(self, id: int) -> str:
+        if id < 0 or id >= len(self.vocab):
+            return ""
+        s = self.vocab[id]
+        if len(s) >= 5 and s.startswith("<0x") and s.endswith(">"):
+            try:
+                return bytes([int(s[3:-1], 16)]).decode("latin-1")
+            except ValueError:
+                return s
+        return s
+
+
+def LoadTokenizer(path: str, vocab_size: int = Vocab) -> Tokenizer:
+    """ane/stories/tokenizer.go:16-55."""
+    with open(path, "rb") as f:
+        b = f.read(4)
+        if len(b) != 4:
+            raise ValueError("read tokenizer header: EOF")
+        (max_len,) = struct.unpack("<i", b)
+        if max_len <= 0:
+            raise ValueError(f"bad tokenizer header: max token len={max_len}")
+        vocab = []
+        for i in range(vocab_size):
+            b = f.read(4)
+            if len(b) != 4:
+                raise ValueError(f"unexpected EOF at token {i}")
+            b = f.read(4)
+            if len(b) != 4:
+                raise ValueError(f"read token[{i}] length: EOF")
+            (n,) = struct.unpack("<i", b)
+            if n < 0 or n > max_len * 8:
+                raise ValueError(f"bad token[{i}] length={n}")
+            s = f.read(n)
+            if len(s) != n:
+                raise ValueError(f"read token[{i}] bytes: EOF")
+            vocab.append(s.decode("utf-8", errors="replace"))
+    return Tokenizer(vocab)
+
+
+@dataclass
+class DecodeOptions:
+    """ane/stories/infer.go:15-21."""
+
+    MaxNewTokens: int = 0
+    Temperature: float = 0.0
+    Seed: int = 0
+    PromptTokens: List[int] = field(default_factory=list)
+
+
+@dataclass
+class DecodeResult:
+    """ane/stories/infer.go:23-28."""
+
+    Tokens: List[int]
+    PromptLength: int
+    Text: str = ""
+    StoppedOnEOS: bool = False
+
+
+class Engine:
+    """One CUDA context: weights on one device plus a paged KV cache of `max_batch`
+    sequence slots of up to `max_pos` positions.  Thin wrapper of the C ABI."""
+
+    def __init__(self, cfg: ModelConfig, dtype: str = "bf16", device: int = 0):
+        self.cfg = cfg
+        self.dtype = dtype
+        h = C.c_void_p()
+        _abi.check(_abi.lib().llm_ctx_create(C.byref(cfg.c_struct()), _abi.DTYPES[dtype], device, C.byref(h)))
+        self.h = h
+        self.max_batch = 0
+        self.max_pos = 0
+
+    def load(self, w: ModelWeights) -> "Engine":
+        cw, keep = w.c_struct()
+        _abi.check(_abi.lib().llm_load_weights_f32(self.h, C.byref(cw)))
+        del keep
+        return self
+
+    def load_synthetic(self, seed: int, out_proj_scale: float = 1.0) -> "Engine":
+        _abi.check(_abi.lib().llm_load_weights_synthetic(self.h, seed, out_proj_scale))
+        return self
+
+    def kv_alloc(self, max_batch: int, max_pos: int) -> "Engine":
+        _abi.check(_abi.lib().llm_kv_alloc(self.h, max_batch, max_pos, 16))
+        self.max_batch, self.max_pos = max_batch, max_pos
+        return self
+
+    def release(self, seq: int) -> None:
+        _abi.check(_abi.lib().llm_seq_release(self.h, seq))
+
+    def prefill(self, seq_ids, prompts: List[List[int]], start_pos=None, want_logits=False):
+        seq = _abi.i32(seq_ids)
+        lens = _abi.i32([len(p) for p in prompts])
+        flat = _abi.i32([t for p in prompts for t in p])
+        sp = None if start_pos is None else _abi.i32(start_pos)
+        nxt = np.zeros(len(prompts), np.int32)
+        lg = np.zeros((len(prompts), self.cfg.vocab), np.float32) if want_logits else None
+        _abi.check(_abi.lib().llm_prefill(self.h, _abi.ptr(seq, C.c_int32), _abi.ptr(flat, C.c_int32),
+                                          _abi.ptr(lens, C.c_int32), _abi.ptr(sp, C.c_int32), len(prompts),
+                                          _abi.ptr(nxt, C.c_int32), _abi.ptr(lg)))
+        return (nxt, lg) if want_logits else nxt
+
+    def decode_step(self, seq_ids, tokens, positions, want_logits=False):
+        seq, tok, pos = _abi.i32(seq_ids), _abi.i32(tokens), _abi.i32(positions)
+        n = len(seq)
+        nxt = np.zeros(n, np.int32)
+        lg = np.zeros((n, self.cfg.vocab), np.float32) if want_logits else None
+        _abi.check(_abi.lib().llm_decode_step(self.h, _abi.ptr(seq, C.c_int32), _abi.ptr(tok, C.c_int32),
+                                              _abi.ptr(pos, C.c_int32), n, _abi.ptr(nxt, C.c_int32), _abi.ptr(lg)))
+        return (nxt, lg) if want_logits else nxt
+
+    def generate(self, seq_ids, tokens, positions, steps: int) -> np.ndarray:
+        seq, tok, pos = _abi.i32(seq_ids), _abi.i32(tokens), _abi.i32(positions)
+        out = np.zeros((steps, len(seq)), np.int32)
+        _abi.check(_abi.lib().llm_generate(self.h, _abi.ptr(seq, C.c_int32), _abi.ptr(tok, C.c_int32),
+                                           _abi.ptr(pos, C.c_int32), len(seq), steps, _abi.ptr(out, C.c_int32)))
+        return out
+
+    def generate_begin(self, seq_ids, tokens, positions, max_steps: int) -> None:
+        seq, tok, pos = _abi.i32(seq_ids), _abi.i32(tokens), _abi.i32(positions)
+        _abi.check(_abi.lib().llm_generate_begin(self.h, _abi.ptr(seq, C.c_int32), _abi.ptr(tok, C.c_int32),
+                                                 _abi.ptr(pos, C.c_int32), len(seq), max_steps))
+        self._gen_n = len(seq)
+        self._gen_max = max_steps
+
+    def generate_steps(self, steps: int) -> None:
+        _abi.check(_abi.lib().llm_generate_steps(self.h, steps))
+
+    def generate_end(self) -> np.ndarray:
+        out = np.zeros((self._gen_max, self._gen_n), np.int32)
+        done = C.c_int32()
+        _abi.check(_abi.lib().llm_generate_end(self.h, _abi.ptr(out, C.c_int32), C.byref(done)))
+        return out[: done.value]
+
+    def stream(self) -> int:
+        s = C.c_void_p()
+        _abi.check(_abi.lib().llm_ctx_stream(self.h, C.byref(s)))
+        return s.value or 0
+
+    def synchronize(self) -> None:
+        _abi.check(_abi.lib().llm_synchronize(self.h))
+
+    def kernel_count(self, n: int) -> int:
+        v = C.c_int32()
+        _abi.check(_abi.lib().llm_step_kernel_count(self.h, n, C.byref(v)))
+        return v.value
+
+    def memory(self) -> dict:
+        a, b, c = C.c_uint64(), C.c_uint64(), C.c_uint64()
+        _abi.check(_abi.lib().llm_memory_bytes(self.h, C.byref(a), C.byref(b), C.byref(c)))
+        return dict(weights=a.value, kv_pool=b.value, other=c.value)
+
+    def time_attention(self, iters: int):
+        us, by = C.c_double(), C.c_double()
+        _abi.check(_abi.lib().llm_time_attention(self.h, iters, C.byref(us), C.byref(by)))
+        return us.value, by.value
+
+    def read_kv(self, layer: int, seq: int, pos: int):
+        k = np.zeros(self.cfg.kv_dim, np.float32)
+        v = np.zeros(self.cfg.kv_dim, np.float32)
+        _abi.check(_abi.lib().llm_debug_read_kv(self.h, layer, seq, pos, _abi.ptr(k), _abi.ptr(v)))
+        return k, v
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            _abi.lib().llm_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Decoder:
+    """ane/stories/infer.go:30-59: KV-cached decoder, here backed by the CUDA Engine."""
+
+    def __init__(self, engine: Engine, maxSeq: int, seed: int):
+        self.engine = engine
+        self.maxSeq = maxSeq
+        self.seed = seed
+
+    def ResetCache(self) -> None:
+        """infer.go:62-71."""
+        for s in range(self.engine.max_batch):
+            self.engine.release(s)
+
+    def EvalNextLogits(self, token: int, pos: int) -> np.ndarray:
+        """infer.go:73-77: logits after `token` at `pos` (sequence slot 0)."""
+        if token < 0 or token >= self.engine.cfg.vocab:
+            raise LLMError(_abi.LLM_ERR_TOKEN_RANGE, f"token out of range: {token}")
+        if pos < 0 or pos >= self.maxSeq:
+            raise LLMError(_abi.LLM_ERR_POS_RANGE, f"position out of range: {pos}")
+        _, lg = self.engine.decode_step([0], [token], [pos], want_logits=True)
+        return lg[0]
+
+    def Decode(self, tok: Optional[Tokenizer], opts: DecodeOptions) -> DecodeResult:
+        """infer.go:136-202 (greedy)."""
+        return self.DecodeBatch(tok, opts, [opts.PromptTokens])[0]
+
+    def DecodeBatch(self, tok: Optional[Tokenizer], opts: DecodeOptions, prompts: List[List[int]]) -> List[DecodeResult]:
+        """Decode of len(prompts) independent sequences in one batch (slots 0..n-1)."""
+        n = len(prompts)
+        if n > self.engine.max_batch:
+            raise LLMError(_abi.LLM_ERR_INVALID, f"batch {n} exceeds the decoder's {self.engine.max_batch} slots")
+        if opts.Temperature < 0:
+            opts = DecodeOptions(opts.MaxNewTokens, 0.0, opts.Seed, opts.PromptTokens)
+        lens = _abi.i32([len(p) for p in prompts])
+        flat = _abi.i32([t for p in prompts for t in p] or [0])
+        out = np.zeros((n, self.maxSeq), np.int32)
+        ntok = np.zeros(n, np.int32)
+        plen = np.zeros(n, np.int32)
+        eos = np.zeros(n, np.int32)
+        _abi.check(_abi.lib().llm_stories_decode_batch(
+            self.engine.h, _abi.ptr(flat, C.c_int32), _abi.ptr(lens, C.c_int32), n, int(opts.MaxNewTokens),
+            float(opts.Temperature), _abi.ptr(out, C.c_int32), _abi.ptr(ntok, C.c_int32), _abi.ptr(plen, C.c_int32),
+            _abi.ptr(eos, C.c_int32)))
+        res = []
+        for i in range(n):
+            toks = out[i, : ntok[i]].tolist()
+            text = "".join(tok.Decode(t) for t in toks[plen[i]:]) if tok is not None else ""
+            res.append(DecodeResult(toks, int(plen[i]), text, bool(eos[i])))
+        return res
+
+    def Close(self) -> None:
+        self.engine.close()
+
+
+def NewDecoder(w: Optional[ModelWeights], maxSeq: int, seed: int, dtype: str = "fp16", device: int = 0,
+               max_batch: int = 1) -> Decoder:
+    """infer.go:80-133.  maxSeq <= 0 selects SeqDefault; it is not clamped to 256 (the
+    CUDA path serves contexts up to the config's max_seq)."""
+    if w is None:
+        raise LLMError(_abi.LLM_ERR_INVALID, "nil model weights")
+    cfg = w.Config
+    if maxSeq <= 0:
+        maxSeq = SeqDefault
+    if len(w.Layers) != cfg.n_layers:
+        raise LLMError(_abi.LLM_ERR_INVALID, f"layers={len(w.Layers)} want={cfg.n_layers}")
+    if w.Embed.size % cfg.dim != 0:
+        raise LLMError(_abi.LLM_ERR_INVALID, f"embed size={w.Embed.size} not divisible by dim={cfg.dim}")
+    if maxSeq > cfg.max_seq:
+        cfg = cfg.with_max_seq(maxSeq)
+    eng = Engine(cfg, dtype, device)
+    eng.load(w)
+    eng.kv_alloc(max_batch, maxSeq)
+    return Decoder(eng, maxSeq, seed)

@@ -1,0 +1,182 @@
+// common.cuh -- device helpers shared by the token-loop kernels (sm_100a).
+//
+// Inline PTX wrappers for the instructions the kernels are built from: warp-level
+// tensor-core MMA (bf16/fp16 -> f32, s8 -> s32), ldmatrix, 16-byte cp.async with zero
+// fill, mbarrier waits with an iteration bound, and the bulk (TMA) global->shared copy.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace llm {
+
+// Error words a kernel writes into the context's device error flag.
+enum DeviceError : int {
+  kDevOk = 0,
+  kDevWaitTimeout = 1,  // an mbarrier wait exceeded its iteration bound
+  kDevBadPage = 2,      // a block-table entry pointed outside the page pool
+};
+
+// Bound on mbarrier polls.  Each try_wait may itself suspend the thread for a
+// hardware-defined interval, so this is far longer than any legitimate wait.
+constexpr uint32_t kMaxWaitPolls = 1u << 24;
+
+// ----------------------------------------------------------------------------- types
+template <typename T> struct ActTraits;
+template <> struct ActTraits<__half> {
+  static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
+  static __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  static __device__ __forceinline__ float2 unpack2(uint32_t v) {
+    __half2 h = *reinterpret_cast<__half2*>(&v);
+    return __half22float2(h);
+  }
+};
+template <> struct ActTraits<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+  static __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  static __device__ __forceinline__ float2 unpack2(uint32_t v) {
+    return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+  }
+};
+
+// ----------------------------------------------------------------------------- mma.sync
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
+                                          __half) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
+                                          __nv_bfloat16) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// s8 x s8 -> s32, k = 32 bytes per instruction.
+__device__ __forceinline__ void mma_16832_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], uint32_t saddr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(saddr));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], uint32_t saddr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(saddr));
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ----------------------------------------------------------------------------- cp.async
+// 16-byte async copy; src_bytes == 0 zero-fills the destination (out-of-range rows).
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+// ----------------------------------------------------------------------------- mbarrier + bulk copy
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+// Returns true once the phase with parity `parity` has completed.
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false when the bound ran out (the caller reports kDevWaitTimeout).
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kMaxWaitPolls; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+// Bulk (TMA engine) copy of `bytes` contiguous bytes from global to this CTA's shared
+// memory, completing `bytes` of transaction count on mbarrier `bar`.  Both addresses
+// 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// ----------------------------------------------------------------------------- misc
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+// float64 xor-butterfly sum: every lane ends with the bitwise-identical total because
+// each level adds the same two operands (IEEE addition is commutative).
+__device__ __forceinline__ double warp_sum_f64(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Order-preserving map of a float to uint32 (larger float -> larger key).
+__device__ __forceinline__ uint32_t float_key(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+// (value desc, index asc) packed so that the unsigned max picks the first maximum.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+  return (static_cast<unsigned long long>(float_key(v)) << 32) | (0xffffffffu - static_cast<uint32_t>(idx));
+}
+__device__ __forceinline__ int argmax_key_index(unsigned long long k) {
+  return static_cast<int>(0xffffffffu - static_cast<uint32_t>(k & 0xffffffffu));
+}
+
+// The bridge quantiser (bridge/ane_bridge.m:389-392) on one value given its row scale:
+// IEEE division, clamp to [-128,127], add +-0.5 in f32, truncate toward zero.
+__device__ __forceinline__ int8_t quant_bridge(float x, float scale) {
+  float v = __fdiv_rn(x, scale);
+  v = fminf(v, 127.0f);
+  v = fmaxf(v, -128.0f);
+  float r = __fadd_rn(v, v >= 0.0f ? 0.5f : -0.5f);
+  return static_cast<int8_t>(__float2int_rz(r));
+}
+
+// Byte offset of 16-byte chunk `chunk` of row `row` in a tile whose rows are `row_bytes`
+// long, XOR-swizzled within each 128-byte group so that 8 consecutive rows reading the
+// same logical chunk hit 8 different bank groups.
+__device__ __forceinline__ uint32_t swz(int row, int chunk, int row_bytes) {
+  return static_cast<uint32_t>(row * row_bytes + ((chunk ^ (row & 7)) << 4));
+}
+
+}  // namespace llm

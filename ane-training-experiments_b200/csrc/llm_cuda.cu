@@ -1,0 +1,1533 @@
+// llm_cuda.cu -- the C ABI of include/llm_cuda.h: context, weights, paged KV cache,
+// the token-loop orchestration (prefill / decode step / device-resident generate with CUDA
+// graphs), the stories.Decoder host mirror, and the bit-exact debug hooks.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <numeric>
+#include <string>
+#include <thread>
+#include <tuple>
+#include <vector>
+
+#include "../../include/llm_cuda.h"
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemm.cuh"
+#include "norm.cuh"
+
+using namespace llm;
+
+// ============================================================================ errors
+namespace {
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define CU(call)                                                                                   \
+  do {                                                                                             \
+    cudaError_t e_ = (call);                                                                       \
+    if (e_ != cudaSuccess) return fail(LLM_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_)); \
+  } while (0)
+
+#define RC(call)                \
+  do {                          \
+    int rc_ = (call);           \
+    if (rc_ != LLM_OK) return rc_; \
+  } while (0)
+}  // namespace
+
+extern "C" int llm_last_error(char* buf, size_t n) {
+  if (buf && n) {
+    size_t k = std::min(n - 1, g_last_error.size());
+    memcpy(buf, g_last_error.data(), k);
+    buf[k] = 0;
+  }
+  return static_cast<int>(g_last_error.size());
+}
+
+// ============================================================================ synthetic weights
+namespace {
+inline uint64_t splitmix64(uint64_t x) {
+  x += 0x9E3779B97F4A7C15ull;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+  return x ^ (x >> 31);
+}
+}  // namespace
+
+extern "C" uint64_t llm_synth_stream(int layer, int kind) {
+  if (kind == 7) return 1;
+  if (kind == 8) return 2;
+  return 100ull + 16ull * static_cast<uint64_t>(layer) + static_cast<uint64_t>(kind);
+}
+
+extern "C" void llm_synth_normal(float* dst, uint64_t n, uint64_t seed, uint64_t stream, double stddev,
+                                 double scale) {
+  const uint64_t key = splitmix64(seed ^ splitmix64(stream * 0xD1B54A32D192ED03ull + 0x8CB92BA72F3D8DD7ull));
+  const double mult = stddev * scale;
+  const uint64_t pairs = (n + 1) / 2;
+  auto work = [&](uint64_t p0, uint64_t p1) {
+    const double two_pi = 6.283185307179586476925286766559;
+    for (uint64_t j = p0; j < p1; ++j) {
+      const uint64_t a = splitmix64(key + 2 * j), b = splitmix64(key + 2 * j + 1);
+      const double u1 = (static_cast<double>(a >> 11) + 0.5) * (1.0 / 9007199254740992.0);
+      const double u2 = static_cast<double>(b >> 11) * (1.0 / 9007199254740992.0);
+      const double r = std::sqrt(-2.0 * std::log(u1));
+      const double z0 = r * std::cos(two_pi * u2), z1 = r * std::sin(two_pi * u2);
+      dst[2 * j] = static_cast<float>(mult * z0);
+      if (2 * j + 1 < n) dst[2 * j + 1] = static_cast<float>(mult * z1);
+    }
+  };
+  unsigned nt = std::max(1u, std::min(32u, std::thread::hardware_concurrency()));
+  if (pairs < (1u << 16)) nt = 1;
+  std::vector<std::thread> th;
+  const uint64_t per = (pairs + nt - 1) / nt;
+  for (unsigned i = 0; i < nt; ++i) {
+    const uint64_t p0 = i * per, p1 = std::min(pairs, p0 + per);
+    if (p0 < p1) th.emplace_back(work, p0, p1);
+  }
+  for (auto& t : th) t.join();
+}
+
+// ============================================================================ small kernels
+namespace {
+
+struct FinishParams {
+  const unsigned long long* part;  // [n_tiles][M]
+  int M, n_tiles;
+  int* next;                       // [M]
+  int* tok_io;                     // optional: tokens <- next
+  int* pos_io;                     // optional: positions += 1
+  const int* gen_start;            // optional with gen_out
+  int* gen_out;                    // [cap][M]
+  int gen_cap;
+};
+
+// Greedy token per row: max over the lm_head tiles' (value, first index) partials.
+__global__ void __launch_bounds__(256) finish_kernel(FinishParams f) {
+  const int row = blockIdx.x * 8 + threadIdx.x / 32, lane = threadIdx.x & 31;
+  if (row >= f.M) return;
+  unsigned long long best = 0ull;
+  for (int t = lane; t < f.n_tiles; t += 32) {
+    const unsigned long long k = f.part[static_cast<size_t>(t) * f.M + row];
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  if (lane == 0) {
+    const int idx = argmax_key_index(best);
+    f.next[row] = idx;
+    if (f.tok_io) f.tok_io[row] = idx;
+    if (f.gen_out) {
+      const int step = f.pos_io[row] - f.gen_start[row];
+      if (step >= 0 && step < f.gen_cap) f.gen_out[static_cast<size_t>(step) * f.M + row] = idx;
+    }
+    if (f.pos_io) f.pos_io[row] += 1;
+  }
+}
+
+// Read one cached K or V row (un-swizzled) as fp32.
+template <typename T>
+__global__ void read_kv_kernel(const T* pool, int layer, int n_pages, int n_kv_heads, int hd, int page, int slot,
+                               float* k, float* v) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int kv_dim = n_kv_heads * hd;
+  if (i >= 2 * kv_dim) return;
+  const int which = i / kv_dim, j = i % kv_dim, head = j / hd, d = j % hd;
+  const size_t blk = ((static_cast<size_t>(layer) * n_pages + page) * n_kv_heads + head) * 2 + which;
+  const T* base = pool + blk * 16 * hd;
+  const int chunk = (d >> 3) ^ (slot & 7);
+  const float val = ActTraits<T>::to_f(base[slot * hd + chunk * 8 + (d & 7)]);
+  (which ? v : k)[j] = val;
+}
+
+template <typename T>
+__global__ void f32_to_act_kernel(const float* src, T* dst, size_t n) {
+  size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
+  if (i < n) dst[i] = ActTraits<T>::from_f(src[i]);
+}
+
+// ---------------------------------------------------------------------------- launchers
+template <typename InT, typename OutT, int BM, int EPI>
+cudaError_t gemm_launch_t(const GemmParams& p, dim3 grid, cudaStream_t s, bool prepare) {
+  constexpr int BN = 128, ST = 4;
+  constexpr int smem = gemm_smem_bytes<BM, BN, ST>();
+  auto k = gemm_kernel<InT, OutT, BM, BN, ST, EPI>;
+  if (prepare) return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  k<<<grid, kGemmThreads, smem, s>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename InT, typename OutT>
+cudaError_t gemm_dispatch(const GemmParams& p, int epi, int bm, dim3 grid, cudaStream_t s, bool prepare) {
+#define LLM_GEMM_CASE(E)                                                                    \
+  case E:                                                                                   \
+    return bm == 64 ? gemm_launch_t<InT, OutT, 64, E>(p, grid, s, prepare)                  \
+                    : gemm_launch_t<InT, OutT, 128, E>(p, grid, s, prepare);
+  switch (epi) {
+    LLM_GEMM_CASE(EPI_F32)
+    LLM_GEMM_CASE(EPI_S32)
+    LLM_GEMM_CASE(EPI_RESID)
+    LLM_GEMM_CASE(EPI_SWIGLU)
+    LLM_GEMM_CASE(EPI_QKV)
+    LLM_GEMM_CASE(EPI_ARGMAX)
+  }
+#undef LLM_GEMM_CASE
+  return cudaErrorInvalidValue;
+}
+
+// act: 1 = fp16, 2 = bf16; in8: int8 A/B
+cudaError_t gemm_any(int act, bool in8, const GemmParams& p, int epi, int bm, dim3 grid, cudaStream_t s,
+                     bool prepare) {
+  if (in8) return act == 1 ? gemm_dispatch<int8_t, __half>(p, epi, bm, grid, s, prepare)
+                           : gemm_dispatch<int8_t, __nv_bfloat16>(p, epi, bm, grid, s, prepare);
+  return act == 1 ? gemm_dispatch<__half, __half>(p, epi, bm, grid, s, prepare)
+                  : gemm_dispatch<__nv_bfloat16, __nv_bfloat16>(p, epi, bm, grid, s, prepare);
+}
+
+template <typename T, int HD>
+cudaError_t attn_launch_t(const AttnParams& p, cudaStream_t s, bool prepare) {
+  auto k = attn_kernel<T, HD>;
+  constexpr int smem = AttnCfg<T, HD>::SMEM;
+  if (prepare) return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  dim3 grid(p.n_blocks, p.n_kv_heads, p.splits);
+  k<<<grid, kAttnWarps * 32, smem, s>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t attn_any(int act, int hd, const AttnParams& p, cudaStream_t s, bool prepare) {
+  if (act == 1) return hd == 64 ? attn_launch_t<__half, 64>(p, s, prepare) : attn_launch_t<__half, 128>(p, s, prepare);
+  return hd == 64 ? attn_launch_t<__nv_bfloat16, 64>(p, s, prepare)
+                  : attn_launch_t<__nv_bfloat16, 128>(p, s, prepare);
+}
+
+cudaError_t norm_any(int act, bool quant, const NormParams& p, cudaStream_t s) {
+  dim3 grid((p.rows + 7) / 8);
+  if (act == 1) {
+    if (quant) norm_rows_kernel<__half, true><<<grid, 256, 0, s>>>(p);
+    else norm_rows_kernel<__half, false><<<grid, 256, 0, s>>>(p);
+  } else {
+    if (quant) norm_rows_kernel<__nv_bfloat16, true><<<grid, 256, 0, s>>>(p);
+    else norm_rows_kernel<__nv_bfloat16, false><<<grid, 256, 0, s>>>(p);
+  }
+  return cudaGetLastError();
+}
+
+struct GemmPlan {
+  int bm = 128, splits = 1, kts = 1, tiles = 1;
+  dim3 grid;
+  size_t ws_floats = 0;
+};
+
+GemmPlan plan_gemm(int M, int N, int K, int esz, int n_sm, int force_splits, size_t ws_cap_floats) {
+  GemmPlan pl;
+  pl.bm = M <= 64 ? 64 : 128;
+  const int mt = (M + pl.bm - 1) / pl.bm, nt = (N + 127) / 128;
+  pl.tiles = mt * nt;
+  const int k_tiles = K * esz / 128;
+  const int occ = pl.bm == 64 ? 2 : 1;
+  const int target = n_sm * occ;
+  int splits = force_splits > 0 ? force_splits
+                                : (pl.tiles >= target ? 1 : std::max(1, std::min(16, target / pl.tiles)));
+  splits = std::max(1, std::min(splits, k_tiles));
+  for (;;) {
+    pl.kts = (k_tiles + splits - 1) / splits;
+    pl.splits = (k_tiles + pl.kts - 1) / pl.kts;
+    pl.ws_floats = pl.splits > 1 ? static_cast<size_t>(pl.splits) * pl.tiles * pl.bm * 128 : 0;
+    if (pl.ws_floats <= ws_cap_floats || splits == 1) break;
+    --splits;
+  }
+  if (pl.splits > 1 && pl.ws_floats > ws_cap_floats) {
+    pl.splits = 1;
+    pl.kts = k_tiles;
+    pl.ws_floats = 0;
+  }
+  pl.grid = dim3(mt, nt, pl.splits);
+  return pl;
+}
+
+}  // namespace
+
+// ============================================================================ context
+struct LayerW {
+  void* wqkv = nullptr;  // [(q_dim + 2 kv_dim) x D]
+  float* sqkv = nullptr;
+  void* wo = nullptr;    // [D x q_dim]
+  float* so = nullptr;
+  void* w13 = nullptr;   // [2F x D], rows interleaved (W1[j], W3[j])
+  float* s13 = nullptr;
+  void* w2 = nullptr;    // [D x F]
+  float* s2 = nullptr;
+  float *rms_att = nullptr, *rms_ffn = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+};
+
+struct GraphKey {
+  int n, splits, mode;  // mode: 0 = step, 1 = step + logits, 2 = generate
+  bool operator<(const GraphKey& o) const { return std::tie(n, splits, mode) < std::tie(o.n, o.splits, o.mode); }
+};
+
+struct llm_ctx {
+  llm_model_config cfg{};
+  int dtype = 0, device = 0, act = 2, n_sm = 148;
+  bool in8 = false;
+  int q_dim = 0, kv_dim = 0, group = 1;
+  cudaStream_t stream = nullptr;
+  std::vector<void*> allocs;
+  uint64_t bytes_weights = 0, bytes_kv = 0, bytes_other = 0;
+
+  // weights
+  bool weights_loaded = false;
+  void* embed = nullptr;
+  void* lm_head = nullptr;
+  float* rms_final = nullptr;
+  std::vector<LayerW> layers;
+  float *rope_cos = nullptr, *rope_sin = nullptr;
+
+  // paged KV
+  bool kv_ready = false;
+  void* kv_pool = nullptr;
+  int n_pages = 0, max_seqs = 0, max_pos = 0, max_pages_per_seq = 0;
+  int* d_block_table = nullptr;
+  std::vector<int> h_block_table, seq_npages, free_pages;
+
+  // activations (max_rows rows)
+  int max_rows = 0;
+  float* x = nullptr;
+  void* xn = nullptr;
+  int8_t* xq = nullptr;
+  float* xs = nullptr;
+  void* qbuf = nullptr;
+  void* attn = nullptr;  // act or fp32
+  int8_t* aq = nullptr;
+  float* as = nullptr;
+  void* gbuf = nullptr;  // act or fp32
+  int8_t* gq = nullptr;
+  float* gs = nullptr;
+  void* xf = nullptr;
+  unsigned long long* argmax_part = nullptr;
+  float* logits = nullptr;
+  size_t logits_rows = 0;
+  int *d_seq = nullptr, *d_tok = nullptr, *d_pos = nullptr, *d_next = nullptr, *d_gen_start = nullptr;
+  int *d_blk_row0 = nullptr, *d_blk_nq = nullptr, *d_final = nullptr;
+  int* d_gen_out = nullptr;
+  size_t gen_out_cap = 0;
+  int32_t* h_pin = nullptr;  // pinned staging
+  size_t h_pin_ints = 0;
+  float* ws = nullptr;
+  size_t ws_floats = 0;
+  int* counters = nullptr;
+  int* d_err = nullptr;
+
+  // generate state
+  int gen_n = 0, gen_steps_done = 0, gen_max_steps = 0, gen_splits = 1;
+  std::vector<int> gen_seq, gen_pos0;
+
+  std::map<GraphKey, cudaGraphExec_t> graphs;
+  bool use_graphs = true;
+};
+
+namespace {
+
+int dalloc(llm_ctx* c, void** p, size_t bytes, uint64_t* counter) {
+  if (bytes == 0) bytes = 16;
+  cudaError_t e = cudaMalloc(p, bytes);
+  if (e != cudaSuccess) return fail(LLM_ERR_OOM, "cudaMalloc(%zu) failed: %s", bytes, cudaGetErrorString(e));
+  c->allocs.push_back(*p);
+  if (counter) *counter += bytes;
+  return LLM_OK;
+}
+template <typename P>
+int dalloc_t(llm_ctx* c, P** p, size_t bytes, uint64_t* counter) {
+  void* v = nullptr;
+  int rc = dalloc(c, &v, bytes, counter);
+  *p = static_cast<P*>(v);
+  return rc;
+}
+
+size_t act_bytes(const llm_ctx* c) { return 2; }
+
+int set_device(const llm_ctx* c) {
+  CU(cudaSetDevice(c->device));
+  return LLM_OK;
+}
+
+int check_device_error(llm_ctx* c) {
+  int h = 0;
+  CU(cudaMemcpyAsync(&h, c->d_err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+  CU(cudaStreamSynchronize(c->stream));
+  if (h != kDevOk) {
+    CU(cudaMemsetAsync(c->d_err, 0, sizeof(int), c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+    return fail(LLM_ERR_DEVICE, "kernel reported device error %d (%s)", h,
+                h == kDevWaitTimeout ? "bounded wait expired" : (h == kDevBadPage ? "bad page index" : "unknown"));
+  }
+  return LLM_OK;
+}
+
+int prepare_kernels(llm_ctx* c) {
+  const int epis[] = {EPI_F32, EPI_S32, EPI_RESID, EPI_SWIGLU, EPI_QKV, EPI_ARGMAX};
+  GemmParams gp{};
+  for (int e : epis)
+    for (int bm : {64, 128}) {
+      CU(gemm_any(c->act, false, gp, e, bm, dim3(1), c->stream, true));
+      if (c->in8) CU(gemm_any(c->act, true, gp, e, bm, dim3(1), c->stream, true));
+    }
+  AttnParams ap{};
+  CU(attn_any(c->act, c->cfg.head_dim, ap, c->stream, true));
+  return LLM_OK;
+}
+
+}  // namespace
+
+extern "C" int llm_ctx_create(const llm_model_config* cfg, int dtype, int device, llm_ctx** out) {
+  if (!cfg || !out) return fail(LLM_ERR_INVALID, "nil config or output handle");
+  *out = nullptr;
+  const llm_model_config& k = *cfg;
+  if (dtype < LLM_DTYPE_F16 || dtype > LLM_DTYPE_W8A8_BF16) return fail(LLM_ERR_INVALID, "unknown dtype %d", dtype);
+  if (k.dim <= 0 || k.hidden <= 0 || k.n_layers <= 0 || k.n_heads <= 0 || k.n_kv_heads <= 0 || k.vocab <= 0 ||
+      k.max_seq <= 0)
+    return fail(LLM_ERR_INVALID, "config dimensions must be positive");
+  if (k.head_dim != 64 && k.head_dim != 128) return fail(LLM_ERR_UNSUPPORTED, "head_dim=%d (supported: 64, 128)", k.head_dim);
+  if (k.n_heads % k.n_kv_heads) return fail(LLM_ERR_INVALID, "heads=%d not a multiple of kv_heads=%d", k.n_heads, k.n_kv_heads);
+  const int group = k.n_heads / k.n_kv_heads;
+  if (group > 8) return fail(LLM_ERR_UNSUPPORTED, "GQA group %d > 8", group);
+  const int q_dim = k.n_heads * k.head_dim, kv_dim = k.n_kv_heads * k.head_dim;
+  if (k.dim % 128 || k.hidden % 128 || q_dim % 128 || kv_dim % 128)
+    return fail(LLM_ERR_UNSUPPORTED, "dim, hidden, heads*head_dim and kv_heads*head_dim must be multiples of 128");
+  if (!(k.norm_eps > 0)) return fail(LLM_ERR_INVALID, "norm_eps must be positive");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
+    return fail(LLM_ERR_CUDA, "no CUDA device available (the token loop has no CPU fallback)");
+  if (device < 0 || device >= ndev) return fail(LLM_ERR_INVALID, "device %d out of range (have %d)", device, ndev);
+
+  llm_ctx* c = new llm_ctx();
+  c->cfg = k;
+  c->dtype = dtype;
+  c->device = device;
+  c->act = (dtype == LLM_DTYPE_F16 || dtype == LLM_DTYPE_W8A8_F16) ? 1 : 2;
+  c->in8 = dtype >= LLM_DTYPE_W8A8_F16;
+  c->q_dim = q_dim;
+  c->kv_dim = kv_dim;
+  c->group = group;
+  auto bail = [&](int rc) {
+    llm_ctx_destroy(c);
+    return rc;
+  };
+  if (cudaSetDevice(device) != cudaSuccess) return bail(fail(LLM_ERR_CUDA, "cudaSetDevice(%d) failed", device));
+  cudaDeviceProp prop{};
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return bail(fail(LLM_ERR_CUDA, "device query failed"));
+  if (prop.major < 10) return bail(fail(LLM_ERR_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a", device, prop.major, prop.minor));
+  c->n_sm = prop.multiProcessorCount;
+  if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess)
+    return bail(fail(LLM_ERR_CUDA, "stream create failed"));
+  // RoPE tables in float64, as ane/stories/infer.go:97-107
+  const int half = k.head_dim / 2;
+  std::vector<float> hc(static_cast<size_t>(k.max_seq) * half), hs(hc.size());
+  for (int pos = 0; pos < k.max_seq; ++pos)
+    for (int i = 0; i < half; ++i) {
+      const double freq = static_cast<double>(pos) / std::pow(k.rope_theta, static_cast<double>(2 * i) / k.head_dim);
+      hc[static_cast<size_t>(pos) * half + i] = static_cast<float>(std::cos(freq));
+      hs[static_cast<size_t>(pos) * half + i] = static_cast<float>(std::sin(freq));
+    }
+  int rc = dalloc_t(c, &c->rope_cos, hc.size() * 4, &c->bytes_other);
+  if (!rc) rc = dalloc_t(c, &c->rope_sin, hs.size() * 4, &c->bytes_other);
+  if (!rc) rc = dalloc_t(c, &c->d_err, 4, &c->bytes_other);
+  if (rc) return bail(rc);
+  if (cudaMemcpy(c->rope_cos, hc.data(), hc.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(c->rope_sin, hs.data(), hs.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemset(c->d_err, 0, 4) != cudaSuccess)
+    return bail(fail(LLM_ERR_CUDA, "table upload failed"));
+  rc = prepare_kernels(c);
+  if (rc) return bail(rc);
+  *out = c;
+  return LLM_OK;
+}
+
+extern "C" int llm_ctx_destroy(llm_ctx* c) {
+  if (!c) return fail(LLM_ERR_INVALID, "nil context");
+  cudaSetDevice(c->device);
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
+  for (void* p : c->allocs) cudaFree(p);
+  if (c->h_pin) cudaFreeHost(c->h_pin);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+  return LLM_OK;
+}
+
+// ============================================================================ weights
+namespace {
+
+// Convert one fp32 host tensor [rows x cols] into device storage; int8 when `quant`.
+int upload_convert(llm_ctx* c, float* dtmp, const float* src, int rows, int cols, void* dst, float* dscale,
+                   bool quant, int row_mul, int row_add) {
+  const size_t n = static_cast<size_t>(rows) * cols;
+  CU(cudaMemcpyAsync(dtmp, src, n * 4, cudaMemcpyHostToDevice, c->stream));
+  ConvertParams p{dtmp, rows, cols, row_mul, row_add, dst, dscale};
+  dim3 grid((rows + 7) / 8);
+  if (quant) convert_rows_kernel<int8_t><<<grid, 256, 0, c->stream>>>(p);
+  else if (c->act == 1) convert_rows_kernel<__half><<<grid, 256, 0, c->stream>>>(p);
+  else convert_rows_kernel<__nv_bfloat16><<<grid, 256, 0, c->stream>>>(p);
+  CU(cudaGetLastError());
+  CU(cudaStreamSynchronize(c->stream));  // dtmp is reused by the next tensor
+  return LLM_OK;
+}
+
+int upload_f32(llm_ctx* c, float** dst, const float* src, size_t n, float fill) {
+  RC(dalloc_t(c, dst, n * 4, &c->bytes_weights));
+  if (src) {
+    CU(cudaMemcpy(*dst, src, n * 4, cudaMemcpyHostToDevice));
+  } else {
+    std::vector<float> ones(n, fill);
+    CU(cudaMemcpy(*dst, ones.data(), n * 4, cudaMemcpyHostToDevice));
+  }
+  return LLM_OK;
+}
+
+// Tensor source: either caller fp32 pointers or the synthetic generator.
+struct Source {
+  const llm_model_weights_f32* w = nullptr;
+  uint64_t seed = 0;
+  float out_scale = 1.f;
+  std::vector<float> host;  // synthetic scratch
+  const float* get(int layer, int kind, size_t n) {
+    if (w) {
+      if (kind == 7) return w->embed;
+      if (kind == 8) return w->lm_head;
+      const llm_layer_weights_f32& L = w->layers[layer];
+      const float* t[7] = {L.wq, L.wk, L.wv, L.wo, L.w1, L.w2, L.w3};
+      return t[kind];
+    }
+    host.resize(n);
+    const double sc = (kind == 3 || kind == 5) ? out_scale : 1.0;
+    llm_synth_normal(host.data(), n, seed, llm_synth_stream(layer, kind), 0.02, sc);
+    return host.data();
+  }
+};
+
+int load_weights(llm_ctx* c, Source& src) {
+  if (c->weights_loaded) return fail(LLM_ERR_STATE, "weights already loaded");
+  RC(set_device(c));
+  const llm_model_config& k = c->cfg;
+  const int D = k.dim, F = k.hidden, V = k.vocab, Q = c->q_dim, KV = c->kv_dim;
+  const size_t ab = act_bytes(c);
+  const size_t wb = c->in8 ? 1 : ab;
+  size_t maxn = std::max({static_cast<size_t>(V) * D, static_cast<size_t>(F) * D, static_cast<size_t>(Q) * D});
+  float* dtmp = nullptr;
+  {
+    void* v = nullptr;
+    CU(cudaMalloc(&v, maxn * 4));
+    dtmp = static_cast<float*>(v);
+  }
+  auto cleanup = [&](int rc) {
+    cudaFree(dtmp);
+    return rc;
+  };
+  int rc;
+  if ((rc = dalloc(c, &c->embed, static_cast<size_t>(V) * D * ab, &c->bytes_weights))) return cleanup(rc);
+  const float* e = src.get(0, 7, static_cast<size_t>(V) * D);
+  if (!e) return cleanup(fail(LLM_ERR_INVALID, "nil embed"));
+  if ((rc = upload_convert(c, dtmp, e, V, D, c->embed, nullptr, false, 1, 0))) return cleanup(rc);
+  if (k.tied_embed) {
+    c->lm_head = c->embed;
+  } else {
+    const float* lh = src.get(0, 8, static_cast<size_t>(V) * D);
+    if (!lh) return cleanup(fail(LLM_ERR_INVALID, "untied model needs lm_head"));
+    if ((rc = dalloc(c, &c->lm_head, static_cast<size_t>(V) * D * ab, &c->bytes_weights))) return cleanup(rc);
+    if ((rc = upload_convert(c, dtmp, lh, V, D, c->lm_head, nullptr, false, 1, 0))) return cleanup(rc);
+  }
+  if ((rc = upload_f32(c, &c->rms_final, src.w ? src.w->rms_final : nullptr, D, 1.f))) return cleanup(rc);
+  c->layers.resize(k.n_layers);
+  const int NQKV = Q + 2 * KV;
+  for (int l = 0; l < k.n_layers; ++l) {
+    LayerW& L = c->layers[l];
+    if ((rc = dalloc(c, &L.wqkv, static_cast<size_t>(NQKV) * D * wb, &c->bytes_weights))) return cleanup(rc);
+    if ((rc = dalloc(c, &L.wo, static_cast<size_t>(D) * Q * wb, &c->bytes_weights))) return cleanup(rc);
+    if ((rc = dalloc(c, &L.w13, static_cast<size_t>(2 * F) * D * wb, &c->bytes_weights))) return cleanup(rc);
+    if ((rc = dalloc(c, &L.w2, static_cast<size_t>(D) * F * wb, &c->bytes_weights))) return cleanup(rc);
+    if (c->in8) {
+      if ((rc = dalloc_t(c, &L.sqkv, NQKV * 4, &c->bytes_weights))) return cleanup(rc);
+      if ((rc = dalloc_t(c, &L.so, D * 4, &c->bytes_weights))) return cleanup(rc);
+      if ((rc = dalloc_t(c, &L.s13, 2 * F * 4, &c->bytes_weights))) return cleanup(rc);
+      if ((rc = dalloc_t(c, &L.s2, D * 4, &c->bytes_weights))) return cleanup(rc);
+    }
+    auto part = [&](int kind, int rows, int cols, void* base, float* sbase, int row_off, int mul, int add) -> int {
+      const float* s = src.get(l, kind, static_cast<size_t>(rows) * cols);
+      if (!s) return fail(LLM_ERR_INVALID, "nil weight (layer %d, tensor %d)", l, kind);
+      uint8_t* dst = static_cast<uint8_t*>(base) + static_cast<size_t>(row_off) * cols * wb;
+      float* ds = sbase ? sbase + row_off : nullptr;
+      return upload_convert(c, dtmp, s, rows, cols, dst, ds, c->in8, mul, add);
+    };
+    if ((rc = part(0, Q, D, L.wqkv, L.sqkv, 0, 1, 0))) return cleanup(rc);
+    if ((rc = part(1, KV, D, L.wqkv, L.sqkv, Q, 1, 0))) return cleanup(rc);
+    if ((rc = part(2, KV, D, L.wqkv, L.sqkv, Q + KV, 1, 0))) return cleanup(rc);
+    if ((rc = part(3, D, Q, L.wo, L.so, 0, 1, 0))) return cleanup(rc);
+    if ((rc = part(4, F, D, L.w13, L.s13, 0, 2, 0))) return cleanup(rc);
+    if ((rc = part(6, F, D, L.w13, L.s13, 0, 2, 1))) return cleanup(rc);
+    if ((rc = part(5, D, F, L.w2, L.s2, 0, 1, 0))) return cleanup(rc);
+    const llm_layer_weights_f32* lw = src.w ? &src.w->layers[l] : nullptr;
+    if ((rc = upload_f32(c, &L.rms_att, lw ? lw->rms_att : nullptr, D, 1.f))) return cleanup(rc);
+    if ((rc = upload_f32(c, &L.rms_ffn, lw ? lw->rms_ffn : nullptr, D, 1.f))) return cleanup(rc);
+    if (k.qk_norm) {
+      if ((rc = upload_f32(c, &L.q_norm, lw ? lw->q_norm : nullptr, k.head_dim, 1.f))) return cleanup(rc);
+      if ((rc = upload_f32(c, &L.k_norm, lw ? lw->k_norm : nullptr, k.head_dim, 1.f))) return cleanup(rc);
+    }
+    if (lw && (!lw->rms_att || !lw->rms_ffn || (k.qk_norm && (!lw->q_norm || !lw->k_norm))))
+      return cleanup(fail(LLM_ERR_INVALID, "nil norm weight in layer %d", l));
+  }
+  c->weights_loaded = true;
+  return cleanup(LLM_OK);
+}
+
+}  // namespace
+
+extern "C" int llm_load_weights_f32(llm_ctx* c, const llm_model_weights_f32* w) {
+  if (!c || !w || !w->layers || !w->embed || !w->rms_final) return fail(LLM_ERR_INVALID, "nil context or weights");
+  Source s;
+  s.w = w;
+  return load_weights(c, s);
+}
+
+extern "C" int llm_load_weights_synthetic(llm_ctx* c, uint64_t seed, float out_proj_scale) {
+  if (!c) return fail(LLM_ERR_INVALID, "nil context");
+  Source s;
+  s.seed = seed;
+  s.out_scale = out_proj_scale;
+  return load_weights(c, s);
+}
+
+// ============================================================================ KV cache
+extern "C" int llm_kv_alloc(llm_ctx* c, int max_seqs, int max_pos, int page_tokens) {
+  if (!c) return fail(LLM_ERR_INVALID, "nil context");
+  if (c->kv_ready) return fail(LLM_ERR_STATE, "KV cache already allocated");
+  if (page_tokens != 16) return fail(LLM_ERR_UNSUPPORTED, "page_tokens=%d (supported: 16)", page_tokens);
+  if (max_seqs <= 0 || max_pos <= 0) return fail(LLM_ERR_INVALID, "max_seqs and max_pos must be positive");
+  if (max_pos > c->cfg.max_seq) return fail(LLM_ERR_INVALID, "max_pos=%d exceeds the config's max_seq=%d", max_pos, c->cfg.max_seq);
+  RC(set_device(c));
+  const llm_model_config& k = c->cfg;
+  c->max_seqs = max_seqs;
+  c->max_pos = max_pos;
+  c->max_pages_per_seq = (max_pos + 15) / 16;
+  c->n_pages = max_seqs * c->max_pages_per_seq;
+  const size_t page_bytes = static_cast<size_t>(k.n_kv_heads) * 2 * 16 * k.head_dim * act_bytes(c);
+  RC(dalloc(c, &c->kv_pool, static_cast<size_t>(k.n_layers) * c->n_pages * page_bytes, &c->bytes_kv));
+  CU(cudaMemset(c->kv_pool, 0, static_cast<size_t>(k.n_layers) * c->n_pages * page_bytes));
+  RC(dalloc_t(c, &c->d_block_table, static_cast<size_t>(max_seqs) * c->max_pages_per_seq * 4, &c->bytes_other));
+  c->h_block_table.assign(static_cast<size_t>(max_seqs) * c->max_pages_per_seq, -1);
+  CU(cudaMemcpy(c->d_block_table, c->h_block_table.data(), c->h_block_table.size() * 4, cudaMemcpyHostToDevice));
+  c->seq_npages.assign(max_seqs, 0);
+  // free list in a scrambled order so block tables are never the identity map
+  int stride = c->n_pages / 2 + 1;
+  while (std::gcd(stride, c->n_pages) != 1) ++stride;
+  c->free_pages.resize(c->n_pages);
+  for (int i = 0; i < c->n_pages; ++i)
+    c->free_pages[c->n_pages - 1 - i] = static_cast<int>((static_cast<long long>(i) * stride) % c->n_pages);
+
+  // activation buffers
+  const int R = std::max(max_seqs, 4096);
+  c->max_rows = R;
+  const size_t D = k.dim, F = k.hidden, Q = c->q_dim, V = k.vocab, ab = act_bytes(c);
+  uint64_t* o = &c->bytes_other;
+  RC(dalloc_t(c, &c->x, R * D * 4, o));
+  RC(dalloc(c, &c->xn, R * D * ab, o));
+  RC(dalloc_t(c, &c->xq, R * D, o));
+  RC(dalloc_t(c, &c->xs, R * 4, o));
+  RC(dalloc(c, &c->qbuf, R * Q * ab, o));
+  RC(dalloc(c, &c->attn, R * Q * 4, o));
+  RC(dalloc_t(c, &c->aq, R * Q, o));
+  RC(dalloc_t(c, &c->as, R * 4, o));
+  RC(dalloc(c, &c->gbuf, R * F * 4, o));
+  RC(dalloc_t(c, &c->gq, R * F, o));
+  RC(dalloc_t(c, &c->gs, R * 4, o));
+  RC(dalloc(c, &c->xf, R * D * ab, o));
+  RC(dalloc_t(c, &c->argmax_part, ((V + 127) / 128) * R * 8, o));
+  for (int** p : {&c->d_seq, &c->d_tok, &c->d_pos, &c->d_next, &c->d_gen_start, &c->d_blk_row0, &c->d_blk_nq, &c->d_final})
+    RC(dalloc_t(c, p, R * 4, o));
+  c->ws_floats = 16u << 20;  // 64 MB split-K / split-attention workspace
+  RC(dalloc_t(c, &c->ws, c->ws_floats * 4, o));
+  RC(dalloc_t(c, &c->counters, 65536 * 4, o));
+  CU(cudaMemset(c->counters, 0, 65536 * 4));
+  c->h_pin_ints = static_cast<size_t>(R) * 8;
+  CU(cudaMallocHost(&c->h_pin, c->h_pin_ints * 4));
+  c->kv_ready = true;
+  return LLM_OK;
+}
+
+extern "C" int llm_seq_release(llm_ctx* c, int seq) {
+  if (!c || !c->kv_ready) return fail(LLM_ERR_STATE, "KV cache not allocated");
+  if (seq < 0 || seq >= c->max_seqs) return fail(LLM_ERR_INVALID, "sequence %d out of range", seq);
+  int* row = c->h_block_table.data() + static_cast<size_t>(seq) * c->max_pages_per_seq;
+  for (int i = 0; i < c->seq_npages[seq]; ++i) {
+    c->free_pages.push_back(row[i]);
+    row[i] = -1;
+  }
+  c->seq_npages[seq] = 0;
+  RC(set_device(c));
+  CU(cudaMemcpyAsync(c->d_block_table + static_cast<size_t>(seq) * c->max_pages_per_seq, row,
+                     c->max_pages_per_seq * 4, cudaMemcpyHostToDevice, c->stream));
+  CU(cudaStreamSynchronize(c->stream));
+  return LLM_OK;
+}
+
+namespace {
+
+// Make sure sequence `seq` owns pages for positions [0, upto]; uploads changed rows.
+int ensure_pages(llm_ctx* c, int seq, int upto, std::vector<int>* dirty) {
+  const int need = upto / 16 + 1;
+  if (need > c->max_pages_per_seq) return fail(LLM_ERR_POS_RANGE, "position out of range: %d", upto);
+  int* row = c->h_block_table.data() + static_cast<size_t>(seq) * c->max_pages_per_seq;
+  bool changed = false;
+  while (c->seq_npages[seq] < need) {
+    if (c->free_pages.empty()) return fail(LLM_ERR_OOM, "KV page pool exhausted");
+    row[c->seq_npages[seq]++] = c->free_pages.back();
+    c->free_pages.pop_back();
+    changed = true;
+  }
+  if (changed) dirty->push_back(seq);
+  return LLM_OK;
+}
+
+int upload_dirty(llm_ctx* c, std::vector<int>& dirty) {
+  std::sort(dirty.begin(), dirty.end());
+  dirty.erase(std::unique(dirty.begin(), dirty.end()), dirty.end());
+  for (int s : dirty)
+    CU(cudaMemcpyAsync(c->d_block_table + static_cast<size_t>(s) * c->max_pages_per_seq,
+                       c->h_block_table.data() + static_cast<size_t>(s) * c->max_pages_per_seq,
+                       c->max_pages_per_seq * 4, cudaMemcpyHostToDevice, c->stream));
+  dirty.clear();
+  return LLM_OK;
+}
+
+int check_ready(llm_ctx* c) {
+  if (!c) return fail(LLM_ERR_INVALID, "nil context");
+  if (!c->weights_loaded) return fail(LLM_ERR_STATE, "weights not loaded");
+  if (!c->kv_ready) return fail(LLM_ERR_STATE, "KV cache not allocated");
+  return LLM_OK;
+}
+
+int validate_row(llm_ctx* c, int seq, int tok, int pos) {
+  if (seq < 0 || seq >= c->max_seqs) return fail(LLM_ERR_INVALID, "sequence %d out of range", seq);
+  if (tok < 0 || tok >= c->cfg.vocab) return fail(LLM_ERR_TOKEN_RANGE, "token out of range: %d", tok);
+  if (pos < 0 || pos >= c->max_pos) return fail(LLM_ERR_POS_RANGE, "position out of range: %d", pos);
+  return LLM_OK;
+}
+
+int attn_splits_for(const llm_ctx* c, int n_blocks, int max_ctx) {
+  const int ctas = n_blocks * c->cfg.n_kv_heads;
+  const int target = 2 * c->n_sm;
+  if (ctas >= target) return 1;
+  const int pages = (max_ctx + 15) / 16;
+  int s = (target + ctas - 1) / ctas;
+  s = std::min(s, std::max(1, pages / 4));
+  s = std::min(s, 64);
+  const size_t need = static_cast<size_t>(n_blocks) * c->cfg.n_kv_heads * s * 8 * (c->cfg.head_dim + 2);
+  while (s > 1 && need > c->ws_floats) --s;
+  return std::max(1, s);
+}
+
+// ---------------------------------------------------------------------------- forward
+struct RowsSpec {
+  int R = 0;
+  const int *d_blk_row0 = nullptr, *d_blk_nq = nullptr;
+  int n_blocks = 0;
+  int attn_splits = 1;
+  const int* d_final = nullptr;  // nullptr: all rows
+  int n_final = 0;
+  float* d_logits = nullptr;
+  int* tok_io = nullptr;
+  int* pos_io = nullptr;
+  const int* gen_start = nullptr;
+  int* gen_out = nullptr;
+  int gen_cap = 0;
+};
+
+int gemm(llm_ctx* c, bool in8, int epi, GemmParams p) {
+  const int esz = in8 ? 1 : 2;
+  GemmPlan pl = plan_gemm(p.M, p.N, p.K, esz, c->n_sm, 0, c->ws_floats);
+  p.k_splits = pl.splits;
+  p.k_tiles_per_split = pl.kts;
+  p.ws = c->ws;
+  p.counters = c->counters;
+  p.err = c->d_err;
+  CU(gemm_any(c->act, in8, p, epi, pl.bm, pl.grid, c->stream, false));
+  return LLM_OK;
+}
+
+int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
+  const llm_model_config& k = c->cfg;
+  const int R = rs.R, D = k.dim, F = k.hidden, Q = c->q_dim, KV = c->kv_dim;
+  const bool i8 = c->in8;
+  cudaStream_t s = c->stream;
+
+  auto norm = [&](const float* x, const float* w, bool embed, int rows, const int* row_index, void* out_act, int8_t* q,
+                  float* sc) -> int {
+    NormParams np{};
+    np.x = x;
+    np.row_index = row_index;
+    np.embed = embed ? c->embed : nullptr;
+    np.tokens = c->d_tok;
+    np.x_out = c->x;
+    np.w = w;
+    np.D = D;
+    np.rows = rows;
+    np.eps = k.norm_eps;
+    np.out = out_act;
+    np.q = q;
+    np.scale = sc;
+    CU(norm_any(c->act, q != nullptr, np, s));
+    return LLM_OK;
+  };
+  auto quant_rows = [&](const float* x, int cols, int8_t* q, float* sc) -> int {
+    NormParams np{};
+    np.x = x;
+    np.w = nullptr;
+    np.D = cols;
+    np.rows = R;
+    np.q = q;
+    np.scale = sc;
+    CU(norm_any(c->act, true, np, s));
+    return LLM_OK;
+  };
+
+  // layer 0 attention norm fused with the embedding gather
+  RC(norm(nullptr, c->layers[0].rms_att, true, R, nullptr, i8 ? nullptr : c->xn, i8 ? c->xq : nullptr, c->xs));
+  for (int l = 0; l < k.n_layers; ++l) {
+    const LayerW& L = c->layers[l];
+    {  // QKV + QK-norm + RoPE + paged KV write
+      GemmParams p{};
+      p.A = i8 ? static_cast<const void*>(c->xq) : c->xn;
+      p.B = L.wqkv;
+      p.M = R;
+      p.N = Q + 2 * KV;
+      p.K = D;
+      p.a_scale = c->xs;
+      p.b_scale = L.sqkv;
+      p.q_out = c->qbuf;
+      p.kv_pool = c->kv_pool;
+      p.block_table = c->d_block_table;
+      p.seq_ids = c->d_seq;
+      p.positions = c->d_pos;
+      p.q_norm = L.q_norm;
+      p.k_norm = L.k_norm;
+      p.rope_cos = c->rope_cos;
+      p.rope_sin = c->rope_sin;
+      p.layer = l;
+      p.n_pages = c->n_pages;
+      p.max_pages_per_seq = c->max_pages_per_seq;
+      p.n_heads = k.n_heads;
+      p.n_kv_heads = k.n_kv_heads;
+      p.head_dim = k.head_dim;
+      p.qk_norm = k.qk_norm;
+      p.eps = k.norm_eps;
+      RC(gemm(c, i8, EPI_QKV, p));
+    }
+    {  // attention over the paged cache
+      AttnParams ap{};
+      ap.q = c->qbuf;
+      ap.kv_pool = c->kv_pool;
+      ap.block_table = c->d_block_table;
+      ap.max_pages_per_seq = c->max_pages_per_seq;
+      ap.seq_ids = c->d_seq;
+      ap.positions = c->d_pos;
+      ap.blk_row0 = rs.d_blk_row0;
+      ap.blk_nq = rs.d_blk_nq;
+      ap.n_blocks = rs.n_blocks;
+      ap.n_heads = k.n_heads;
+      ap.n_kv_heads = k.n_kv_heads;
+      ap.layer = l;
+      ap.n_pages = c->n_pages;
+      ap.splits = rs.attn_splits;
+      ap.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(k.head_dim)));
+      ap.out = c->attn;
+      ap.out_f32 = i8 ? 1 : 0;
+      ap.ws = c->ws;
+      ap.counters = c->counters;
+      ap.err = c->d_err;
+      CU(attn_any(c->act, k.head_dim, ap, s, false));
+    }
+    if (i8) RC(quant_rows(static_cast<const float*>(c->attn), Q, c->aq, c->as));
+    {  // Wo + residual
+      GemmParams p{};
+      p.A = i8 ? static_cast<const void*>(c->aq) : c->attn;
+      p.B = L.wo;
+      p.M = R;
+      p.N = D;
+      p.K = Q;
+      p.a_scale = c->as;
+      p.b_scale = L.so;
+      p.out = c->x;
+      p.resid = c->x;
+      p.ldo = D;
+      RC(gemm(c, i8, EPI_RESID, p));
+    }
+    RC(norm(c->x, L.rms_ffn, false, R, nullptr, i8 ? nullptr : c->xn, i8 ? c->xq : nullptr, c->xs));
+    {  // W1/W3 + SiLU gate
+      GemmParams p{};
+      p.A = i8 ? static_cast<const void*>(c->xq) : c->xn;
+      p.B = L.w13;
+      p.M = R;
+      p.N = 2 * F;
+      p.K = D;
+      p.a_scale = c->xs;
+      p.b_scale = L.s13;
+      p.out = c->gbuf;
+      p.swiglu_f32 = i8 ? 1 : 0;
+      RC(gemm(c, i8, EPI_SWIGLU, p));
+    }
+    if (i8) RC(quant_rows(static_cast<const float*>(c->gbuf), F, c->gq, c->gs));
+    {  // W2 + residual
+      GemmParams p{};
+      p.A = i8 ? static_cast<const void*>(c->gq) : c->gbuf;
+      p.B = L.w2;
+      p.M = R;
+      p.N = D;
+      p.K = F;
+      p.a_scale = c->gs;
+      p.b_scale = L.s2;
+      p.out = c->x;
+      p.resid = c->x;
+      p.ldo = D;
+      RC(gemm(c, i8, EPI_RESID, p));
+    }
+    if (l + 1 < k.n_layers)
+      RC(norm(c->x, c->layers[l + 1].rms_att, false, R, nullptr, i8 ? nullptr : c->xn, i8 ? c->xq : nullptr, c->xs));
+  }
+  // final norm on the rows whose next token is wanted, tied/untied lm_head + argmax
+  const int NF = rs.d_final ? rs.n_final : R;
+  RC(norm(c->x, c->rms_final, false, NF, rs.d_final, c->xf, nullptr, nullptr));
+  {
+    GemmParams p{};
+    p.A = c->xf;
+    p.B = c->lm_head;
+    p.M = NF;
+    p.N = k.vocab;
+    p.K = D;
+    p.argmax_part = c->argmax_part;
+    p.logits = rs.d_logits;
+    p.ld_logits = k.vocab;
+    RC(gemm(c, false, EPI_ARGMAX, p));
+  }
+  {
+    FinishParams f{};
+    f.part = c->argmax_part;
+    f.M = NF;
+    f.n_tiles = (k.vocab + 127) / 128;
+    f.next = c->d_next;
+    f.tok_io = rs.tok_io;
+    f.pos_io = rs.pos_io;
+    f.gen_start = rs.gen_start;
+    f.gen_out = rs.gen_out;
+    f.gen_cap = rs.gen_cap;
+    finish_kernel<<<(NF + 7) / 8, 256, 0, s>>>(f);
+    CU(cudaGetLastError());
+  }
+  return LLM_OK;
+}
+
+int ensure_logits(llm_ctx* c, int rows) {
+  if (c->logits && c->logits_rows >= static_cast<size_t>(rows)) return LLM_OK;
+  if (c->logits) {
+    CU(cudaStreamSynchronize(c->stream));
+    cudaFree(c->logits);
+    c->allocs.erase(std::find(c->allocs.begin(), c->allocs.end(), static_cast<void*>(c->logits)));
+    c->logits = nullptr;
+  }
+  RC(dalloc_t(c, &c->logits, static_cast<size_t>(rows) * c->cfg.vocab * 4, &c->bytes_other));
+  c->logits_rows = rows;
+  return LLM_OK;
+}
+
+// Decode step over rows 0..n-1 of d_seq/d_tok/d_pos, via a cached CUDA graph.
+int run_step(llm_ctx* c, int n, int splits, int mode) {
+  RowsSpec rs;
+  rs.R = n;
+  rs.n_blocks = n;
+  rs.attn_splits = splits;
+  if (mode == 1) rs.d_logits = c->logits;
+  if (mode == 2) {
+    rs.tok_io = c->d_tok;
+    rs.pos_io = c->d_pos;
+    rs.gen_start = c->d_gen_start;
+    rs.gen_out = c->d_gen_out;
+    rs.gen_cap = c->gen_max_steps;
+  }
+  if (!c->use_graphs) return enqueue_forward(c, rs);
+  GraphKey key{n, splits, mode};
+  auto it = c->graphs.find(key);
+  if (it == c->graphs.end()) {
+    cudaGraph_t g = nullptr;
+    CU(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_forward(c, rs);
+    cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+    if (rc) {
+      if (g) cudaGraphDestroy(g);
+      return rc;
+    }
+    if (e != cudaSuccess) return fail(LLM_ERR_CUDA, "graph capture failed: %s", cudaGetErrorString(e));
+    cudaGraphExec_t ge = nullptr;
+    e = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return fail(LLM_ERR_CUDA, "graph instantiate failed: %s", cudaGetErrorString(e));
+    it = c->graphs.emplace(key, ge).first;
+  }
+  CU(cudaGraphLaunch(it->second, c->stream));
+  return LLM_OK;
+}
+
+}  // namespace
+
+// ============================================================================ token loop API
+extern "C" int llm_decode_step(llm_ctx* c, const int32_t* seq_ids, const int32_t* tokens, const int32_t* positions,
+                               int n, int32_t* next_tokens, float* logits) {
+  RC(check_ready(c));
+  if (!seq_ids || !tokens || !positions || !next_tokens) return fail(LLM_ERR_INVALID, "nil buffer");
+  if (n <= 0 || n > c->max_seqs) return fail(LLM_ERR_INVALID, "batch %d out of range (1..%d)", n, c->max_seqs);
+  RC(set_device(c));
+  std::vector<int> dirty;
+  int max_ctx = 0;
+  for (int i = 0; i < n; ++i) {
+    RC(validate_row(c, seq_ids[i], tokens[i], positions[i]));
+    for (int j = 0; j < i; ++j)
+      if (seq_ids[j] == seq_ids[i]) return fail(LLM_ERR_INVALID, "sequence %d appears twice in one step", seq_ids[i]);
+    RC(ensure_pages(c, seq_ids[i], positions[i], &dirty));
+    max_ctx = std::max(max_ctx, positions[i] + 1);
+  }
+  RC(upload_dirty(c, dirty));
+  int32_t* h = c->h_pin;
+  memcpy(h, seq_ids, n * 4);
+  memcpy(h + n, tokens, n * 4);
+  memcpy(h + 2 * n, positions, n * 4);
+  CU(cudaMemcpyAsync(c->d_seq, h, n * 4, cudaMemcpyHostToDevice, c->stream));
+  CU(cudaMemcpyAsync(c->d_tok, h + n, n * 4, cudaMemcpyHostToDevice, c->stream));
+  CU(cudaMemcpyAsync(c->d_pos, h + 2 * n, n * 4, cudaMemcpyHostToDevice, c->stream));
+  if (logits) RC(ensure_logits(c, n));
+  // splits sized for the largest context this graph shape is likely to see: round up to a
+  // power-of-two page count so graphs are reused across steps
+  int pages = (max_ctx + 15) / 16, p2 = 1;
+  while (p2 < pages) p2 <<= 1;
+  const int splits = attn_splits_for(c, n, p2 * 16);
+  RC(run_step(c, n, splits, logits ? 1 : 0));
+  CU(cudaMemcpyAsync(h + 3 * n, c->d_next, n * 4, cudaMemcpyDeviceToHost, c->stream));
+  if (logits)
+    CU(cudaMemcpyAsync(logits, c->logits, static_cast<size_t>(n) * c->cfg.vocab * 4, cudaMemcpyDeviceToHost, c->stream));
+  CU(cudaStreamSynchronize(c->stream));
+  memcpy(next_tokens, h + 3 * n, n * 4);
+  return check_device_error(c);
+}
+
+extern "C" int llm_prefill(llm_ctx* c, const int32_t* seq_ids, const int32_t* tokens, const int32_t* lens,
+                           const int32_t* start_pos, int nseq, int32_t* next_tokens, float* logits) {
+  RC(check_ready(c));
+  if (!seq_ids || !tokens || !lens || !next_tokens) return fail(LLM_ERR_INVALID, "nil buffer");
+  if (nseq <= 0 || nseq > c->max_seqs) return fail(LLM_ERR_INVALID, "nseq %d out of range", nseq);
+  RC(set_device(c));
+  const int qpos = std::max(1, 8 / c->group);
+  // rows (seq, tok, pos, owner)
+  struct Row { int seq, tok, pos, owner; };
+  std::vector<Row> rows;
+  std::vector<int> dirty;
+  size_t off = 0;
+  for (int i = 0; i < nseq; ++i) {
+    if (lens[i] <= 0) return fail(LLM_ERR_INVALID, "prompt %d is empty", i);
+    const int p0 = start_pos ? start_pos[i] : 0;
+    for (int j = 0; j < i; ++j)
+      if (seq_ids[j] == seq_ids[i]) return fail(LLM_ERR_INVALID, "sequence %d appears twice", seq_ids[i]);
+    for (int j = 0; j < lens[i]; ++j) {
+      RC(validate_row(c, seq_ids[i], tokens[off + j], p0 + j));
+      rows.push_back({seq_ids[i], tokens[off + j], p0 + j, i});
+    }
+    RC(ensure_pages(c, seq_ids[i], p0 + lens[i] - 1, &dirty));
+    off += lens[i];
+  }
+  RC(upload_dirty(c, dirty));
+  if (logits) RC(ensure_logits(c, nseq));
+  const int Rmax = c->max_rows;
+  size_t r = 0;
+  while (r < rows.size()) {
+    const size_t r1 = std::min(rows.size(), r + Rmax);
+    const int R = static_cast<int>(r1 - r);
+    int32_t* h = c->h_pin;  // [seq R][tok R][pos R][row0 R][nq R][final R] and owners on host
+    std::vector<int> final_owner;
+    int nb = 0, nf = 0;
+    for (int i = 0; i < R; ++i) {
+      const Row& w = rows[r + i];
+      h[i] = w.seq;
+      h[R + i] = w.tok;
+      h[2 * R + i] = w.pos;
+    }
+    // query blocks: runs of consecutive rows of one sequence, up to qpos rows each
+    for (int i = 0; i < R;) {
+      int j = i + 1;
+      while (j < R && j - i < qpos && rows[r + j].owner == rows[r + i].owner) ++j;
+      h[3 * R + nb] = i;
+      h[4 * R + nb] = j - i;
+      ++nb;
+      i = j;
+    }
+    for (int i = 0; i < R; ++i) {
+      const Row& w = rows[r + i];
+      const bool last = (r + i + 1 == rows.size()) || rows[r + i + 1].owner != w.owner;
+      if (last) {
+        h[5 * R + nf++] = i;
+        final_owner.push_back(w.owner);
+      }
+    }
+    CU(cudaMemcpyAsync(c->d_seq, h, R * 4, cudaMemcpyHostToDevice, c->stream));
+    CU(cudaMemcpyAsync(c->d_tok, h + R, R * 4, cudaMemcpyHostToDevice, c->stream));
+    CU(cudaMemcpyAsync(c->d_pos, h + 2 * R, R * 4, cudaMemcpyHostToDevice, c->stream));
+    CU(cudaMemcpyAsync(c->d_blk_row0, h + 3 * R, nb * 4, cudaMemcpyHostToDevice, c->stream));
+    CU(cudaMemcpyAsync(c->d_blk_nq, h + 4 * R, nb * 4, cudaMemcpyHostToDevice, c->stream));
+    if (nf) CU(cudaMemcpyAsync(c->d_final, h + 5 * R, nf * 4, cudaMemcpyHostToDevice, c->stream));
+    int max_ctx = 0;
+    for (int i = 0; i < R; ++i) max_ctx = std::max(max_ctx, rows[r + i].pos + 1);
+    RowsSpec rs;
+    rs.R = R;
+    rs.d_blk_row0 = c->d_blk_row0;
+    rs.d_blk_nq = c->d_blk_nq;
+    rs.n_blocks = nb;
+    rs.attn_splits = attn_splits_for(c, nb, max_ctx);
+    rs.d_final = c->d_final;
+    rs.n_final = nf;
+    rs.d_logits = logits ? c->logits : nullptr;
+    if (nf > 0) {
+      RC(enqueue_forward(c, rs));
+      std::vector<int> nxt(nf);
+      CU(cudaMemcpyAsync(nxt.data(), c->d_next, nf * 4, cudaMemcpyDeviceToHost, c->stream));
+      if (logits)
+        for (int i = 0; i < nf; ++i)
+          CU(cudaMemcpyAsync(logits + static_cast<size_t>(final_owner[i]) * c->cfg.vocab,
+                             c->logits + static_cast<size_t>(i) * c->cfg.vocab, c->cfg.vocab * 4,
+                             cudaMemcpyDeviceToHost, c->stream));
+      CU(cudaStreamSynchronize(c->stream));
+      for (int i = 0; i < nf; ++i) next_tokens[final_owner[i]] = nxt[i];
+    } else {
+      // every row continues in the next chunk; the lm_head is still run on one row so the
+      // launch sequence stays uniform (its result is discarded)
+      h[5 * R] = R - 1;
+      CU(cudaMemcpyAsync(c->d_final, h + 5 * R, 4, cudaMemcpyHostToDevice, c->stream));
+      rs.n_final = 1;
+      rs.d_logits = nullptr;
+      RC(enqueue_forward(c, rs));
+      CU(cudaStreamSynchronize(c->stream));
+    }
+    r = r1;
+  }
+  return check_device_error(c);
+}
+
+extern "C" int llm_generate_begin(llm_ctx* c, const int32_t* seq_ids, const int32_t* tokens, const int32_t* positions,
+                                  int n, int max_steps) {
+  RC(check_ready(c));
+  if (!seq_ids || !tokens || !positions) return fail(LLM_ERR_INVALID, "nil buffer");
+  if (n <= 0 || n > c->max_seqs) return fail(LLM_ERR_INVALID, "batch %d out of range", n);
+  if (max_steps <= 0) return fail(LLM_ERR_INVALID, "max_steps must be positive");
+  RC(set_device(c));
+  std::vector<int> dirty;
+  int max_ctx = 0;
+  for (int i = 0; i < n; ++i) {
+    RC(validate_row(c, seq_ids[i], tokens[i], positions[i]));
+    if (positions[i] + max_steps - 1 >= c->max_pos)
+      return fail(LLM_ERR_POS_RANGE, "position out of range: %d", positions[i] + max_steps - 1);
+    for (int j = 0; j < i; ++j)
+      if (seq_ids[j] == seq_ids[i]) return fail(LLM_ERR_INVALID, "sequence %d appears twice", seq_ids[i]);
+    RC(ensure_pages(c, seq_ids[i], positions[i] + max_steps - 1, &dirty));
+    max_ctx = std::max(max_ctx, positions[i] + max_steps);
+  }
+  RC(upload_dirty(c, dirty));
+  const size_t need = static_cast<size_t>(max_steps) * n;
+  if (need > c->gen_out_cap) {
+    if (c->d_gen_out) {
+      CU(cudaStreamSynchronize(c->stream));
+      cudaFree(c->d_gen_out);
+      c->allocs.erase(std::find(c->allocs.begin(), c->allocs.end(), static_cast<void*>(c->d_gen_out)));
+      c->d_gen_out = nullptr;
+      // graphs captured with the old buffer are stale
+      for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
+      c->graphs.clear();
+    }
+    RC(dalloc_t(c, &c->d_gen_out, need * 4, &c->bytes_other));
+    c->gen_out_cap = need;
+  }
+  if (c->gen_max_steps != max_steps) {
+    // the step capacity is baked into captured generate graphs
+    for (auto it = c->graphs.begin(); it != c->graphs.end();) {
+      if (it->first.mode == 2) {
+        cudaGraphExecDestroy(it->second);
+        it = c->graphs.erase(it);
+      } else {
+        ++it;
+      }
+    }
+  }
+  int32_t* h = c->h_pin;
+  memcpy(h, seq_ids, n * 4);
+  memcpy(h + n, tokens, n * 4);
+  memcpy(h + 2 * n, positions, n * 4);
+  CU(cudaMemcpyAsync(c->d_seq, h, n * 4, cudaMemcpyHostToDevice, c->stream));
+  CU(cudaMemcpyAsync(c->d_tok, h + n, n * 4, cudaMemcpyHostToDevice, c->stream));
+  CU(cudaMemcpyAsync(c->d_pos, h + 2 * n, n * 4, cudaMemcpyHostToDevice, c->stream));
+  CU(cudaMemcpyAsync(c->d_gen_start, h + 2 * n, n * 4, cudaMemcpyHostToDevice, c->stream));
+  CU(cudaStreamSynchronize(c->stream));
+  c->gen_n = n;
+  c->gen_steps_done = 0;
+  c->gen_max_steps = max_steps;
+  c->gen_splits = attn_splits_for(c, n, max_ctx);
+  c->gen_seq.assign(seq_ids, seq_ids + n);
+  c->gen_pos0.assign(positions, positions + n);
+  return LLM_OK;
+}
+
+extern "C" int llm_generate_steps(llm_ctx* c, int steps) {
+  RC(check_ready(c));
+  if (c->gen_n <= 0) return fail(LLM_ERR_STATE, "llm_generate_begin not called");
+  if (steps < 0 || c->gen_steps_done + steps > c->gen_max_steps)
+    return fail(LLM_ERR_INVALID, "steps %d exceed the reserved %d", c->gen_steps_done + steps, c->gen_max_steps);
+  RC(set_device(c));
+  for (int i = 0; i < steps; ++i) RC(run_step(c, c->gen_n, c->gen_splits, 2));
+  c->gen_steps_done += steps;
+  return LLM_OK;
+}
+
+extern "C" int llm_generate_end(llm_ctx* c, int32_t* out_tokens, int32_t* steps_done) {
+  RC(check_ready(c));
+  RC(set_device(c));
+  CU(cudaStreamSynchronize(c->stream));
+  if (out_tokens && c->gen_steps_done > 0)
+    CU(cudaMemcpy(out_tokens, c->d_gen_out, static_cast<size_t>(c->gen_steps_done) * c->gen_n * 4, cudaMemcpyDeviceToHost));
+  if (steps_done) *steps_done = c->gen_steps_done;
+  return check_device_error(c);
+}
+
+extern "C" int llm_generate(llm_ctx* c, const int32_t* seq_ids, const int32_t* tokens, const int32_t* positions, int n,
+                            int steps, int32_t* out_tokens) {
+  RC(llm_generate_begin(c, seq_ids, tokens, positions, n, steps));
+  RC(llm_generate_steps(c, steps));
+  int32_t done = 0;
+  return llm_generate_end(c, out_tokens, &done);
+}
+
+// ============================================================================ stories.Decoder mirror
+extern "C" int llm_stories_decode_batch(llm_ctx* c, const int32_t* prompts, const int32_t* prompt_lens, int nseq,
+                                        int max_new, float temperature, int32_t* out_tokens, int32_t* n_tokens,
+                                        int32_t* prompt_len, int32_t* stopped_on_eos) {
+  RC(check_ready(c));
+  if (!out_tokens || !n_tokens || !prompt_len || !stopped_on_eos || (!prompts && nseq > 0) || !prompt_lens)
+    return fail(LLM_ERR_INVALID, "nil buffer");
+  if (nseq <= 0 || nseq > c->max_seqs) return fail(LLM_ERR_INVALID, "nseq %d out of range", nseq);
+  if (temperature > 1e-6f)
+    return fail(LLM_ERR_UNSUPPORTED, "temperature %g: sampling is not implemented on the CUDA path (greedy only)",
+                static_cast<double>(temperature));
+  const int max_seq = c->max_pos;  // Decoder.maxSeq
+  if (max_new <= 0) max_new = 64;  // infer.go:147-149
+  std::vector<std::vector<int>> toks(nseq);
+  size_t off = 0;
+  for (int i = 0; i < nseq; ++i) {
+    const int L = prompt_lens[i];
+    std::vector<int> p(prompts + off, prompts + off + std::max(0, L));
+    off += std::max(0, L);
+    if (p.empty()) p.push_back(1);                                                     // :153-155
+    if (static_cast<int>(p.size()) > max_seq) p.erase(p.begin(), p.end() - max_seq);  // :156-158
+    for (size_t j = 0; j < p.size(); ++j)
+      if (p[j] < 0 || p[j] >= c->cfg.vocab)
+        return fail(LLM_ERR_TOKEN_RANGE, "prompt token[%zu]=%d out of range", j, p[j]);
+    toks[i] = std::move(p);
+    prompt_len[i] = static_cast<int32_t>(toks[i].size());
+    stopped_on_eos[i] = 0;
+  }
+  for (int i = 0; i < nseq; ++i) RC(llm_seq_release(c, i));
+  // prefill every prompt; the next token of a prompt that already fills max_seq is unused
+  std::vector<int> seq(nseq), lens(nseq), flat;
+  for (int i = 0; i < nseq; ++i) {
+    seq[i] = i;
+    lens[i] = static_cast<int>(toks[i].size());
+    flat.insert(flat.end(), toks[i].begin(), toks[i].end());
+  }
+  std::vector<int> next(nseq);
+  RC(llm_prefill(c, seq.data(), flat.data(), lens.data(), nullptr, nseq, next.data(), nullptr));
+  std::vector<int> active(nseq, 1), steps(nseq, 0);
+  auto accept = [&](int i, int tok) {
+    toks[i].push_back(tok);
+    ++steps[i];
+    if (tok == 2) {  // EOS, infer.go:190-193
+      stopped_on_eos[i] = 1;
+      active[i] = 0;
+    }
+    if (steps[i] >= max_new || static_cast<int>(toks[i].size()) >= max_seq) active[i] = 0;
+  };
+  for (int i = 0; i < nseq; ++i) {
+    if (max_new > 0 && static_cast<int>(toks[i].size()) < max_seq) accept(i, next[i]);
+    else active[i] = 0;
+  }
+  // constant batch: finished rows re-run their last position and their outputs are ignored
+  std::vector<int> tk(nseq), ps(nseq), nx(nseq);
+  for (;;) {
+    bool any = false;
+    for (int i = 0; i < nseq; ++i) any |= active[i] != 0;
+    if (!any) break;
+    for (int i = 0; i < nseq; ++i) {
+      tk[i] = toks[i].back();
+      ps[i] = static_cast<int>(toks[i].size()) - 1;
+    }
+    RC(llm_decode_step(c, seq.data(), tk.data(), ps.data(), nseq, nx.data(), nullptr));
+    for (int i = 0; i < nseq; ++i)
+      if (active[i]) accept(i, nx[i]);
+  }
+  for (int i = 0; i < nseq; ++i) {
+    n_tokens[i] = static_cast<int32_t>(toks[i].size());
+    std::copy(toks[i].begin(), toks[i].end(), out_tokens + static_cast<size_t>(i) * max_seq);
+  }
+  return LLM_OK;
+}
+
+extern "C" int llm_stories_decode(llm_ctx* c, int seq, const int32_t* prompt, int n_prompt, int max_new,
+                                  float temperature, int32_t* out_tokens, int32_t* n_tokens, int32_t* prompt_len,
+                                  int32_t* stopped_on_eos) {
+  if (seq != 0) return fail(LLM_ERR_INVALID, "llm_stories_decode uses sequence slot 0");
+  int32_t lens = n_prompt;
+  static const int32_t empty = 0;
+  return llm_stories_decode_batch(c, prompt ? prompt : &empty, &lens, 1, max_new, temperature, out_tokens, n_tokens,
+                                  prompt_len, stopped_on_eos);
+}
+
+// ============================================================================ introspection
+extern "C" int llm_ctx_stream(llm_ctx* c, void** stream) {
+  if (!c || !stream) return fail(LLM_ERR_INVALID, "nil argument");
+  *stream = c->stream;
+  return LLM_OK;
+}
+
+extern "C" int llm_synchronize(llm_ctx* c) {
+  if (!c) return fail(LLM_ERR_INVALID, "nil context");
+  RC(set_device(c));
+  CU(cudaStreamSynchronize(c->stream));
+  return check_device_error(c);
+}
+
+extern "C" int llm_step_kernel_count(llm_ctx* c, int n, int* count) {
+  if (!c || !count) return fail(LLM_ERR_INVALID, "nil argument");
+  // embed+norm, per layer: qkv, attention, wo, norm, w13, w2 (+ 2 quant kernels for int8)
+  // + the next layer's norm, then final norm, lm_head, finish
+  const int per_layer = 6 + (c->in8 ? 2 : 0);
+  *count = 1 + c->cfg.n_layers * per_layer + (c->cfg.n_layers - 1) + 3;
+  (void)n;
+  return LLM_OK;
+}
+
+extern "C" int llm_memory_bytes(llm_ctx* c, uint64_t* weights, uint64_t* kv_pool, uint64_t* other) {
+  if (!c) return fail(LLM_ERR_INVALID, "nil context");
+  if (weights) *weights = c->bytes_weights;
+  if (kv_pool) *kv_pool = c->bytes_kv;
+  if (other) *other = c->bytes_other;
+  return LLM_OK;
+}
+
+extern "C" int llm_time_attention(llm_ctx* c, int iters, double* us_per_launch, double* bytes_per_launch) {
+  RC(check_ready(c));
+  if (c->gen_n <= 0) return fail(LLM_ERR_STATE, "llm_generate_begin not called");
+  if (iters <= 0) return fail(LLM_ERR_INVALID, "iters must be positive");
+  RC(set_device(c));
+  const llm_model_config& k = c->cfg;
+  AttnParams ap{};
+  ap.q = c->qbuf;
+  ap.kv_pool = c->kv_pool;
+  ap.block_table = c->d_block_table;
+  ap.max_pages_per_seq = c->max_pages_per_seq;
+  ap.seq_ids = c->d_seq;
+  ap.positions = c->d_pos;
+  ap.n_blocks = c->gen_n;
+  ap.n_heads = k.n_heads;
+  ap.n_kv_heads = k.n_kv_heads;
+  ap.n_pages = c->n_pages;
+  ap.splits = c->gen_splits;
+  ap.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(k.head_dim)));
+  ap.out = c->attn;
+  ap.out_f32 = c->in8 ? 1 : 0;
+  ap.ws = c->ws;
+  ap.counters = c->counters;
+  ap.err = c->d_err;
+  cudaEvent_t e0, e1;
+  CU(cudaEventCreate(&e0));
+  CU(cudaEventCreate(&e1));
+  // warm-up pass over every layer
+  for (int l = 0; l < k.n_layers; ++l) {
+    ap.layer = l;
+    CU(attn_any(c->act, k.head_dim, ap, c->stream, false));
+  }
+  CU(cudaEventRecord(e0, c->stream));
+  for (int i = 0; i < iters; ++i)
+    for (int l = 0; l < k.n_layers; ++l) {
+      ap.layer = l;
+      CU(attn_any(c->act, k.head_dim, ap, c->stream, false));
+    }
+  CU(cudaEventRecord(e1, c->stream));
+  CU(cudaEventSynchronize(e1));
+  float ms = 0.f;
+  CU(cudaEventElapsedTime(&ms, e0, e1));
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  const double launches = static_cast<double>(iters) * k.n_layers;
+  if (us_per_launch) *us_per_launch = ms * 1e3 / launches;
+  if (bytes_per_launch) {
+    // K and V of every cached position of the context (positions pos0 + steps_done,
+    // inclusive), the q rows read and the attention rows written
+    double b = 0;
+    const double per_tok = 2.0 * c->kv_dim * act_bytes(c);
+    for (int i = 0; i < c->gen_n; ++i) b += per_tok * (c->gen_pos0[i] + c->gen_steps_done + 1);
+    b += static_cast<double>(c->gen_n) * c->q_dim * act_bytes(c);
+    b += static_cast<double>(c->gen_n) * c->q_dim * (c->in8 ? 4.0 : static_cast<double>(act_bytes(c)));
+    *bytes_per_launch = b;
+  }
+  return check_device_error(c);
+}
+
+extern "C" int llm_debug_read_kv(llm_ctx* c, int layer, int seq, int pos, float* kout, float* vout) {
+  RC(check_ready(c));
+  if (layer < 0 || layer >= c->cfg.n_layers) return fail(LLM_ERR_INVALID, "layer %d out of range", layer);
+  if (seq < 0 || seq >= c->max_seqs) return fail(LLM_ERR_INVALID, "sequence %d out of range", seq);
+  if (pos < 0 || pos / 16 >= c->seq_npages[seq]) return fail(LLM_ERR_POS_RANGE, "position out of range: %d", pos);
+  RC(set_device(c));
+  const int page = c->h_block_table[static_cast<size_t>(seq) * c->max_pages_per_seq + pos / 16];
+  float* d = nullptr;
+  CU(cudaMalloc(&d, 2 * c->kv_dim * 4));
+  const int n = 2 * c->kv_dim;
+  if (c->act == 1)
+    read_kv_kernel<__half><<<(n + 255) / 256, 256, 0, c->stream>>>(static_cast<const __half*>(c->kv_pool), layer, c->n_pages,
+                                                                  c->cfg.n_kv_heads, c->cfg.head_dim, page, pos & 15, d, d + c->kv_dim);
+  else
+    read_kv_kernel<__nv_bfloat16><<<(n + 255) / 256, 256, 0, c->stream>>>(static_cast<const __nv_bfloat16*>(c->kv_pool), layer,
+                                                                          c->n_pages, c->cfg.n_kv_heads, c->cfg.head_dim, page,
+                                                                          pos & 15, d, d + c->kv_dim);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+  if (e == cudaSuccess) e = cudaMemcpy(kout, d, c->kv_dim * 4, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) e = cudaMemcpy(vout, d + c->kv_dim, c->kv_dim * 4, cudaMemcpyDeviceToHost);
+  cudaFree(d);
+  if (e != cudaSuccess) return fail(LLM_ERR_CUDA, "read kv: %s", cudaGetErrorString(e));
+  return LLM_OK;
+}
+
+// ============================================================================ debug hooks
+namespace {
+struct DevBuf {
+  void* p = nullptr;
+  ~DevBuf() {
+    if (p) cudaFree(p);
+  }
+};
+}  // namespace
+
+extern "C" int llm_debug_norm_quant(int device, const float* x, const float* w, int rows, int cols, double eps, int8_t* q,
+                                    float* scales) {
+  if (!x || !q || !scales || rows <= 0 || cols <= 0 || cols % 4) return fail(LLM_ERR_INVALID, "bad arguments");
+  CU(cudaSetDevice(device));
+  DevBuf dx, dw, dq, ds;
+  CU(cudaMalloc(&dx.p, static_cast<size_t>(rows) * cols * 4));
+  CU(cudaMalloc(&dq.p, static_cast<size_t>(rows) * cols));
+  CU(cudaMalloc(&ds.p, rows * 4));
+  CU(cudaMemcpy(dx.p, x, static_cast<size_t>(rows) * cols * 4, cudaMemcpyHostToDevice));
+  if (w) {
+    CU(cudaMalloc(&dw.p, cols * 4));
+    CU(cudaMemcpy(dw.p, w, cols * 4, cudaMemcpyHostToDevice));
+  }
+  NormParams np{};
+  np.x = static_cast<const float*>(dx.p);
+  np.w = static_cast<const float*>(dw.p);
+  np.D = cols;
+  np.rows = rows;
+  np.eps = eps;
+  np.q = static_cast<int8_t*>(dq.p);
+  np.scale = static_cast<float*>(ds.p);
+  CU(norm_any(2, true, np, 0));
+  CU(cudaDeviceSynchronize());
+  CU(cudaMemcpy(q, dq.p, static_cast<size_t>(rows) * cols, cudaMemcpyDeviceToHost));
+  CU(cudaMemcpy(scales, ds.p, rows * 4, cudaMemcpyDeviceToHost));
+  return LLM_OK;
+}
+
+namespace {
+int debug_gemm(int device, bool in8, int act, const void* hA, const void* hB, size_t esz, int M, int N, int K, int splits,
+               int epi, void* hC) {
+  CU(cudaSetDevice(device));
+  cudaDeviceProp prop{};
+  CU(cudaGetDeviceProperties(&prop, device));
+  DevBuf dA, dB, dC, dws, dcnt, dsa, dsb;
+  CU(cudaMalloc(&dA.p, static_cast<size_t>(M) * K * esz));
+  CU(cudaMalloc(&dB.p, static_cast<size_t>(N) * K * esz));
+  CU(cudaMalloc(&dC.p, static_cast<size_t>(M) * N * 4));
+  CU(cudaMemcpy(dA.p, hA, static_cast<size_t>(M) * K * esz, cudaMemcpyHostToDevice));
+  CU(cudaMemcpy(dB.p, hB, static_cast<size_t>(N) * K * esz, cudaMemcpyHostToDevice));
+  const size_t ws_cap = 32u << 20;
+  CU(cudaMalloc(&dws.p, ws_cap * 4));
+  CU(cudaMalloc(&dcnt.p, 65536 * 4));
+  CU(cudaMemset(dcnt.p, 0, 65536 * 4));
+  GemmPlan pl = plan_gemm(M, N, K, in8 ? 1 : 2, prop.multiProcessorCount, splits, ws_cap);
+  GemmParams p{};
+  p.A = dA.p;
+  p.B = dB.p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.k_splits = pl.splits;
+  p.k_tiles_per_split = pl.kts;
+  p.ws = static_cast<float*>(dws.p);
+  p.counters = static_cast<int*>(dcnt.p);
+  p.out = dC.p;
+  p.ldo = N;
+  CU(gemm_any(act, in8, p, epi, pl.bm, pl.grid, 0, true));
+  CU(gemm_any(act, in8, p, epi, pl.bm, pl.grid, 0, false));
+  CU(cudaDeviceSynchronize());
+  CU(cudaMemcpy(hC, dC.p, static_cast<size_t>(M) * N * 4, cudaMemcpyDeviceToHost));
+  return LLM_OK;
+}
+}  // namespace
+
+extern "C" int llm_debug_gemm_i8(int device, const int8_t* A, const int8_t* B, int M, int N, int K, int splits, int32_t* C) {
+  if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0 || K % 128) return fail(LLM_ERR_INVALID, "bad arguments (K %% 128 == 0)");
+  return debug_gemm(device, true, 2, A, B, 1, M, N, K, splits, EPI_S32, C);
+}
+
+extern "C" int llm_debug_gemm_f16(int device, int dtype, const float* A, const float* B, int M, int N, int K, int splits,
+                                  float* C) {
+  if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0 || K % 64 || N % 2) return fail(LLM_ERR_INVALID, "bad arguments");
+  if (dtype != LLM_DTYPE_F16 && dtype != LLM_DTYPE_BF16) return fail(LLM_ERR_INVALID, "dtype must be F16 or BF16");
+  const int act = dtype == LLM_DTYPE_F16 ? 1 : 2;
+  // round on the device with the model's conversion
+  CU(cudaSetDevice(device));
+  DevBuf fA, fB, hA, hB;
+  const size_t na = static_cast<size_t>(M) * K, nb = static_cast<size_t>(N) * K;
+  CU(cudaMalloc(&fA.p, na * 4));
+  CU(cudaMalloc(&fB.p, nb * 4));
+  CU(cudaMalloc(&hA.p, na * 2));
+  CU(cudaMalloc(&hB.p, nb * 2));
+  CU(cudaMemcpy(fA.p, A, na * 4, cudaMemcpyHostToDevice));
+  CU(cudaMemcpy(fB.p, B, nb * 4, cudaMemcpyHostToDevice));
+  if (act == 1) {
+    f32_to_act_kernel<__half><<<(na + 255) / 256, 256>>>(static_cast<float*>(fA.p), static_cast<__half*>(hA.p), na);
+    f32_to_act_kernel<__half><<<(nb + 255) / 256, 256>>>(static_cast<float*>(fB.p), static_cast<__half*>(hB.p), nb);
+  } else {
+    f32_to_act_kernel<__nv_bfloat16><<<(na + 255) / 256, 256>>>(static_cast<float*>(fA.p), static_cast<__nv_bfloat16*>(hA.p), na);
+    f32_to_act_kernel<__nv_bfloat16><<<(nb + 255) / 256, 256>>>(static_cast<float*>(fB.p), static_cast<__nv_bfloat16*>(hB.p), nb);
+  }
+  CU(cudaGetLastError());
+  std::vector<uint16_t> ha(na), hb(nb);
+  CU(cudaMemcpy(ha.data(), hA.p, na * 2, cudaMemcpyDeviceToHost));
+  CU(cudaMemcpy(hb.data(), hB.p, nb * 2, cudaMemcpyDeviceToHost));
+  return debug_gemm(device, false, act, ha.data(), hb.data(), 2, M, N, K, splits, EPI_F32, C);
+}

@@ -1,0 +1,193 @@
+/*
+ * llm_cuda.h -- C ABI of the B200 token loop (prefill + greedy decode) for the Llama-style
+ * models of tmc/ane-training-experiments (Stories110M MHA, Qwen3-0.6B GQA).
+ *
+ * This is the boundary a cgo shim binds.  Plain C types only: opaque
+ * handles, int status codes, host pointers and sizes.  The context owns all device memory;
+ * the caller owns every host buffer it passes.  Status: 0 = LLM_OK, negative = error, with
+ * the message available from llm_last_error() (precedent: bridge/stories_trainer_bridge.h:32-36,
+ * bridge/ane_bridge.h:25-27).  A context is not thread-safe; serialise calls per context
+ * (precedent: the per-kernel mutex of ane/linear/executor.go:44-50).
+ *
+ * There is no CPU fallback: every compute entry point runs CUDA kernels on the context's
+ * device and fails with LLM_ERR_CUDA when that is impossible.
+ */
+#ifndef LLM_CUDA_H
+#define LLM_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status codes */
+#define LLM_OK 0
+#define LLM_ERR_INVALID -1      /* bad argument / configuration                        */
+#define LLM_ERR_TOKEN_RANGE -2  /* "token out of range: %d"    (ane/stories/infer.go:205-207) */
+#define LLM_ERR_POS_RANGE -3    /* "position out of range: %d" (ane/stories/infer.go:208-210) */
+#define LLM_ERR_CUDA -4         /* CUDA runtime failure                                */
+#define LLM_ERR_OOM -5          /* device or page-pool memory exhausted                */
+#define LLM_ERR_STATE -6        /* call order (weights / KV cache not set up)          */
+#define LLM_ERR_UNSUPPORTED -7  /* a mode this build does not implement                */
+#define LLM_ERR_DEVICE -8       /* a kernel reported an error (bounded wait expired, bad page) */
+
+/* ---------------------------------------------------------------- configuration */
+/* Arithmetic of the CUDA path. */
+#define LLM_DTYPE_F16 1       /* fp16 weights/activations/KV, fp32 accumulate          */
+#define LLM_DTYPE_BF16 2      /* bf16 weights/activations/KV, fp32 accumulate          */
+#define LLM_DTYPE_W8A8_F16 3  /* int8 layer weights (per-output-channel scales) and
+                                 per-token int8 activations, int32 accumulate; fp16
+                                 embeddings/lm_head/KV                                 */
+#define LLM_DTYPE_W8A8_BF16 4 /* as above with bf16 embeddings/lm_head/KV              */
+
+/* Runtime model description; replaces the compile-time constants of
+ * ane/stories/config.go:3-18 and training/training_dynamic/models/qwen3_06b.h:6-16. */
+typedef struct llm_model_config {
+  int32_t dim;         /* model width D                                           */
+  int32_t hidden;      /* SwiGLU width F                                          */
+  int32_t n_layers;
+  int32_t n_heads;     /* query heads                                             */
+  int32_t n_kv_heads;  /* key/value heads (GQA when < n_heads)                    */
+  int32_t head_dim;    /* 64 or 128                                               */
+  int32_t vocab;
+  int32_t max_seq;     /* RoPE table length = largest position + 1                */
+  int32_t qk_norm;     /* 1: per-head RMSNorm of q and k before RoPE (Qwen3)      */
+  int32_t tied_embed;  /* 1: lm_head = embedding (ane/stories/infer.go:243)       */
+  double norm_eps;     /* RMSNorm epsilon (Go: float64 1e-5, infer.go:307)        */
+  double rope_theta;   /* RoPE base (Go: 10000, infer.go:102)                     */
+} llm_model_config;
+
+/* fp32 host weights in the reference's row-major [out, in] layout
+ * (ane/stories/weights.go:13-23: LayerWeights / ModelWeights). */
+typedef struct llm_layer_weights_f32 {
+  const float *wq, *wk, *wv, *wo, *w1, *w2, *w3;
+  const float *rms_att, *rms_ffn;
+  const float *q_norm, *k_norm; /* [head_dim], read only when qk_norm */
+} llm_layer_weights_f32;
+
+typedef struct llm_model_weights_f32 {
+  const float *embed;     /* [vocab, dim] */
+  const float *rms_final; /* [dim] */
+  const float *lm_head;   /* [vocab, dim] or NULL when tied */
+  const llm_layer_weights_f32 *layers; /* n_layers entries */
+} llm_model_weights_f32;
+
+typedef struct llm_ctx llm_ctx;
+
+/* ---------------------------------------------------------------- errors */
+/* Copies the calling thread's last error message (NUL-terminated, truncated to n).
+ * Returns the full message length.  Replaces ane_bridge's last-error accessor. */
+int llm_last_error(char *buf, size_t n);
+
+/* ---------------------------------------------------------------- context / weights */
+/* Create a context on CUDA device `device`.  Replaces model.Compile
+ * (ane/model/model_darwin.go:138-171) and stories.NewDecoder's setup
+ * (ane/stories/infer.go:80-133: RoPE tables). */
+int llm_ctx_create(const llm_model_config *cfg, int dtype, int device, llm_ctx **out);
+/* Release every device resource.  Replaces Kernel.Close (ane/model/model_darwin.go:542-556). */
+int llm_ctx_destroy(llm_ctx *ctx);
+
+/* Upload fp32 host weights; conversion (rounding to fp16/bf16, or the int8 quantiser of
+ * bridge/ane_bridge.m:374-398 per output row) runs on the device.  Replaces the weight
+ * blob staging of model.CompileOptions.WeightBlob (ane/model/model_other.go:13-24). */
+int llm_load_weights_f32(llm_ctx *ctx, const llm_model_weights_f32 *w);
+
+/* Seeded synthetic weights, generated on the host by llm_synth_normal (streams below):
+ * matrices N(0, 0.02); Wo and W2 additionally x out_proj_scale (Stories: 1/sqrt(2*12));
+ * RMSNorm and QK-norm weights 1.  Stands in for stories.RandomInit (ane/stories/weights.go:124-153),
+ * whose Go math/rand stream cannot be reproduced here. */
+int llm_load_weights_synthetic(llm_ctx *ctx, uint64_t seed, float out_proj_scale);
+
+/* Counter-based N(0, stddev) generator: element i of stream `stream` is a function of
+ * (seed, stream, i) only (SplitMix64 -> Box-Muller in double, one rounding to f32).
+ * value = (float)(stddev * scale * z).  Multithreaded, deterministic. */
+void llm_synth_normal(float *dst, uint64_t n, uint64_t seed, uint64_t stream, double stddev, double scale);
+/* Stream id of each synthetic tensor: kind 0..6 = wq,wk,wv,wo,w1,w2,w3 of `layer`,
+ * kind 7 = embed (layer ignored), kind 8 = untied lm_head (layer ignored). */
+uint64_t llm_synth_stream(int layer, int kind);
+
+/* ---------------------------------------------------------------- paged KV cache */
+/* Allocate the page pool for `max_seqs` sequence slots of up to `max_pos` positions in
+ * pages of `page_tokens` (must be 16) positions.  Replaces the [layer][pos][dim] cache of
+ * stories.NewDecoder (ane/stories/infer.go:113-114).  Also sizes activation buffers. */
+int llm_kv_alloc(llm_ctx *ctx, int max_seqs, int max_pos, int page_tokens);
+/* Return a sequence slot's pages to the pool.  Replaces Decoder.ResetCache
+ * (ane/stories/infer.go:62-71) for one slot. */
+int llm_seq_release(llm_ctx *ctx, int seq);
+
+/* ---------------------------------------------------------------- token loop */
+/* Prefill: for each of `nseq` sequences, run its `lens[i]` prompt tokens (concatenated in
+ * `tokens`) at positions start_pos[i].. (start_pos NULL = 0) and return the greedy next
+ * token after the last one.  logits (optional) receives [nseq, vocab] for that position.
+ * Replaces the one-token-at-a-time prompt loop of Decoder.Decode (ane/stories/infer.go:171-175). */
+int llm_prefill(llm_ctx *ctx, const int32_t *seq_ids, const int32_t *tokens, const int32_t *lens,
+                const int32_t *start_pos, int nseq, int32_t *next_tokens, float *logits);
+
+/* One decode step for n sequences: token tokens[i] at position positions[i] of slot
+ * seq_ids[i]; writes the greedy next token (first maximum wins, infer.go:373-383) and,
+ * optionally, logits [n, vocab].  Host buffers; host<->device copies are inside the call.
+ * Replaces Decoder.forwardOne + sampleFromLogits at temperature 0 (infer.go:204-245,347-350)
+ * and Decoder.EvalNextLogits (infer.go:62-77). */
+int llm_decode_step(llm_ctx *ctx, const int32_t *seq_ids, const int32_t *tokens, const int32_t *positions,
+                    int n, int32_t *next_tokens, float *logits);
+
+/* Device-resident greedy loop (no per-token host synchronisation): begin copies the
+ * initial tokens/positions and reserves pages for max_steps; steps enqueues `steps`
+ * decode steps on the context stream (each feeds its tokens to the next); end waits and
+ * copies out_tokens [steps_done, n].  llm_generate = begin + steps + end. */
+int llm_generate_begin(llm_ctx *ctx, const int32_t *seq_ids, const int32_t *tokens, const int32_t *positions,
+                       int n, int max_steps);
+int llm_generate_steps(llm_ctx *ctx, int steps);
+int llm_generate_end(llm_ctx *ctx, int32_t *out_tokens, int32_t *steps_done);
+int llm_generate(llm_ctx *ctx, const int32_t *seq_ids, const int32_t *tokens, const int32_t *positions, int n,
+                 int steps, int32_t *out_tokens);
+
+/* ---------------------------------------------------------------- stories.Decoder mirror */
+/* Greedy Decode of one sequence slot with the reference's host rules (ane/stories/infer.go:136-202):
+ * empty prompt -> [BOS=1]; prompt longer than max_seq keeps its last max_seq tokens;
+ * prompt tokens range-checked ("prompt token[%d]=%d out of range"); stop at max_new
+ * (<= 0 -> 64), at max_seq, or after EOS=2.  temperature > 1e-6 returns LLM_ERR_UNSUPPORTED.
+ * out_tokens needs max_seq entries; it receives prompt + generated tokens. */
+int llm_stories_decode(llm_ctx *ctx, int seq, const int32_t *prompt, int n_prompt, int max_new,
+                       float temperature, int32_t *out_tokens, int32_t *n_tokens, int32_t *prompt_len,
+                       int32_t *stopped_on_eos);
+/* The batched form: nseq independent slots 0..nseq-1, prompts concatenated; out_tokens is
+ * [nseq, max_seq]; per-sequence n_tokens / prompt_len / stopped_on_eos. */
+int llm_stories_decode_batch(llm_ctx *ctx, const int32_t *prompts, const int32_t *prompt_lens, int nseq,
+                             int max_new, float temperature, int32_t *out_tokens, int32_t *n_tokens,
+                             int32_t *prompt_len, int32_t *stopped_on_eos);
+
+/* ---------------------------------------------------------------- introspection / timing */
+/* The context's CUDA stream (cudaStream_t) so callers can record events on it. */
+int llm_ctx_stream(llm_ctx *ctx, void **stream);
+int llm_synchronize(llm_ctx *ctx);
+/* Number of kernel launches one decode step of n sequences makes. */
+int llm_step_kernel_count(llm_ctx *ctx, int n, int *count);
+/* Device bytes held by the context (weights, KV pool, buffers, workspace). */
+int llm_memory_bytes(llm_ctx *ctx, uint64_t *weights, uint64_t *kv_pool, uint64_t *other);
+/* Time `iters` back-to-back launches of the attention kernel of every layer for the
+ * current generate batch (after llm_generate_begin) with CUDA events on the context
+ * stream; returns the mean duration of one launch in microseconds and the algorithmic
+ * bytes one launch reads and writes. */
+int llm_time_attention(llm_ctx *ctx, int iters, double *us_per_launch, double *bytes_per_launch);
+
+/* ---------------------------------------------------------------- bit-exact debug hooks */
+/* RMSNorm + per-token quantiser on host rows x [rows, cols] run on the device with the
+ * model kernel (w NULL: quantise only). */
+int llm_debug_norm_quant(int device, const float *x, const float *w, int rows, int cols, double eps,
+                         int8_t *q, float *scales);
+/* int8 GEMM C = A . B^T with the model's GEMM kernel; splits forces split-K (0 = auto). */
+int llm_debug_gemm_i8(int device, const int8_t *A, const int8_t *B, int M, int N, int K, int splits,
+                      int32_t *C);
+/* 16-bit GEMM (dtype LLM_DTYPE_F16 / BF16; inputs given as fp32 and rounded) -> fp32 C. */
+int llm_debug_gemm_f16(int device, int dtype, const float *A, const float *B, int M, int N, int K,
+                       int splits, float *C);
+/* Read back cached K and V of (layer, seq, pos) as fp32 [kv_dim] each. */
+int llm_debug_read_kv(llm_ctx *ctx, int layer, int seq, int pos, float *k, float *v);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LLM_CUDA_H */

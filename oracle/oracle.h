@@ -1,0 +1,140 @@
+/*
+ * oracle.h -- CPU restatement of the reference token loop (TEST INFRASTRUCTURE).
+ *
+ * This library is the checker for the CUDA token loop.  Only tests/,
+ * __graft_entry__.smoke() and bench.py's cpu_baseline / reference legs load
+ * it; the product library never links or calls it.
+ *
+ * What it restates (file:line in the reference project tmc/ane-training-experiments):
+ *   ane/stories/infer.go:80-133   NewDecoder: RoPE tables (float64 pow/cos/sin -> f32),
+ *                                 KV cache [layer][pos][kv_dim]
+ *   ane/stories/infer.go:136-202  Decode: prompt prefill one token at a time, greedy loop,
+ *                                 EOS (id 2) stop, maxSeq stop, BOS (id 1) default prompt
+ *   ane/stories/infer.go:204-245  forwardOne: layer order and residual form
+ *   ane/stories/infer.go:247-265  applyRoPE: interleaved (2i, 2i+1) pairs
+ *   ane/stories/infer.go:267-299  storeKV / attend (f32 dot, * 1/sqrt(hd), softmaxPrefix, PV)
+ *   ane/stories/infer.go:301-311  rmsNormVec: float64 sum of squares, f32 rrms, x*rrms*w
+ *   ane/stories/infer.go:313-322  matVec: serial f32 sum per output row
+ *   ane/stories/infer.go:324-326  silu via float64 exp
+ *   ane/stories/infer.go:328-345  softmaxPrefix: f32 max, float64 exp/sum, f32 probs
+ *   ane/stories/infer.go:373-383  argmax: strict '>' (first maximum wins)
+ *   training/training_dynamic/io.h:434-455   GQA head map kv_head = q_head / (heads/kv_heads)
+ *   bridge/ane_bridge.m:374-398   int8 quantiser: scale = maxabs/127 (0 -> 1), v = x/scale,
+ *                                 clamp [-128,127], (int8)(v + (v>=0 ? 0.5 : -0.5))
+ *
+ * Generalisations beyond the Go decoder (which hard-codes Stories110M):
+ *   kv_heads / head_dim / QK-norm (per-head RMSNorm of q and k before RoPE) / theta / eps /
+ *   max_seq without the 256 clamp, and precision-emulation modes that round at exactly the
+ *   points where the CUDA path rounds (fp16/bf16 weights, GEMM inputs, KV cache, q, the
+ *   attention output, the SwiGLU output) and that quantise like the CUDA W8A8 path
+ *   (per-output-channel weight scales, per-token activation scales, both with the bridge
+ *   rule applied row-wise).  Softmax weights are not rounded (the CUDA kernel carries them
+ *   as a two-term split with ~16 mantissa bits).
+ *
+ * PARITY UNPINNED: the reference publishes no golden tokens/logits for this path and its Go
+ * code cannot be run in this environment (no Go toolchain, and the module's tmc/apple
+ * dependency is replaced to a path that does not exist).  The building blocks are pinned
+ * by the known-answer tests under tests/ that restate the reference's own unit tests and
+ * hand-derived values; the end-to-end decoder is pinned only by self-consistency fixtures.
+ */
+#ifndef ORACLE_H
+#define ORACLE_H
+
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  ORACLE_F32 = 0,        /* the reference arithmetic, unchanged                    */
+  ORACLE_F16 = 1,        /* fp16 weights / GEMM inputs / KV, f32 accumulate         */
+  ORACLE_BF16 = 2,       /* bf16 weights / GEMM inputs / KV, f32 accumulate         */
+  ORACLE_W8A8_F16 = 3,   /* int8 layer weights + per-token int8 acts, fp16 rest     */
+  ORACLE_W8A8_BF16 = 4,  /* int8 layer weights + per-token int8 acts, bf16 rest     */
+};
+
+typedef struct oracle_config {
+  int32_t dim, hidden, n_layers, n_heads, n_kv_heads, head_dim, vocab;
+  int32_t max_seq;
+  int32_t qk_norm;     /* 1: per-head RMSNorm on q and k before RoPE (Qwen3) */
+  int32_t mode;        /* ORACLE_* */
+  double norm_eps;     /* Go uses the float64 constant 1e-5 */
+  double rope_theta;   /* Go uses 10000 */
+} oracle_config;
+
+typedef struct oracle_layer_f32 {
+  const float *wq, *wk, *wv, *wo;   /* [q_dim,dim] [kv_dim,dim] [kv_dim,dim] [dim,q_dim] */
+  const float *w1, *w2, *w3;        /* [hidden,dim] [dim,hidden] [hidden,dim]            */
+  const float *rms_att, *rms_ffn;   /* [dim]                                              */
+  const float *q_norm, *k_norm;     /* [head_dim] (only read when qk_norm)                */
+} oracle_layer_f32;
+
+typedef struct oracle_weights_f32 {
+  const float *embed;      /* [vocab, dim] */
+  const float *rms_final;  /* [dim] */
+  const float *lm_head;    /* [vocab, dim] or NULL when tied to embed */
+  const oracle_layer_f32 *layers;
+} oracle_weights_f32;
+
+typedef struct oracle_model oracle_model;
+typedef struct oracle_seq oracle_seq;
+
+/* Error codes (negative), mirroring the C-ABI's. */
+#define ORACLE_OK 0
+#define ORACLE_EINVAL -1
+#define ORACLE_ERANGE_TOKEN -2
+#define ORACLE_ERANGE_POS -3
+
+oracle_model *oracle_model_new(const oracle_config *cfg, const oracle_weights_f32 *w);
+void oracle_model_free(oracle_model *m);
+oracle_seq *oracle_seq_new(const oracle_model *m);
+void oracle_seq_free(oracle_seq *s);
+void oracle_seq_reset(oracle_seq *s);
+/* Fill the KV cache positions [0, n_pos) with seeded values (for timing samples only). */
+void oracle_seq_fill_kv_synthetic(const oracle_model *m, oracle_seq *s, int n_pos, uint64_t seed);
+/* forwardOne: returns ORACLE_OK or an error; logits_out may be NULL. */
+int oracle_forward(const oracle_model *m, oracle_seq *s, int token, int pos, float *logits_out);
+/* Decode (greedy; temperature <= 1e-6 branch of sampleFromLogits).  out_tokens receives
+ * prompt + generated tokens (capacity max_seq).  Returns ORACLE_OK or an error. */
+int oracle_decode(const oracle_model *m, oracle_seq *s, const int32_t *prompt, int n_prompt,
+                  int max_new, int32_t *out_tokens, int32_t *n_tokens, int32_t *prompt_len,
+                  int32_t *stopped_on_eos);
+/* Teacher-forced pass: feed tokens[0..n) at positions 0..n-1; argmax_out[i] = argmax after
+ * token i; logits_out (optional) gets [n, vocab]. */
+int oracle_teacher_forced(const oracle_model *m, oracle_seq *s, const int32_t *tokens, int n,
+                          int32_t *argmax_out, float *logits_out);
+
+/* ---- building blocks (known-answer and bit-exact checks) ---- */
+int oracle_argmax(const float *v, int n);
+void oracle_rmsnorm(float *out, const float *x, const float *w, int n, double eps);
+void oracle_rope_tables(int max_pos, int head_dim, double theta, float *cos_out, float *sin_out);
+void oracle_softmax_prefix(float *dst, const float *src, int n);
+float oracle_silu(float x);
+float oracle_round_f16(float x);
+float oracle_round_bf16(float x);
+/* Bridge quantiser applied per row (rows x cols); scales[rows]. */
+void oracle_quant_rows(const float *x, int rows, int cols, int8_t *q, float *scales);
+/* RMSNorm then per-row quantisation, with the float64 sum of squares taken in the order
+ * the CUDA row kernel documents (32 lane partials over float4 groups, xor butterfly). */
+void oracle_norm_quant_rows_lane_order(const float *x, const float *w, int rows, int cols,
+                                       double eps, int8_t *q, float *scales);
+/* Same lane-ordered RMSNorm without quantisation, output rounded per mode (F16/BF16/none). */
+void oracle_norm_rows_lane_order(const float *x, const float *w, int rows, int cols,
+                                 double eps, int round_mode, float *out);
+/* Exact int8 GEMM: C[m][n] = sum_k A[m][k]*B[n][k]. */
+void oracle_gemm_i8(const int8_t *A, const int8_t *B, int M, int N, int K, int32_t *C);
+/* Dequantise an int32 accumulator the way the CUDA epilogue does: (float)acc*sa*sw. */
+float oracle_dequant(int32_t acc, float sa, float sw);
+
+/* Test-only: 1 = sum the attention PV products in reverse position order (emulation modes). */
+void oracle_set_attn_reverse(int on);
+/* Thread count used by row-parallel loops (OpenMP); 0 = library default. */
+void oracle_set_threads(int n);
+int oracle_get_threads(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
