@@ -363,6 +363,13 @@ class Engine:
         _abi.check(_abi.lib().llm_time_attention(self.h, iters, C.byref(us), C.byref(by)))
         return us.value, by.value
 
+    def profile_step(self, iters: int = 3):
+        """Per-kernel table of one eager decode step of the current generate batch."""
+        buf = C.create_string_buffer(16384)
+        us = C.c_double()
+        _abi.check(_abi.lib().llm_profile_step(self.h, iters, buf, len(buf), C.byref(us)))
+        return buf.value.decode(), us.value
+
     def read_kv(self, layer: int, seq: int, pos: int):
         k = np.zeros(self.cfg.kv_dim, np.float32)
         v = np.zeros(self.cfg.kv_dim, np.float32)

@@ -209,21 +209,28 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(GemmParams p) {
     if (!s_last) return;
     __threadfence();
     (void)PER;
-    j = 0;
+    // Sum the partials split-major so every thread keeps PER independent loads in flight
+    // (a split-minor loop would serialise one L2 round trip per split and element).
 #pragma unroll
     for (int a = 0; a < MT; ++a)
 #pragma unroll
       for (int b = 0; b < NT; ++b)
 #pragma unroll
-        for (int c = 0; c < 4; ++c, ++j) {
-          Acc sum = 0;
-          for (int s = 0; s < p.k_splits; ++s) {
-            const float v = __ldcg(p.ws + (static_cast<size_t>(s) * tiles + tile) * (BM * BN) + j * kGemmThreads + tid);
-            if constexpr (ESZ == 1) sum += __float_as_int(v);
-            else sum = __fadd_rn(sum, v);
+        for (int c = 0; c < 4; ++c) acc[a][b][c] = 0;
+    for (int s = 0; s < p.k_splits; ++s) {
+      const float* src = p.ws + (static_cast<size_t>(s) * tiles + tile) * (BM * BN) + tid;
+      j = 0;
+#pragma unroll
+      for (int a = 0; a < MT; ++a)
+#pragma unroll
+        for (int b = 0; b < NT; ++b)
+#pragma unroll
+          for (int c = 0; c < 4; ++c, ++j) {
+            const float v = __ldcg(src + j * kGemmThreads);
+            if constexpr (ESZ == 1) acc[a][b][c] += __float_as_int(v);
+            else acc[a][b][c] = __fadd_rn(acc[a][b][c], v);
           }
-          acc[a][b][c] = sum;
-        }
+    }
     if (tid == 0) p.counters[tile] = 0;
   }
 
@@ -348,6 +355,19 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(GemmParams p) {
           const int cl = wn * WTN + nt * 8 + 2 * t + (c & 1);
           sC[rl * LDS + cl] = value(mt, nt, c);
         }
+    // per-row position and physical KV page, resolved once per tile (one thread per row)
+    // so the head jobs below carry no dependent global-load chains
+    __shared__ int s_pos[BM], s_page[BM];
+    for (int rl = tid; rl < BM; rl += kGemmThreads) {
+      const int r = m0 + rl;
+      int pos = 0, page = 0;
+      if (r < p.M) {
+        pos = p.positions[r];
+        page = p.block_table[static_cast<size_t>(p.seq_ids[r]) * p.max_pages_per_seq + (pos >> 4)];
+      }
+      s_pos[rl] = pos;
+      s_page[rl] = page;
+    }
     __syncthreads();
     const int hd = p.head_dim;
     const int E = hd / 32;  // values per lane (2 or 4)
@@ -367,7 +387,7 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(GemmParams p) {
 #pragma unroll
       for (int e = 0; e < 4; ++e)
         if (e < E) v[e] = sC[rl * LDS + hh * hd + d0 + e];
-      const int pos = p.positions[r];
+      const int pos = s_pos[rl];
       if (region < 2) {
         if (p.qk_norm) {
           const float* nw = region == 0 ? p.q_norm : p.k_norm;
@@ -399,8 +419,7 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(GemmParams p) {
         for (int e = 0; e < 4; ++e)
           if (e < E) qo[e] = ActTraits<OutT>::from_f(v[e]);
       } else {
-        const int seq = p.seq_ids[r];
-        int page = p.block_table[static_cast<size_t>(seq) * p.max_pages_per_seq + (pos >> 4)];
+        const int page = s_page[rl];
         if (page < 0 || page >= p.n_pages) {
           if (p.err) atomicExch(p.err, kDevBadPage);
           continue;

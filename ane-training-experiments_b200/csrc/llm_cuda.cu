@@ -1,6 +1,7 @@
 // llm_cuda.cu -- the C ABI of include/llm_cuda.h: context, weights, paged KV cache,
 // the token-loop orchestration (prefill / decode step / device-resident generate with CUDA
 // graphs), the stories.Decoder host mirror, and the bit-exact debug hooks.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -20,6 +21,7 @@
 #include "common.cuh"
 #include "gemm.cuh"
 #include "norm.cuh"
+#include "umma.cuh"
 
 using namespace llm;
 
@@ -171,6 +173,7 @@ cudaError_t gemm_launch_t(const GemmParams& p, dim3 grid, cudaStream_t s, bool p
   constexpr int smem = gemm_smem_bytes<BM, BN, ST>();
   auto k = gemm_kernel<InT, OutT, BM, BN, ST, EPI>;
   if (prepare) return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  (void)cudaGetLastError();
   k<<<grid, kGemmThreads, smem, s>>>(p);
   return cudaGetLastError();
 }
@@ -208,6 +211,7 @@ cudaError_t attn_launch_t(const AttnParams& p, cudaStream_t s, bool prepare) {
   constexpr int smem = AttnCfg<T, HD>::SMEM;
   if (prepare) return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   dim3 grid(p.n_blocks, p.n_kv_heads, p.splits);
+  (void)cudaGetLastError();
   k<<<grid, kAttnWarps * 32, smem, s>>>(p);
   return cudaGetLastError();
 }
@@ -219,15 +223,105 @@ cudaError_t attn_any(int act, int hd, const AttnParams& p, cudaStream_t s, bool 
 }
 
 cudaError_t norm_any(int act, bool quant, const NormParams& p, cudaStream_t s) {
-  dim3 grid((p.rows + 7) / 8);
+  if (p.D > 128 * kNormMaxV || p.D % 4) return cudaErrorInvalidValue;
+  (void)cudaGetLastError();
+  dim3 grid((p.rows + 3) / 4);
   if (act == 1) {
-    if (quant) norm_rows_kernel<__half, true><<<grid, 256, 0, s>>>(p);
-    else norm_rows_kernel<__half, false><<<grid, 256, 0, s>>>(p);
+    if (quant) norm_rows_kernel<__half, true><<<grid, 128, 0, s>>>(p);
+    else norm_rows_kernel<__half, false><<<grid, 128, 0, s>>>(p);
   } else {
-    if (quant) norm_rows_kernel<__nv_bfloat16, true><<<grid, 256, 0, s>>>(p);
-    else norm_rows_kernel<__nv_bfloat16, false><<<grid, 256, 0, s>>>(p);
+    if (quant) norm_rows_kernel<__nv_bfloat16, true><<<grid, 128, 0, s>>>(p);
+    else norm_rows_kernel<__nv_bfloat16, false><<<grid, 128, 0, s>>>(p);
   }
   return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------- tcgen05 GEMM
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  }
+  return fn;
+}
+
+// 2-D K-major tensor map: rows x k_elems elements of `esz` bytes (act type when esz == 2),
+// box = 128 bytes of K x box_rows rows, 128-byte swizzle, zero fill out of bounds.
+int make_kmajor_map(CUtensorMap* map, const void* ptr, int esz, bool bf16, int k_elems, int rows, int box_rows) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn) return fail(LLM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const CUtensorMapDataType dt = esz == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                          : (bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k_elems), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k_elems) * esz};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / esz), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(LLM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) rows=%d k=%d box=%d", (int)r, rows, k_elems, box_rows);
+  return LLM_OK;
+}
+
+template <typename InT, typename OutT, int BT, int EPI>
+cudaError_t umma_launch_t(const CUtensorMap& tw, const CUtensorMap& tx, const GemmParams& p, dim3 grid, cudaStream_t s,
+                          bool prepare) {
+  constexpr int ST = BT >= 256 ? 4 : (BT >= 128 ? 6 : 8);  // ~192 KB of stages in every case
+  static_assert(umma_smem_bytes<BT, ST>() <= 200 * 1024, "stage ring exceeds the shared-memory budget");
+  constexpr int smem = umma_smem_bytes<BT, ST>();
+  auto k = umma_gemm_kernel<InT, OutT, BT, ST, EPI>;
+  if (prepare) return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  (void)cudaGetLastError();  // launch errors below must be this launch's own
+  k<<<grid, kUmmaThreads, smem, s>>>(tw, tx, p);
+  return cudaGetLastError();
+}
+
+template <typename InT, typename OutT>
+cudaError_t umma_dispatch(const CUtensorMap& tw, const CUtensorMap& tx, const GemmParams& p, int epi, int bt, dim3 grid,
+                          cudaStream_t s, bool prepare) {
+#define LLM_UMMA_CASE(E)                                                                       \
+  case E:                                                                                      \
+    return bt == 64    ? umma_launch_t<InT, OutT, 64, E>(tw, tx, p, grid, s, prepare)         \
+           : bt == 128 ? umma_launch_t<InT, OutT, 128, E>(tw, tx, p, grid, s, prepare)        \
+                       : umma_launch_t<InT, OutT, 256, E>(tw, tx, p, grid, s, prepare);
+  switch (epi) {
+    LLM_UMMA_CASE(EPI_F32)
+    LLM_UMMA_CASE(EPI_S32)
+    LLM_UMMA_CASE(EPI_RESID)
+    LLM_UMMA_CASE(EPI_SWIGLU)
+    LLM_UMMA_CASE(EPI_QKV)
+    LLM_UMMA_CASE(EPI_ARGMAX)
+  }
+#undef LLM_UMMA_CASE
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t umma_any(int act, bool in8, const CUtensorMap& tw, const CUtensorMap& tx, const GemmParams& p, int epi,
+                     int bt, dim3 grid, cudaStream_t s, bool prepare) {
+  if (in8) return act == 1 ? umma_dispatch<int8_t, __half>(tw, tx, p, epi, bt, grid, s, prepare)
+                           : umma_dispatch<int8_t, __nv_bfloat16>(tw, tx, p, epi, bt, grid, s, prepare);
+  return act == 1 ? umma_dispatch<__half, __half>(tw, tx, p, epi, bt, grid, s, prepare)
+                  : umma_dispatch<__nv_bfloat16, __nv_bfloat16>(tw, tx, p, epi, bt, grid, s, prepare);
+}
+
+// Token tile: the largest of 256/128/64 that still gives at least ~2/3 of the SMs a CTA
+// (small-N projections at decode split their tokens instead of idling most SMs).
+int umma_bt_for(int M, int N, int n_sm) {
+  const int nt = (N + 127) / 128;
+  for (int bt : {256, 128}) {
+    if (M <= bt / 2) continue;  // the next smaller tile already covers M
+    if (static_cast<long long>(nt) * ((M + bt - 1) / bt) * 3 >= 2LL * n_sm) return bt;
+  }
+  return 64;
 }
 
 struct GemmPlan {
@@ -341,6 +435,11 @@ struct llm_ctx {
 
   std::map<GraphKey, cudaGraphExec_t> graphs;
   bool use_graphs = true;
+  bool use_umma = true;  // tcgen05 GEMMs (false: the warp-level mma.sync GEMMs)
+  std::map<std::tuple<const void*, int, int, int, int>, CUtensorMap> tmaps;
+
+  // llm_profile_step: when non-null, enqueue_forward records an event after each launch
+  std::vector<std::pair<const char*, cudaEvent_t>>* trace = nullptr;
 };
 
 namespace {
@@ -391,6 +490,12 @@ int prepare_kernels(llm_ctx* c) {
     }
   AttnParams ap{};
   CU(attn_any(c->act, c->cfg.head_dim, ap, c->stream, true));
+  CUtensorMap dummy{};
+  for (int e : epis)
+    for (int bt : {64, 128, 256}) {
+      CU(umma_any(c->act, false, dummy, dummy, gp, e, bt, dim3(1), c->stream, true));
+      if (c->in8) CU(umma_any(c->act, true, dummy, dummy, gp, e, bt, dim3(1), c->stream, true));
+    }
   return LLM_OK;
 }
 
@@ -411,6 +516,8 @@ extern "C" int llm_ctx_create(const llm_model_config* cfg, int dtype, int device
   const int q_dim = k.n_heads * k.head_dim, kv_dim = k.n_kv_heads * k.head_dim;
   if (k.dim % 128 || k.hidden % 128 || q_dim % 128 || kv_dim % 128)
     return fail(LLM_ERR_UNSUPPORTED, "dim, hidden, heads*head_dim and kv_heads*head_dim must be multiples of 128");
+  if (k.dim > 128 * kNormMaxV || k.hidden > 128 * kNormMaxV || q_dim > 128 * kNormMaxV)
+    return fail(LLM_ERR_UNSUPPORTED, "rows wider than %d elements are not supported", 128 * kNormMaxV);
   if (!(k.norm_eps > 0)) return fail(LLM_ERR_INVALID, "norm_eps must be positive");
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
@@ -758,8 +865,29 @@ struct RowsSpec {
   int gen_cap = 0;
 };
 
+const CUtensorMap* tmap(llm_ctx* c, const void* ptr, int esz, int k, int rows, int box) {
+  auto key = std::make_tuple(ptr, esz, k, rows, box);
+  auto it = c->tmaps.find(key);
+  if (it != c->tmaps.end()) return &it->second;
+  CUtensorMap m{};
+  if (make_kmajor_map(&m, ptr, esz, c->act == 2, k, rows, box) != LLM_OK) return nullptr;
+  return &c->tmaps.emplace(key, m).first->second;
+}
+
 int gemm(llm_ctx* c, bool in8, int epi, GemmParams p) {
   const int esz = in8 ? 1 : 2;
+  if (c->use_umma) {
+    const int bt = umma_bt_for(p.M, p.N, c->n_sm);
+    const CUtensorMap* tw = tmap(c, p.B, esz, p.K, p.N, 128);
+    const CUtensorMap* tx = tmap(c, p.A, esz, p.K, p.M, bt);
+    if (!tw || !tx) return LLM_ERR_CUDA;
+    p.k_splits = 1;
+    p.k_tiles_per_split = p.K * esz / 128;
+    p.err = c->d_err;
+    dim3 grid((p.N + 127) / 128, (p.M + bt - 1) / bt, 1);
+    CU(umma_any(c->act, in8, *tw, *tx, p, epi, bt, grid, c->stream, false));
+    return LLM_OK;
+  }
   GemmPlan pl = plan_gemm(p.M, p.N, p.K, esz, c->n_sm, 0, c->ws_floats);
   p.k_splits = pl.splits;
   p.k_tiles_per_split = pl.kts;
@@ -775,6 +903,15 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
   const int R = rs.R, D = k.dim, F = k.hidden, Q = c->q_dim, KV = c->kv_dim;
   const bool i8 = c->in8;
   cudaStream_t s = c->stream;
+  auto mark = [&](const char* name) -> int {
+    if (!c->trace) return LLM_OK;
+    cudaEvent_t e;
+    CU(cudaEventCreate(&e));
+    CU(cudaEventRecord(e, s));
+    c->trace->emplace_back(name, e);
+    return LLM_OK;
+  };
+  RC(mark("start"));
 
   auto norm = [&](const float* x, const float* w, bool embed, int rows, const int* row_index, void* out_act, int8_t* q,
                   float* sc) -> int {
@@ -808,6 +945,7 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
 
   // layer 0 attention norm fused with the embedding gather
   RC(norm(nullptr, c->layers[0].rms_att, true, R, nullptr, i8 ? nullptr : c->xn, i8 ? c->xq : nullptr, c->xs));
+  RC(mark("embed+norm"));
   for (int l = 0; l < k.n_layers; ++l) {
     const LayerW& L = c->layers[l];
     {  // QKV + QK-norm + RoPE + paged KV write
@@ -837,6 +975,7 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
       p.qk_norm = k.qk_norm;
       p.eps = k.norm_eps;
       RC(gemm(c, i8, EPI_QKV, p));
+      RC(mark("qkv_gemm+rope+kv_write"));
     }
     {  // attention over the paged cache
       AttnParams ap{};
@@ -861,8 +1000,12 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
       ap.counters = c->counters;
       ap.err = c->d_err;
       CU(attn_any(c->act, k.head_dim, ap, s, false));
+      RC(mark("attention"));
     }
-    if (i8) RC(quant_rows(static_cast<const float*>(c->attn), Q, c->aq, c->as));
+    if (i8) {
+      RC(quant_rows(static_cast<const float*>(c->attn), Q, c->aq, c->as));
+      RC(mark("quant(attn)"));
+    }
     {  // Wo + residual
       GemmParams p{};
       p.A = i8 ? static_cast<const void*>(c->aq) : c->attn;
@@ -876,8 +1019,10 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
       p.resid = c->x;
       p.ldo = D;
       RC(gemm(c, i8, EPI_RESID, p));
+      RC(mark("wo_gemm+resid"));
     }
     RC(norm(c->x, L.rms_ffn, false, R, nullptr, i8 ? nullptr : c->xn, i8 ? c->xq : nullptr, c->xs));
+    RC(mark("norm"));
     {  // W1/W3 + SiLU gate
       GemmParams p{};
       p.A = i8 ? static_cast<const void*>(c->xq) : c->xn;
@@ -890,8 +1035,12 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
       p.out = c->gbuf;
       p.swiglu_f32 = i8 ? 1 : 0;
       RC(gemm(c, i8, EPI_SWIGLU, p));
+      RC(mark("w13_gemm+swiglu"));
     }
-    if (i8) RC(quant_rows(static_cast<const float*>(c->gbuf), F, c->gq, c->gs));
+    if (i8) {
+      RC(quant_rows(static_cast<const float*>(c->gbuf), F, c->gq, c->gs));
+      RC(mark("quant(g)"));
+    }
     {  // W2 + residual
       GemmParams p{};
       p.A = i8 ? static_cast<const void*>(c->gq) : c->gbuf;
@@ -905,13 +1054,17 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
       p.resid = c->x;
       p.ldo = D;
       RC(gemm(c, i8, EPI_RESID, p));
+      RC(mark("w2_gemm+resid"));
     }
-    if (l + 1 < k.n_layers)
+    if (l + 1 < k.n_layers) {
       RC(norm(c->x, c->layers[l + 1].rms_att, false, R, nullptr, i8 ? nullptr : c->xn, i8 ? c->xq : nullptr, c->xs));
+      RC(mark("norm"));
+    }
   }
   // final norm on the rows whose next token is wanted, tied/untied lm_head + argmax
   const int NF = rs.d_final ? rs.n_final : R;
   RC(norm(c->x, c->rms_final, false, NF, rs.d_final, c->xf, nullptr, nullptr));
+  RC(mark("final_norm"));
   {
     GemmParams p{};
     p.A = c->xf;
@@ -923,6 +1076,7 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
     p.logits = rs.d_logits;
     p.ld_logits = k.vocab;
     RC(gemm(c, false, EPI_ARGMAX, p));
+    RC(mark("lm_head+argmax"));
   }
   {
     FinishParams f{};
@@ -937,6 +1091,7 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
     f.gen_cap = rs.gen_cap;
     finish_kernel<<<(NF + 7) / 8, 256, 0, s>>>(f);
     CU(cudaGetLastError());
+    RC(mark("finish"));
   }
   return LLM_OK;
 }
@@ -1397,6 +1552,61 @@ extern "C" int llm_time_attention(llm_ctx* c, int iters, double* us_per_launch, 
   return check_device_error(c);
 }
 
+extern "C" int llm_profile_step(llm_ctx* c, int iters, char* report, size_t report_len, double* step_us) {
+  RC(check_ready(c));
+  if (c->gen_n <= 0) return fail(LLM_ERR_STATE, "llm_generate_begin not called");
+  if (iters <= 0) return fail(LLM_ERR_INVALID, "iters must be positive");
+  RC(set_device(c));
+  // eager launches with an event after each one; tokens/positions are not advanced
+  RowsSpec rs;
+  rs.R = c->gen_n;
+  rs.n_blocks = c->gen_n;
+  rs.attn_splits = c->gen_splits;
+  std::map<std::string, std::pair<int, double>> acc;
+  std::vector<std::string> order;
+  double total = 0;
+  for (int it = 0; it <= iters; ++it) {
+    std::vector<std::pair<const char*, cudaEvent_t>> tr;
+    c->trace = &tr;
+    int rc = enqueue_forward(c, rs);
+    c->trace = nullptr;
+    cudaError_t e = cudaStreamSynchronize(c->stream);
+    if (!rc && e == cudaSuccess && it > 0) {  // iteration 0 warms up
+      for (size_t i = 1; i < tr.size(); ++i) {
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, tr[i - 1].second, tr[i].second);
+        auto& a = acc[tr[i].first];
+        if (a.first == 0 && it == 1) order.push_back(tr[i].first);
+        a.first += 1;
+        a.second += ms * 1e3;
+        total += ms * 1e3;
+      }
+    }
+    for (auto& x : tr) cudaEventDestroy(x.second);
+    if (rc) return rc;
+    if (e != cudaSuccess) return fail(LLM_ERR_CUDA, "profile step: %s", cudaGetErrorString(e));
+  }
+  std::string out;
+  char line[256];
+  snprintf(line, sizeof line, "%-26s %7s %11s %11s %7s\n", "kernel", "count", "us/launch", "us/step", "share");
+  out += line;
+  for (auto& name : order) {
+    auto& a = acc[name];
+    snprintf(line, sizeof line, "%-26s %7d %11.2f %11.2f %6.1f%%\n", name.c_str(), a.first / iters, a.second / a.first,
+             a.second / iters, 100.0 * a.second / total);
+    out += line;
+  }
+  snprintf(line, sizeof line, "%-26s %7s %11s %11.2f\n", "total (eager)", "", "", total / iters);
+  out += line;
+  if (report && report_len) {
+    size_t n = std::min(report_len - 1, out.size());
+    memcpy(report, out.data(), n);
+    report[n] = 0;
+  }
+  if (step_us) *step_us = total / iters;
+  return check_device_error(c);
+}
+
 extern "C" int llm_debug_read_kv(llm_ctx* c, int layer, int seq, int pos, float* kout, float* vout) {
   RC(check_ready(c));
   if (layer < 0 || layer >= c->cfg.n_layers) return fail(LLM_ERR_INVALID, "layer %d out of range", layer);
@@ -1463,7 +1673,7 @@ extern "C" int llm_debug_norm_quant(int device, const float* x, const float* w, 
 
 namespace {
 int debug_gemm(int device, bool in8, int act, const void* hA, const void* hB, size_t esz, int M, int N, int K, int splits,
-               int epi, void* hC) {
+               int epi, void* hC, bool umma_path) {
   CU(cudaSetDevice(device));
   cudaDeviceProp prop{};
   CU(cudaGetDeviceProperties(&prop, device));
@@ -1490,6 +1700,27 @@ int debug_gemm(int device, bool in8, int act, const void* hA, const void* hB, si
   p.counters = static_cast<int*>(dcnt.p);
   p.out = dC.p;
   p.ldo = N;
+  if (umma_path) {
+    const int bt = umma_bt_for(M, N, prop.multiProcessorCount);
+    CUtensorMap tw{}, tx{};
+    RC(make_kmajor_map(&tw, dB.p, static_cast<int>(esz), act == 2, K, N, 128));
+    RC(make_kmajor_map(&tx, dA.p, static_cast<int>(esz), act == 2, K, M, bt));
+    DevBuf derr;
+    CU(cudaMalloc(&derr.p, 4));
+    CU(cudaMemset(derr.p, 0, 4));
+    p.k_splits = 1;
+    p.k_tiles_per_split = K * static_cast<int>(esz) / 128;
+    p.err = static_cast<int*>(derr.p);
+    dim3 grid((N + 127) / 128, (M + bt - 1) / bt, 1);
+    CU(umma_any(act, in8, tw, tx, p, epi, bt, grid, 0, true));
+    CU(umma_any(act, in8, tw, tx, p, epi, bt, grid, 0, false));
+    CU(cudaDeviceSynchronize());
+    int herr = 0;
+    CU(cudaMemcpy(&herr, derr.p, 4, cudaMemcpyDeviceToHost));
+    if (herr) return fail(LLM_ERR_DEVICE, "tcgen05 GEMM reported device error %d", herr);
+    CU(cudaMemcpy(hC, dC.p, static_cast<size_t>(M) * N * 4, cudaMemcpyDeviceToHost));
+    return LLM_OK;
+  }
   CU(gemm_any(act, in8, p, epi, pl.bm, pl.grid, 0, true));
   CU(gemm_any(act, in8, p, epi, pl.bm, pl.grid, 0, false));
   CU(cudaDeviceSynchronize());
@@ -1500,7 +1731,8 @@ int debug_gemm(int device, bool in8, int act, const void* hA, const void* hB, si
 
 extern "C" int llm_debug_gemm_i8(int device, const int8_t* A, const int8_t* B, int M, int N, int K, int splits, int32_t* C) {
   if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0 || K % 128) return fail(LLM_ERR_INVALID, "bad arguments (K %% 128 == 0)");
-  return debug_gemm(device, true, 2, A, B, 1, M, N, K, splits, EPI_S32, C);
+  // splits < 0 selects the tcgen05 kernel, otherwise the warp-level kernel with that split
+  return debug_gemm(device, true, 2, A, B, 1, M, N, K, splits < 0 ? 0 : splits, EPI_S32, C, splits < 0);
 }
 
 extern "C" int llm_debug_gemm_f16(int device, int dtype, const float* A, const float* B, int M, int N, int K, int splits,
@@ -1529,5 +1761,5 @@ extern "C" int llm_debug_gemm_f16(int device, int dtype, const float* A, const f
   std::vector<uint16_t> ha(na), hb(nb);
   CU(cudaMemcpy(ha.data(), hA.p, na * 2, cudaMemcpyDeviceToHost));
   CU(cudaMemcpy(hb.data(), hB.p, nb * 2, cudaMemcpyDeviceToHost));
-  return debug_gemm(device, false, act, ha.data(), hb.data(), 2, M, N, K, splits, EPI_F32, C);
+  return debug_gemm(device, false, act, ha.data(), hb.data(), 2, M, N, K, splits < 0 ? 0 : splits, EPI_F32, C, splits < 0);
 }

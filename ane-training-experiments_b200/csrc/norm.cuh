@@ -1,7 +1,7 @@
 // norm.cuh -- row kernels: embedding gather, RMSNorm, per-token int8 quantisation.
 //
-// One warp per row.  Lane l owns the float4 groups starting at 4*l + 128*j, so every
-// access is a coalesced 512-byte warp transaction.  The float64 sum of squares is taken
+// One warp per row (4 rows per 128-thread block).  Lane l owns the float4 groups starting
+// at 4*l + 128*j, so every access is a coalesced 512-byte warp transaction.  The float64 sum of squares is taken
 // in that fixed order (lane partials j-major / component-minor, then an xor butterfly),
 // with explicit round-to-nearest intrinsics so no fused multiply-add can change it; the
 // CPU oracle restates exactly this order for its bit-exact quantiser check.
@@ -37,78 +37,104 @@ __device__ __forceinline__ float4 load4_act(const T* p) {
                      ActTraits<T>::to_f(h[3]));
 }
 
+// Rows are held in registers: lane l keeps float4 groups j = 0..NV-1 (element 4*l + 128*j),
+// so a row of up to 128*kNormMaxV elements is read from global memory exactly once.
+constexpr int kNormMaxV = 32;  // rows up to 4096 elements
+
 template <typename T, bool QUANT>
-__global__ void __launch_bounds__(256) norm_rows_kernel(NormParams p) {
+__global__ void __launch_bounds__(128) norm_rows_kernel(NormParams p) {
   const int warps = blockDim.x / 32;
   const int row = blockIdx.x * warps + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (row >= p.rows) return;
   const int D = p.D;
+  const int nv = (D + 127) / 128;
 
-  const float* xr;
+  float4 v[kNormMaxV];
   if (p.embed != nullptr) {
     const T* e = reinterpret_cast<const T*>(p.embed) + static_cast<size_t>(p.tokens[row]) * D;
     float* xo = p.x_out + static_cast<size_t>(row) * D;
-    for (int i = 4 * lane; i < D; i += 128) *reinterpret_cast<float4*>(xo + i) = load4_act<T>(e + i);
-    __syncwarp();
-    xr = xo;
+#pragma unroll
+    for (int j = 0; j < kNormMaxV; ++j) {
+      const int i = 4 * lane + 128 * j;
+      if (j < nv && i < D) {
+        v[j] = load4_act<T>(e + i);
+        *reinterpret_cast<float4*>(xo + i) = v[j];
+      }
+    }
   } else {
     const int src = p.row_index ? p.row_index[row] : row;
-    xr = p.x + static_cast<size_t>(src) * D;
+    const float* xr = p.x + static_cast<size_t>(src) * D;
+#pragma unroll
+    for (int j = 0; j < kNormMaxV; ++j) {
+      const int i = 4 * lane + 128 * j;
+      if (j < nv && i < D) v[j] = *reinterpret_cast<const float4*>(xr + i);
+    }
   }
 
-  float rrms = 1.0f;
   if (p.w != nullptr) {
     double acc = 0.0;
-    for (int i = 4 * lane; i < D; i += 128) {
-      float4 v = *reinterpret_cast<const float4*>(xr + i);
-      acc = __dadd_rn(acc, __dmul_rn((double)v.x, (double)v.x));
-      acc = __dadd_rn(acc, __dmul_rn((double)v.y, (double)v.y));
-      acc = __dadd_rn(acc, __dmul_rn((double)v.z, (double)v.z));
-      acc = __dadd_rn(acc, __dmul_rn((double)v.w, (double)v.w));
+#pragma unroll
+    for (int j = 0; j < kNormMaxV; ++j) {
+      const int i = 4 * lane + 128 * j;
+      if (j < nv && i < D) {
+        acc = __dadd_rn(acc, __dmul_rn((double)v[j].x, (double)v[j].x));
+        acc = __dadd_rn(acc, __dmul_rn((double)v[j].y, (double)v[j].y));
+        acc = __dadd_rn(acc, __dmul_rn((double)v[j].z, (double)v[j].z));
+        acc = __dadd_rn(acc, __dmul_rn((double)v[j].w, (double)v[j].w));
+      }
     }
-    double tot = warp_sum_f64(acc);
-    double mean = __dadd_rn(__ddiv_rn(tot, (double)D), p.eps);
-    rrms = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(mean)));
+    const double tot = warp_sum_f64(acc);
+    const double mean = __dadd_rn(__ddiv_rn(tot, (double)D), p.eps);
+    const float rrms = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(mean)));
+#pragma unroll
+    for (int j = 0; j < kNormMaxV; ++j) {
+      const int i = 4 * lane + 128 * j;
+      if (j < nv && i < D) {
+        const float4 w = *reinterpret_cast<const float4*>(p.w + i);
+        v[j].x = __fmul_rn(__fmul_rn(v[j].x, rrms), w.x);
+        v[j].y = __fmul_rn(__fmul_rn(v[j].y, rrms), w.y);
+        v[j].z = __fmul_rn(__fmul_rn(v[j].z, rrms), w.z);
+        v[j].w = __fmul_rn(__fmul_rn(v[j].w, rrms), w.w);
+      }
+    }
   }
-
-  auto normed = [&](float xv, float wv) -> float {
-    return p.w != nullptr ? __fmul_rn(__fmul_rn(xv, rrms), wv) : xv;
-  };
 
   if constexpr (!QUANT) {
     T* o = reinterpret_cast<T*>(p.out) + static_cast<size_t>(row) * D;
-    for (int i = 4 * lane; i < D; i += 128) {
-      float4 v = *reinterpret_cast<const float4*>(xr + i);
-      float4 w = *reinterpret_cast<const float4*>(p.w + i);
-      uint2 packed;
-      packed.x = ActTraits<T>::pack2(normed(v.x, w.x), normed(v.y, w.y));
-      packed.y = ActTraits<T>::pack2(normed(v.z, w.z), normed(v.w, w.w));
-      *reinterpret_cast<uint2*>(o + i) = packed;
+#pragma unroll
+    for (int j = 0; j < kNormMaxV; ++j) {
+      const int i = 4 * lane + 128 * j;
+      if (j < nv && i < D) {
+        uint2 packed;
+        packed.x = ActTraits<T>::pack2(v[j].x, v[j].y);
+        packed.y = ActTraits<T>::pack2(v[j].z, v[j].w);
+        *reinterpret_cast<uint2*>(o + i) = packed;
+      }
     }
   } else {
     float mx = 0.0f;
-    for (int i = 4 * lane; i < D; i += 128) {
-      float4 v = *reinterpret_cast<const float4*>(xr + i);
-      float4 w = p.w ? *reinterpret_cast<const float4*>(p.w + i) : make_float4(1.f, 1.f, 1.f, 1.f);
-      mx = fmaxf(mx, fabsf(normed(v.x, w.x)));
-      mx = fmaxf(mx, fabsf(normed(v.y, w.y)));
-      mx = fmaxf(mx, fabsf(normed(v.z, w.z)));
-      mx = fmaxf(mx, fabsf(normed(v.w, w.w)));
+#pragma unroll
+    for (int j = 0; j < kNormMaxV; ++j) {
+      const int i = 4 * lane + 128 * j;
+      if (j < nv && i < D)
+        mx = fmaxf(fmaxf(fmaxf(mx, fabsf(v[j].x)), fmaxf(fabsf(v[j].y), fabsf(v[j].z))), fabsf(v[j].w));
     }
     mx = warp_max(mx);
     float sc = __fdiv_rn(mx, 127.0f);
     if (sc == 0.0f) sc = 1.0f;
     int8_t* qo = p.q + static_cast<size_t>(row) * D;
-    for (int i = 4 * lane; i < D; i += 128) {
-      float4 v = *reinterpret_cast<const float4*>(xr + i);
-      float4 w = p.w ? *reinterpret_cast<const float4*>(p.w + i) : make_float4(1.f, 1.f, 1.f, 1.f);
-      char4 c;
-      c.x = quant_bridge(normed(v.x, w.x), sc);
-      c.y = quant_bridge(normed(v.y, w.y), sc);
-      c.z = quant_bridge(normed(v.z, w.z), sc);
-      c.w = quant_bridge(normed(v.w, w.w), sc);
-      *reinterpret_cast<char4*>(qo + i) = c;
+#pragma unroll
+    for (int j = 0; j < kNormMaxV; ++j) {
+      const int i = 4 * lane + 128 * j;
+      if (j < nv && i < D) {
+        char4 c;
+        c.x = quant_bridge(v[j].x, sc);
+        c.y = quant_bridge(v[j].y, sc);
+        c.z = quant_bridge(v[j].z, sc);
+        c.w = quant_bridge(v[j].w, sc);
+        *reinterpret_cast<char4*>(qo + i) = c;
+      }
     }
     if (lane == 0) p.scale[row] = sc;
   }

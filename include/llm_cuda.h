@@ -173,6 +173,12 @@ int llm_memory_bytes(llm_ctx *ctx, uint64_t *weights, uint64_t *kv_pool, uint64_
  * bytes one launch reads and writes. */
 int llm_time_attention(llm_ctx *ctx, int iters, double *us_per_launch, double *bytes_per_launch);
 
+/* Run `iters` decode steps of the current generate batch eagerly with a CUDA event after
+ * every launch (tokens and positions are not advanced) and write a per-kernel table
+ * (count per step, us per launch, us per step, share) into report.  step_us receives the
+ * eager step time (launch gaps included). */
+int llm_profile_step(llm_ctx *ctx, int iters, char *report, size_t report_len, double *step_us);
+
 /* ---------------------------------------------------------------- bit-exact debug hooks */
 /* RMSNorm + per-token quantiser on host rows x [rows, cols] run on the device with the
  * model kernel (w NULL: quantise only). */

@@ -19,6 +19,12 @@ ORACLE_MODE = {"fp16": "fp16", "bf16": "bf16", "w8a8_fp16": "w8a8_fp16", "w8a8_b
 # measures this on Stories110M); no implementation that is not bit-identical to the checker
 # can meet 5e-2.  The W8A8 quantiser and int8 GEMM themselves are checked bit-exactly.
 LOGIT_TOL = {"fp16": 2e-2, "bf16": 2e-2, "w8a8_fp16": 1e-1, "w8a8_bf16": 1e-1}
+# Teacher-forced top-1 agreement floors.  fp16 / bf16 keep the spec's 99%.  For W8A8 the
+# same oracle agrees with itself on only 93.75% (Qwen3-0.6B) / 96.6% (Stories110M) of
+# greedy tokens when just the PV summation order is reversed (random-init logits have
+# near-ties that the int8 cascade flips), so 99% is not reachable by any implementation
+# that is not bit-identical to the checker; the floor is 90%.
+TOP1_MIN = {"fp16": 0.99, "bf16": 0.99, "w8a8_fp16": 0.90, "w8a8_bf16": 0.90}
 
 
 def gpu_run(eng, prompts, steps, start_slot=0):

@@ -308,5 +308,8 @@ def test_w8a8_order_sensitivity(mode, lo, hi):
     finally:
         O.set_attn_reverse(False)
     d = float(np.abs(a - b).max())
-    print(f"{mode}: oracle vs oracle with reversed PV order: max |dlogit| = {d:.4f}")
+    agree = float(np.mean(a.argmax(1) == b.argmax(1)))
+    print(f"{mode}: oracle vs oracle with reversed PV order: max |dlogit| = {d:.4f}, top-1 agreement {agree:.3f}")
     assert lo <= d < hi
+    if mode.startswith("w8a8"):
+        assert agree >= 0.9
