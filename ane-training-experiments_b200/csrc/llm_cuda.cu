@@ -52,6 +52,9 @@ int fail(int code, const char* fmt, ...) {
   } while (0)
 }  // namespace
 
+// Lets the library's other translation units record the thread's last error.
+int llm_detail_fail(int code, const char* msg) { return fail(code, "%s", msg); }
+
 extern "C" int llm_last_error(char* buf, size_t n) {
   if (buf && n) {
     size_t k = std::min(n - 1, g_last_error.size());

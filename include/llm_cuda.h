@@ -179,6 +179,21 @@ int llm_time_attention(llm_ctx *ctx, int iters, double *us_per_launch, double *b
  * eager step time (launch gaps included). */
 int llm_profile_step(llm_ctx *ctx, int iters, char *report, size_t report_len, double *step_us);
 
+/* ---------------------------------------------------------------- allocation-free entry point */
+/* No counterpart in the reference.  Split-K int8 GEMM C[M,N] = A[M,K] . B[N,K]^T with int32
+ * output that allocates nothing: for callers that cannot allocate device memory while they
+ * run (a server whose KV page pool already holds the GPU's memory, a decode loop that must not
+ * take cudaFree's device-wide synchronisation mid-step, an FFI host that owns the memory
+ * policy).  A, B and C are caller-owned DEVICE pointers; the work is enqueued on `stream`
+ * (NULL = default stream) and the call returns without waiting.  The split partials and tile
+ * counters live in one fixed device array of 4 MiB + 1024 counters inside the library; a
+ * shape/split combination needing more is rejected with LLM_ERR_INVALID.  The first call on a
+ * device resolves that array's device address and sets kernel attributes, so make it before
+ * any stream capture.  Every call shares the array: calls whose executions overlap on the GPU
+ * (other streams or threads) race. */
+int llm_gemm_i8_splitk_noalloc(int device, const int8_t *A, const int8_t *B, int M, int N, int K, int splits,
+                               int32_t *C, void *stream);
+
 /* ---------------------------------------------------------------- bit-exact debug hooks */
 /* RMSNorm + per-token quantiser on host rows x [rows, cols] run on the device with the
  * model kernel (w NULL: quantise only). */
