@@ -42,6 +42,11 @@ struct AttnParams {
   int out_f32;
   float* ws;                  // splits > 1: [n_blocks][n_kv_heads][splits][8][HD + 2]
   int* counters;              // splits > 1: [n_blocks][n_kv_heads]
+  // optional fused per-token int8 quantisation of the fp32 output (out_f32 only): the last
+  // CTA to finish a row (row_counters, zero between launches) quantises it
+  int8_t* q8;                 // [rows][n_heads * HD]
+  float* q8_scale;            // [rows]
+  int* row_counters;          // [rows]
   int* err;
 };
 
@@ -60,6 +65,59 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
 }
 
+// Fused per-token quantisation: called by every CTA after it stored its rows' fp32 outputs.
+// The CTA that completes a row (the last of its n_kv_heads producers) reads the whole row back
+// from L2 and applies the bridge quantiser exactly as the row kernel in norm.cuh does.
+template <int HD>
+__device__ void attn_quant_rows(const AttnParams& p, int r0, int nq, int group, int* s_rowlast, float* s_wmax) {
+  if (p.q8 == nullptr) return;
+  const int nrows = min(nq, 8);  // rows r0..r0+nq-1 (nq <= 8 / group)
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x < nrows) {
+    const int prev = atomicAdd(p.row_counters + r0 + threadIdx.x, 1);
+    s_rowlast[threadIdx.x] = prev == p.n_kv_heads - 1;
+  }
+  __syncthreads();
+  const int cols = p.n_heads * HD;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = 0; i < nrows; ++i) {
+    if (!s_rowlast[i]) continue;  // uniform across the CTA
+    __threadfence();
+    const int row = r0 + i;
+    const float* src = reinterpret_cast<const float*>(p.out) + static_cast<size_t>(row) * cols;
+    float mx = 0.0f;
+    for (int c = 4 * threadIdx.x; c < cols; c += 4 * kAttnWarps * 32) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(src + c));
+      mx = fmaxf(fmaxf(fmaxf(mx, fabsf(v.x)), fmaxf(fabsf(v.y), fabsf(v.z))), fabsf(v.w));
+    }
+    mx = warp_max(mx);
+    if (lane == 0) s_wmax[warp] = mx;
+    __syncthreads();
+    mx = s_wmax[0];
+#pragma unroll
+    for (int w = 1; w < kAttnWarps; ++w) mx = fmaxf(mx, s_wmax[w]);
+    float sc = __fdiv_rn(mx, 127.0f);
+    if (sc == 0.0f) sc = 1.0f;
+    const float inv = __fdiv_rn(1.0f, sc);
+    int8_t* qo = p.q8 + static_cast<size_t>(row) * cols;
+    for (int c = 4 * threadIdx.x; c < cols; c += 4 * kAttnWarps * 32) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(src + c));
+      char4 q;
+      q.x = quant_bridge_fast(v.x, sc, inv);
+      q.y = quant_bridge_fast(v.y, sc, inv);
+      q.z = quant_bridge_fast(v.z, sc, inv);
+      q.w = quant_bridge_fast(v.w, sc, inv);
+      *reinterpret_cast<char4*>(qo + c) = q;
+    }
+    if (threadIdx.x == 0) {
+      p.q8_scale[row] = sc;
+      p.row_counters[row] = 0;
+    }
+    __syncthreads();
+  }
+}
+
 template <typename T, int HD>
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(AttnParams p) {
   using Cfg = AttnCfg<T, HD>;
@@ -71,6 +129,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(AttnParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ __align__(8) uint64_t bars[kAttnWarps][STAGES];
   __shared__ int s_last;
+  __shared__ int s_rowlast[8];
+  __shared__ float s_wmax[kAttnWarps];
 
   const int blk = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -307,7 +367,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(AttnParams p) {
       }
     }
   }
-  if (!multi) return;
+  if (!multi) {
+    attn_quant_rows<HD>(p, r0, nq, group, s_rowlast, s_wmax);
+    return;
+  }
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -337,6 +400,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(AttnParams p) {
     else reinterpret_cast<T*>(p.out)[oi] = ActTraits<T>::from_f(v);
   }
   if (threadIdx.x == 0) p.counters[blk * p.n_kv_heads + kvh] = 0;
+  attn_quant_rows<HD>(p, r0, nq, group, s_rowlast, s_wmax);
 }
 
 }  // namespace llm

@@ -172,6 +172,23 @@ __device__ __forceinline__ int8_t quant_bridge(float x, float scale) {
   return static_cast<int8_t>(__float2int_rz(r));
 }
 
+// The same result as quant_bridge(x, scale) without a division in the common case:
+// y = x * inv (inv = 1/scale rounded) is within 2 ulps of fl(x / scale), and the bridge rule
+// only depends on where the quotient falls relative to the k + 0.5 rounding points and the
+// clamp, so when y is more than 4 ulps from every such point it decides the same integer;
+// otherwise the exact IEEE quotient is computed.
+__device__ __forceinline__ int8_t quant_bridge_fast(float x, float scale, float inv) {
+  const float y = __fmul_rn(x, inv);
+  const float a = fabsf(y);
+  const float frac = a - floorf(a);
+  const bool near = fabsf(frac - 0.5f) <= __fmul_rn(a, 4.76837158203125e-7f) + 1e-30f || a >= 126.0f;
+  const float v0 = near ? __fdiv_rn(x, scale) : y;
+  float v = fminf(v0, 127.0f);
+  v = fmaxf(v, -128.0f);
+  const float r = __fadd_rn(v, v >= 0.0f ? 0.5f : -0.5f);
+  return static_cast<int8_t>(__float2int_rz(r));
+}
+
 // Byte offset of 16-byte chunk `chunk` of row `row` in a tile whose rows are `row_bytes`
 // long, XOR-swizzled within each 128-byte group so that 8 consecutive rows reading the
 // same logical chunk hit 8 different bank groups.

@@ -225,18 +225,29 @@ cudaError_t attn_any(int act, int hd, const AttnParams& p, cudaStream_t s, bool 
                   : attn_launch_t<__nv_bfloat16, 128>(p, s, prepare);
 }
 
+template <typename T, bool Q>
+cudaError_t norm_launch(const NormParams& p, cudaStream_t s) {
+  dim3 grid((p.rows + 3) / 4);
+  (void)cudaGetLastError();
+  switch (p.D / 128) {
+#define LLM_NORM_NV(n) \
+  case n:              \
+    if (p.D == 128 * n) { norm_rows_kernel<T, Q, n><<<grid, 128, 0, s>>>(p); return cudaGetLastError(); } \
+    break;
+    LLM_NORM_NV(1) LLM_NORM_NV(2) LLM_NORM_NV(4) LLM_NORM_NV(6) LLM_NORM_NV(8) LLM_NORM_NV(12) LLM_NORM_NV(16)
+    LLM_NORM_NV(24) LLM_NORM_NV(32)
+#undef LLM_NORM_NV
+    default:
+      break;
+  }
+  norm_rows_kernel<T, Q, 0><<<grid, 128, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
 cudaError_t norm_any(int act, bool quant, const NormParams& p, cudaStream_t s) {
   if (p.D > 128 * kNormMaxV || p.D % 4) return cudaErrorInvalidValue;
-  (void)cudaGetLastError();
-  dim3 grid((p.rows + 3) / 4);
-  if (act == 1) {
-    if (quant) norm_rows_kernel<__half, true><<<grid, 128, 0, s>>>(p);
-    else norm_rows_kernel<__half, false><<<grid, 128, 0, s>>>(p);
-  } else {
-    if (quant) norm_rows_kernel<__nv_bfloat16, true><<<grid, 128, 0, s>>>(p);
-    else norm_rows_kernel<__nv_bfloat16, false><<<grid, 128, 0, s>>>(p);
-  }
-  return cudaGetLastError();
+  if (act == 1) return quant ? norm_launch<__half, true>(p, s) : norm_launch<__half, false>(p, s);
+  return quant ? norm_launch<__nv_bfloat16, true>(p, s) : norm_launch<__nv_bfloat16, false>(p, s);
 }
 
 // ---------------------------------------------------------------------------- tcgen05 GEMM
@@ -430,6 +441,7 @@ struct llm_ctx {
   float* ws = nullptr;
   size_t ws_floats = 0;
   int* counters = nullptr;
+  int* row_counters = nullptr;  // [max_rows] fused attention-output quantisation
   int* d_err = nullptr;
 
   // generate state
@@ -774,6 +786,8 @@ extern "C" int llm_kv_alloc(llm_ctx* c, int max_seqs, int max_pos, int page_toke
   RC(dalloc_t(c, &c->ws, c->ws_floats * 4, o));
   RC(dalloc_t(c, &c->counters, 65536 * 4, o));
   CU(cudaMemset(c->counters, 0, 65536 * 4));
+  RC(dalloc_t(c, &c->row_counters, static_cast<size_t>(R) * 4, o));
+  CU(cudaMemset(c->row_counters, 0, static_cast<size_t>(R) * 4));
   c->h_pin_ints = static_cast<size_t>(R) * 8;
   CU(cudaMallocHost(&c->h_pin, c->h_pin_ints * 4));
   c->kv_ready = true;
@@ -1002,12 +1016,13 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
       ap.ws = c->ws;
       ap.counters = c->counters;
       ap.err = c->d_err;
+      if (i8) {  // per-token quantisation of the output fused into the attention kernel
+        ap.q8 = c->aq;
+        ap.q8_scale = c->as;
+        ap.row_counters = c->row_counters;
+      }
       CU(attn_any(c->act, k.head_dim, ap, s, false));
-      RC(mark("attention"));
-    }
-    if (i8) {
-      RC(quant_rows(static_cast<const float*>(c->attn), Q, c->aq, c->as));
-      RC(mark("quant(attn)"));
+      RC(mark(i8 ? "attention+quant" : "attention"));
     }
     {  // Wo + residual
       GemmParams p{};
@@ -1480,9 +1495,9 @@ extern "C" int llm_synchronize(llm_ctx* c) {
 
 extern "C" int llm_step_kernel_count(llm_ctx* c, int n, int* count) {
   if (!c || !count) return fail(LLM_ERR_INVALID, "nil argument");
-  // embed+norm, per layer: qkv, attention, wo, norm, w13, w2 (+ 2 quant kernels for int8)
+  // embed+norm, per layer: qkv, attention, wo, norm, w13, w2 (+ the SwiGLU quant kernel for int8)
   // + the next layer's norm, then final norm, lm_head, finish
-  const int per_layer = 6 + (c->in8 ? 2 : 0);
+  const int per_layer = 6 + (c->in8 ? 1 : 0);
   *count = 1 + c->cfg.n_layers * per_layer + (c->cfg.n_layers - 1) + 3;
   (void)n;
   return LLM_OK;

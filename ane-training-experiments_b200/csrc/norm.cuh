@@ -38,104 +38,94 @@ __device__ __forceinline__ float4 load4_act(const T* p) {
 }
 
 // Rows are held in registers: lane l keeps float4 groups j = 0..NV-1 (element 4*l + 128*j),
-// so a row of up to 128*kNormMaxV elements is read from global memory exactly once.
+// so a row of 128*NV elements is read from global memory exactly once.  NV is a template
+// parameter so the code is exactly as long as the row needs (a generic NV = 0 variant loops
+// over any multiple of 4 up to 128*kNormMaxV).
 constexpr int kNormMaxV = 32;  // rows up to 4096 elements
 
-template <typename T, bool QUANT>
+template <typename T, bool QUANT, int NV>
 __global__ void __launch_bounds__(128) norm_rows_kernel(NormParams p) {
+  constexpr int CAP = NV > 0 ? NV : kNormMaxV;
   const int warps = blockDim.x / 32;
   const int row = blockIdx.x * warps + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (row >= p.rows) return;
   const int D = p.D;
-  const int nv = (D + 127) / 128;
+  const int nv = NV > 0 ? NV : (D + 127) / 128;
+  auto live = [&](int j) { return NV > 0 ? true : (j < nv && 4 * lane + 128 * j < D); };
 
-  float4 v[kNormMaxV];
+  float4 v[CAP];
   if (p.embed != nullptr) {
     const T* e = reinterpret_cast<const T*>(p.embed) + static_cast<size_t>(p.tokens[row]) * D;
     float* xo = p.x_out + static_cast<size_t>(row) * D;
 #pragma unroll
-    for (int j = 0; j < kNormMaxV; ++j) {
-      const int i = 4 * lane + 128 * j;
-      if (j < nv && i < D) {
-        v[j] = load4_act<T>(e + i);
-        *reinterpret_cast<float4*>(xo + i) = v[j];
+    for (int j = 0; j < CAP; ++j)
+      if (live(j)) {
+        v[j] = load4_act<T>(e + 4 * lane + 128 * j);
+        *reinterpret_cast<float4*>(xo + 4 * lane + 128 * j) = v[j];
       }
-    }
   } else {
     const int src = p.row_index ? p.row_index[row] : row;
     const float* xr = p.x + static_cast<size_t>(src) * D;
 #pragma unroll
-    for (int j = 0; j < kNormMaxV; ++j) {
-      const int i = 4 * lane + 128 * j;
-      if (j < nv && i < D) v[j] = *reinterpret_cast<const float4*>(xr + i);
-    }
+    for (int j = 0; j < CAP; ++j)
+      if (live(j)) v[j] = *reinterpret_cast<const float4*>(xr + 4 * lane + 128 * j);
   }
 
   if (p.w != nullptr) {
     double acc = 0.0;
 #pragma unroll
-    for (int j = 0; j < kNormMaxV; ++j) {
-      const int i = 4 * lane + 128 * j;
-      if (j < nv && i < D) {
+    for (int j = 0; j < CAP; ++j)
+      if (live(j)) {
         acc = __dadd_rn(acc, __dmul_rn((double)v[j].x, (double)v[j].x));
         acc = __dadd_rn(acc, __dmul_rn((double)v[j].y, (double)v[j].y));
         acc = __dadd_rn(acc, __dmul_rn((double)v[j].z, (double)v[j].z));
         acc = __dadd_rn(acc, __dmul_rn((double)v[j].w, (double)v[j].w));
       }
-    }
     const double tot = warp_sum_f64(acc);
     const double mean = __dadd_rn(__ddiv_rn(tot, (double)D), p.eps);
     const float rrms = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(mean)));
 #pragma unroll
-    for (int j = 0; j < kNormMaxV; ++j) {
-      const int i = 4 * lane + 128 * j;
-      if (j < nv && i < D) {
-        const float4 w = *reinterpret_cast<const float4*>(p.w + i);
+    for (int j = 0; j < CAP; ++j)
+      if (live(j)) {
+        const float4 w = *reinterpret_cast<const float4*>(p.w + 4 * lane + 128 * j);
         v[j].x = __fmul_rn(__fmul_rn(v[j].x, rrms), w.x);
         v[j].y = __fmul_rn(__fmul_rn(v[j].y, rrms), w.y);
         v[j].z = __fmul_rn(__fmul_rn(v[j].z, rrms), w.z);
         v[j].w = __fmul_rn(__fmul_rn(v[j].w, rrms), w.w);
       }
-    }
   }
 
   if constexpr (!QUANT) {
     T* o = reinterpret_cast<T*>(p.out) + static_cast<size_t>(row) * D;
 #pragma unroll
-    for (int j = 0; j < kNormMaxV; ++j) {
-      const int i = 4 * lane + 128 * j;
-      if (j < nv && i < D) {
+    for (int j = 0; j < CAP; ++j)
+      if (live(j)) {
         uint2 packed;
         packed.x = ActTraits<T>::pack2(v[j].x, v[j].y);
         packed.y = ActTraits<T>::pack2(v[j].z, v[j].w);
-        *reinterpret_cast<uint2*>(o + i) = packed;
+        *reinterpret_cast<uint2*>(o + 4 * lane + 128 * j) = packed;
       }
-    }
   } else {
     float mx = 0.0f;
 #pragma unroll
-    for (int j = 0; j < kNormMaxV; ++j) {
-      const int i = 4 * lane + 128 * j;
-      if (j < nv && i < D)
-        mx = fmaxf(fmaxf(fmaxf(mx, fabsf(v[j].x)), fmaxf(fabsf(v[j].y), fabsf(v[j].z))), fabsf(v[j].w));
-    }
+    for (int j = 0; j < CAP; ++j)
+      if (live(j)) mx = fmaxf(fmaxf(fmaxf(mx, fabsf(v[j].x)), fmaxf(fabsf(v[j].y), fabsf(v[j].z))), fabsf(v[j].w));
     mx = warp_max(mx);
     float sc = __fdiv_rn(mx, 127.0f);
     if (sc == 0.0f) sc = 1.0f;
+    const float inv = __fdiv_rn(1.0f, sc);
     int8_t* qo = p.q + static_cast<size_t>(row) * D;
 #pragma unroll
-    for (int j = 0; j < kNormMaxV; ++j) {
-      const int i = 4 * lane + 128 * j;
-      if (j < nv && i < D) {
+    for (int j = 0; j < CAP; ++j)
+      if (live(j)) {
         char4 c;
-        c.x = quant_bridge(v[j].x, sc);
-        c.y = quant_bridge(v[j].y, sc);
-        c.z = quant_bridge(v[j].z, sc);
-        c.w = quant_bridge(v[j].w, sc);
-        *reinterpret_cast<char4*>(qo + i) = c;
+        c.x = quant_bridge_fast(v[j].x, sc, inv);
+        c.y = quant_bridge_fast(v[j].y, sc, inv);
+        c.z = quant_bridge_fast(v[j].z, sc, inv);
+        c.w = quant_bridge_fast(v[j].w, sc, inv);
+        *reinterpret_cast<char4*>(qo + 4 * lane + 128 * j) = c;
       }
-    }
     if (lane == 0) p.scale[row] = sc;
   }
 }

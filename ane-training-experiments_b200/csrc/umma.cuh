@@ -271,28 +271,36 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
           }
         }
       } else if constexpr (EPI == EPI_ARGMAX) {
+        if (p.logits) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int m = m0 + c0 + j;
-          unsigned long long key = 0ull;
-          if (n < p.N && m < p.M) {
-            key = argmax_key(v[j], n);
-            if (p.logits) p.logits[static_cast<size_t>(m) * p.ld_logits + n] = v[j];
+          for (int j = 0; j < 32; ++j) {
+            const int m = m0 + c0 + j;
+            if (n < p.N && m < p.M) p.logits[static_cast<size_t>(m) * p.ld_logits + n] = v[j];
           }
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) {
-            const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
-            key = other > key ? other : key;
-          }
-          if (lane == j) s_best[q][j] = key;
         }
+        // transpose the 32 channels x 32 tokens block so thread `lane` scans token lane's
+        // 32 channels in ascending order (first maximum wins), then combine the 4 warps
+        float* tb = s_tr[q];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) tb[j * 33 + lane] = v[j];
+        __syncwarp();
+        unsigned long long best = 0ull;
+        const int nbase = n0 + q * 32;
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          if (nbase + c < p.N) {
+            const unsigned long long k = argmax_key(tb[lane * 33 + c], nbase + c);
+            best = k > best ? k : best;
+          }
+        }
+        s_best[q][lane] = best;
         epi_bar();
         if (et < 32) {
-          unsigned long long best = s_best[0][et];
+          unsigned long long b = s_best[0][et];
 #pragma unroll
-          for (int w = 1; w < 4; ++w) best = s_best[w][et] > best ? s_best[w][et] : best;
+          for (int w = 1; w < 4; ++w) b = s_best[w][et] > b ? s_best[w][et] : b;
           const int m = m0 + c0 + et;
-          if (m < p.M) p.argmax_part[static_cast<size_t>(n_tile) * p.M + m] = best;
+          if (m < p.M) p.argmax_part[static_cast<size_t>(n_tile) * p.M + m] = b;
         }
         epi_bar();
       } else if constexpr (EPI == EPI_QKV) {

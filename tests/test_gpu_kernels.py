@@ -48,6 +48,34 @@ def test_quant_only_bit_exact():
     np.testing.assert_array_equal(q, qo)
 
 
+def test_quantiser_rounding_boundaries_bit_exact():
+    """Values within a few ulps of every k + 0.5 quotient for a non-power-of-two scale: the
+    device quantiser's reciprocal fast path must fall back to the IEEE quotient there."""
+    rows = []
+    for mx in (100.0, 3.7, 0.0123, 5000.0):
+        sc = np.float32(mx) / np.float32(127.0)
+        vals = []
+        for k in range(-128, 127):
+            c = np.float32((k + 0.5) * sc)
+            for d in range(-3, 4):
+                vals.append(np.float32(c) if d == 0 else np.nextafter(c, np.float32(np.inf if d > 0 else -np.inf), dtype=np.float32))
+                for _ in range(abs(d) - 1):
+                    vals[-1] = np.nextafter(vals[-1], np.float32(np.inf if d > 0 else -np.inf), dtype=np.float32)
+        vals = np.array(vals, np.float32)
+        vals = np.clip(vals, -mx, mx)
+        n = (len(vals) + 1 + 127) // 128 * 128
+        row = np.zeros(n, np.float32)
+        row[0] = mx
+        row[1:1 + len(vals)] = vals
+        rows.append(row)
+    width = max(len(r) for r in rows)
+    x = np.stack([np.pad(r, (0, width - len(r))) for r in rows]).astype(np.float32)
+    q, s = dev_norm_quant(x, None, 1e-5)
+    qo, so = O.quant_rows(x)
+    np.testing.assert_array_equal(s, so)
+    np.testing.assert_array_equal(q, qo)
+
+
 def dev_gemm_i8(A, B, splits):
     """splits < 0: the tcgen05 kernel; otherwise the warp-level kernel with that split."""
     M, K = A.shape
