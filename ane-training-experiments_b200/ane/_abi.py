@@ -45,8 +45,12 @@ EXPORTS = [
     "llm_generate_steps", "llm_generate_end", "llm_generate", "llm_stories_decode",
     "llm_stories_decode_batch", "llm_ctx_stream", "llm_synchronize", "llm_step_kernel_count",
     "llm_memory_bytes", "llm_time_attention", "llm_profile_step", "llm_debug_norm_quant", "llm_debug_gemm_i8",
-    "llm_debug_gemm_f16", "llm_debug_read_kv", "llm_gemm_i8_splitk_noalloc",
+    "llm_debug_gemm_f16", "llm_debug_read_kv", "llm_gemm_i8_splitk_noalloc", "llm_set_option",
 ]
+
+LLM_OPT_CUDA_GRAPHS = 1
+LLM_OPT_TCGEN05_GEMM = 2
+LLM_OPT_PDL = 3
 
 
 class LLMError(RuntimeError):
@@ -116,6 +120,7 @@ def lib() -> C.CDLL:
         "llm_debug_gemm_i8": (C.c_int, [C.c_int, C.POINTER(C.c_int8), C.POINTER(C.c_int8), C.c_int, C.c_int, C.c_int, C.c_int, i32p]),
         "llm_debug_gemm_f16": (C.c_int, [C.c_int, C.c_int, _FP, _FP, C.c_int, C.c_int, C.c_int, C.c_int, _FP]),
         "llm_debug_read_kv": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, _FP, _FP]),
+        "llm_set_option": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
         "llm_gemm_i8_splitk_noalloc": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                                                  C.c_void_p, C.c_void_p]),
     }

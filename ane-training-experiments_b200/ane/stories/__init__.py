@@ -363,6 +363,9 @@ class Engine:
         _abi.check(_abi.lib().llm_time_attention(self.h, iters, C.byref(us), C.byref(by)))
         return us.value, by.value
 
+    def set_option(self, option: int, value: int) -> None:
+        _abi.check(_abi.lib().llm_set_option(self.h, option, int(value)))
+
     def profile_step(self, iters: int = 3):
         """Per-kernel table of one eager decode step of the current generate batch."""
         buf = C.create_string_buffer(16384)

@@ -132,6 +132,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(AttnParams p) {
   __shared__ int s_rowlast[8];
   __shared__ float s_wmax[kAttnWarps];
 
+  griddep_launch_dependents();
+  griddep_wait();
   const int blk = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;

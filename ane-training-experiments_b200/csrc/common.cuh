@@ -18,8 +18,8 @@ enum DeviceError : int {
   kDevBadPage = 2,      // a block-table entry pointed outside the page pool
 };
 
-// Bound on mbarrier polls.  Each try_wait may itself suspend the thread for a
-// hardware-defined interval, so this is far longer than any legitimate wait.
+// Bound on mbarrier polls (each try_wait sleeps up to ~64 ns): about a second, far longer
+// than any legitimate wait.
 constexpr uint32_t kMaxWaitPolls = 1u << 24;
 
 // ----------------------------------------------------------------------------- types
@@ -109,13 +109,16 @@ __device__ __forceinline__ void fence_mbar_init() {
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
 }
-// Returns true once the phase with parity `parity` has completed.
+// Returns true once the phase with parity `parity` has completed.  The suspend-time hint
+// (nanoseconds) bounds how long a waiting thread sleeps before re-checking: without it the
+// system default applies, and a wait that spans a whole GEMM main loop was observed to round
+// kernel durations up to multiples of ~2 us.
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(64u)
       : "memory");
   return ok != 0;
 }
@@ -134,6 +137,17 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       "l"(src), "r"(bytes), "r"(bar)
       : "memory");
 }
+
+// ----------------------------------------------------------------------------- programmatic dependent launch
+// Kernels of the token loop are launched with programmatic stream serialisation: a kernel
+// may start while its predecessor drains.  Every kernel signals its dependents as soon as all
+// of its CTAs are resident (deadlock-free: the dependent grid starts only after every CTA of
+// this grid has executed the signal) and waits for its predecessor's completion and memory
+// before it reads anything the predecessor produced.  Outside such launches both are no-ops.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 
 // ----------------------------------------------------------------------------- misc
 __device__ __forceinline__ float warp_max(float v) {

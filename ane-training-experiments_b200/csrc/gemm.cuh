@@ -87,6 +87,8 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(GemmParams p) {
   static_assert(CHUNKS % kGemmThreads == 0, "tile chunks must divide the CTA");
 
   extern __shared__ __align__(1024) uint8_t smem[];
+  griddep_launch_dependents();
+  griddep_wait();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int wm = warp / WARPS_N, wn = warp % WARPS_N;
   const int m_tile = blockIdx.x, n_tile = blockIdx.y, split = blockIdx.z;

@@ -124,6 +124,8 @@ struct FinishParams {
 
 // Greedy token per row: max over the lm_head tiles' (value, first index) partials.
 __global__ void __launch_bounds__(256) finish_kernel(FinishParams f) {
+  griddep_launch_dependents();
+  griddep_wait();
   const int row = blockIdx.x * 8 + threadIdx.x / 32, lane = threadIdx.x & 31;
   if (row >= f.M) return;
   unsigned long long best = 0ull;
@@ -170,6 +172,23 @@ __global__ void f32_to_act_kernel(const float* src, T* dst, size_t n) {
 }
 
 // ---------------------------------------------------------------------------- launchers
+// Launch with programmatic stream serialisation (see griddep_* in common.cuh) unless the
+// calling context disabled it (llm_set_option LLM_OPT_PDL); the flag is per host thread.
+thread_local bool t_use_pdl = true;
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = t_use_pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
 template <typename InT, typename OutT, int BM, int EPI>
 cudaError_t gemm_launch_t(const GemmParams& p, dim3 grid, cudaStream_t s, bool prepare) {
   constexpr int BN = 128, ST = 4;
@@ -215,8 +234,7 @@ cudaError_t attn_launch_t(const AttnParams& p, cudaStream_t s, bool prepare) {
   if (prepare) return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   dim3 grid(p.n_blocks, p.n_kv_heads, p.splits);
   (void)cudaGetLastError();
-  k<<<grid, kAttnWarps * 32, smem, s>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(k, grid, dim3(kAttnWarps * 32), smem, s, p);
 }
 
 cudaError_t attn_any(int act, int hd, const AttnParams& p, cudaStream_t s, bool prepare) {
@@ -227,25 +245,15 @@ cudaError_t attn_any(int act, int hd, const AttnParams& p, cudaStream_t s, bool 
 
 template <typename T, bool Q>
 cudaError_t norm_launch(const NormParams& p, cudaStream_t s) {
-  dim3 grid((p.rows + 3) / 4);
   (void)cudaGetLastError();
-  switch (p.D / 128) {
-#define LLM_NORM_NV(n) \
-  case n:              \
-    if (p.D == 128 * n) { norm_rows_kernel<T, Q, n><<<grid, 128, 0, s>>>(p); return cudaGetLastError(); } \
-    break;
-    LLM_NORM_NV(1) LLM_NORM_NV(2) LLM_NORM_NV(4) LLM_NORM_NV(6) LLM_NORM_NV(8) LLM_NORM_NV(12) LLM_NORM_NV(16)
-    LLM_NORM_NV(24) LLM_NORM_NV(32)
-#undef LLM_NORM_NV
-    default:
-      break;
-  }
-  norm_rows_kernel<T, Q, 0><<<grid, 128, 0, s>>>(p);
-  return cudaGetLastError();
+  const dim3 block(norm_threads(p.D));
+  if (norm_groups_per_thread(p.D) == 2) return launch_pdl(norm_rows_kernel<T, Q, 2>, dim3(p.rows), block, 0, s, p);
+  return launch_pdl(norm_rows_kernel<T, Q, 1>, dim3(p.rows), block, 0, s, p);
 }
 
 cudaError_t norm_any(int act, bool quant, const NormParams& p, cudaStream_t s) {
-  if (p.D > 128 * kNormMaxV || p.D % 4) return cudaErrorInvalidValue;
+  if (p.D > kNormMaxD || p.D % (4 * norm_groups_per_thread(p.D)) || norm_threads(p.D) % 32 || p.rows <= 0)
+    return cudaErrorInvalidValue;
   if (act == 1) return quant ? norm_launch<__half, true>(p, s) : norm_launch<__half, false>(p, s);
   return quant ? norm_launch<__nv_bfloat16, true>(p, s) : norm_launch<__nv_bfloat16, false>(p, s);
 }
@@ -289,14 +297,31 @@ int make_kmajor_map(CUtensorMap* map, const void* ptr, int esz, bool bf16, int k
 template <typename InT, typename OutT, int BT, int EPI>
 cudaError_t umma_launch_t(const CUtensorMap& tw, const CUtensorMap& tx, const GemmParams& p, dim3 grid, cudaStream_t s,
                           bool prepare) {
-  constexpr int ST = BT >= 256 ? 4 : (BT >= 128 ? 6 : 8);  // ~192 KB of stages in every case
+  // BT <= 128: ~96 KB of stages so two CTAs share an SM (a decode GEMM's tiles then run in a
+  // single wave); BT = 256 (lm_head, prefill): four 48 KB stages, one CTA per SM
+  constexpr int ST = BT >= 256 ? 4 : (BT >= 128 ? 3 : 4);
   static_assert(umma_smem_bytes<BT, ST>() <= 200 * 1024, "stage ring exceeds the shared-memory budget");
   constexpr int smem = umma_smem_bytes<BT, ST>();
   auto k = umma_gemm_kernel<InT, OutT, BT, ST, EPI>;
   if (prepare) return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   (void)cudaGetLastError();  // launch errors below must be this launch's own
-  k<<<grid, kUmmaThreads, smem, s>>>(tw, tx, p);
-  return cudaGetLastError();
+  if (p.k_splits <= 1) return launch_pdl(k, grid, dim3(kUmmaThreads), smem, s, tw, tx, p);
+  // split-K: the splits of a tile form one cluster along z (see umma.cuh)
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kUmmaThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = p.k_splits;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = t_use_pdl ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, k, tw, tx, p);
 }
 
 template <typename InT, typename OutT>
@@ -451,6 +476,12 @@ struct llm_ctx {
   std::map<GraphKey, cudaGraphExec_t> graphs;
   bool use_graphs = true;
   bool use_umma = true;  // tcgen05 GEMMs (false: the warp-level mma.sync GEMMs)
+  // programmatic dependent launch between the step's kernels: off by default, it measured
+  // 2% slower on the Qwen3 W8A8 decode step (9.47 vs 9.28 ms at 256 sequences)
+  bool use_pdl = false;
+  // cluster split-K of the residual projections: correct, but its DSMEM reduction measured
+  // ~5x slower than the unsplit kernel (27.7 vs 4.0 us for Wo), so it is off by default
+  bool umma_cluster_splitk = false;
   std::map<std::tuple<const void*, int, int, int, int>, CUtensorMap> tmaps;
 
   // llm_profile_step: when non-null, enqueue_forward records an event after each launch
@@ -531,8 +562,8 @@ extern "C" int llm_ctx_create(const llm_model_config* cfg, int dtype, int device
   const int q_dim = k.n_heads * k.head_dim, kv_dim = k.n_kv_heads * k.head_dim;
   if (k.dim % 128 || k.hidden % 128 || q_dim % 128 || kv_dim % 128)
     return fail(LLM_ERR_UNSUPPORTED, "dim, hidden, heads*head_dim and kv_heads*head_dim must be multiples of 128");
-  if (k.dim > 128 * kNormMaxV || k.hidden > 128 * kNormMaxV || q_dim > 128 * kNormMaxV)
-    return fail(LLM_ERR_UNSUPPORTED, "rows wider than %d elements are not supported", 128 * kNormMaxV);
+  if (k.dim > kNormMaxD || k.hidden > kNormMaxD || q_dim > kNormMaxD)
+    return fail(LLM_ERR_UNSUPPORTED, "rows wider than %d elements are not supported", kNormMaxD);
   if (!(k.norm_eps > 0)) return fail(LLM_ERR_INVALID, "norm_eps must be positive");
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
@@ -898,10 +929,18 @@ int gemm(llm_ctx* c, bool in8, int epi, GemmParams p) {
     const CUtensorMap* tw = tmap(c, p.B, esz, p.K, p.N, 128);
     const CUtensorMap* tx = tmap(c, p.A, esz, p.K, p.M, bt);
     if (!tw || !tx) return LLM_ERR_CUDA;
-    p.k_splits = 1;
-    p.k_tiles_per_split = p.K * esz / 128;
+    const int k_tiles = p.K * esz / 128;
+    const int tiles = ((p.N + 127) / 128) * ((p.M + bt - 1) / bt);
+    // residual projections with few output tiles split K over a cluster of 2 or 4 CTAs
+    int splits = 1;
+    if (epi == EPI_RESID && c->umma_cluster_splitk)
+      while (splits < 4 && tiles * splits * 3 < 2 * c->n_sm && k_tiles % (2 * splits) == 0 &&
+             k_tiles / (2 * splits) >= 2 && bt % (2 * splits) == 0)
+        splits *= 2;
+    p.k_splits = splits;
+    p.k_tiles_per_split = k_tiles / splits;
     p.err = c->d_err;
-    dim3 grid((p.N + 127) / 128, (p.M + bt - 1) / bt, 1);
+    dim3 grid((p.N + 127) / 128, (p.M + bt - 1) / bt, splits);
     CU(umma_any(c->act, in8, *tw, *tx, p, epi, bt, grid, c->stream, false));
     return LLM_OK;
   }
@@ -916,6 +955,7 @@ int gemm(llm_ctx* c, bool in8, int epi, GemmParams p) {
 }
 
 int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
+  t_use_pdl = c->use_pdl;
   const llm_model_config& k = c->cfg;
   const int R = rs.R, D = k.dim, F = k.hidden, Q = c->q_dim, KV = c->kv_dim;
   const bool i8 = c->in8;
@@ -1107,8 +1147,7 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
     f.gen_start = rs.gen_start;
     f.gen_out = rs.gen_out;
     f.gen_cap = rs.gen_cap;
-    finish_kernel<<<(NF + 7) / 8, 256, 0, s>>>(f);
-    CU(cudaGetLastError());
+    CU(launch_pdl(finish_kernel, dim3((NF + 7) / 8), dim3(256), 0, s, f));
     RC(mark("finish"));
   }
   return LLM_OK;
@@ -1477,6 +1516,26 @@ extern "C" int llm_stories_decode(llm_ctx* c, int seq, const int32_t* prompt, in
   static const int32_t empty = 0;
   return llm_stories_decode_batch(c, prompt ? prompt : &empty, &lens, 1, max_new, temperature, out_tokens, n_tokens,
                                   prompt_len, stopped_on_eos);
+}
+
+// ============================================================================ options
+extern "C" int llm_set_option(llm_ctx* c, int option, int value) {
+  if (!c) return fail(LLM_ERR_INVALID, "nil context");
+  bool* flag = nullptr;
+  switch (option) {
+    case LLM_OPT_CUDA_GRAPHS: flag = &c->use_graphs; break;
+    case LLM_OPT_TCGEN05_GEMM: flag = &c->use_umma; break;
+    case LLM_OPT_PDL: flag = &c->use_pdl; break;
+    default: return fail(LLM_ERR_INVALID, "unknown option %d", option);
+  }
+  if (*flag != (value != 0)) {
+    RC(set_device(c));
+    CU(cudaStreamSynchronize(c->stream));
+    for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
+    c->graphs.clear();
+    *flag = value != 0;
+  }
+  return LLM_OK;
 }
 
 // ============================================================================ introspection

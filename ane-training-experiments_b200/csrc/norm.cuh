@@ -1,10 +1,8 @@
 // norm.cuh -- row kernels: embedding gather, RMSNorm, per-token int8 quantisation.
 //
-// One warp per row (4 rows per 128-thread block).  Lane l owns the float4 groups starting
-// at 4*l + 128*j, so every access is a coalesced 512-byte warp transaction.  The float64 sum of squares is taken
-// in that fixed order (lane partials j-major / component-minor, then an xor butterfly),
-// with explicit round-to-nearest intrinsics so no fused multiply-add can change it; the
-// CPU oracle restates exactly this order for its bit-exact quantiser check.
+// One CTA per row (see norm_rows_kernel for the thread layout and the fixed float64
+// summation order); explicit round-to-nearest intrinsics keep fused multiply-adds out, and
+// the CPU oracle restates the same order for its bit-exact quantiser check.
 //
 // Reference arithmetic: ane/stories/infer.go:301-311 (rmsNormVec: float64 sum, f32 rrms,
 // x*rrms*w), bridge/ane_bridge.m:374-398 (quantiser, applied per row).
@@ -37,96 +35,113 @@ __device__ __forceinline__ float4 load4_act(const T* p) {
                      ActTraits<T>::to_f(h[3]));
 }
 
-// Rows are held in registers: lane l keeps float4 groups j = 0..NV-1 (element 4*l + 128*j),
-// so a row of 128*NV elements is read from global memory exactly once.  NV is a template
-// parameter so the code is exactly as long as the row needs (a generic NV = 0 variant loops
-// over any multiple of 4 up to 128*kNormMaxV).
-constexpr int kNormMaxV = 32;  // rows up to 4096 elements
+// One CTA per row: thread t of the row's nt = D/(4*NV) threads holds the float4 groups
+// starting at elements 4*t + 4*nt*j (j = 0..NV-1), so loads are coalesced and every thread's
+// dependent chain is NV groups long.  The float64 sum of squares is taken in a fixed order:
+// each thread j-major / component-minor, an xor butterfly inside each warp, then thread 0
+// adds the warp totals in warp order.  oracle_norm_quant_rows restates exactly this order.
+constexpr int kNormMaxD = 8192;
+
+__host__ __device__ constexpr int norm_groups_per_thread(int D) { return D >= 512 ? 2 : 1; }
+__host__ __device__ constexpr int norm_threads(int D) { return D / (4 * norm_groups_per_thread(D)); }
 
 template <typename T, bool QUANT, int NV>
-__global__ void __launch_bounds__(128) norm_rows_kernel(NormParams p) {
-  constexpr int CAP = NV > 0 ? NV : kNormMaxV;
-  const int warps = blockDim.x / 32;
-  const int row = blockIdx.x * warps + threadIdx.x / 32;
-  const int lane = threadIdx.x & 31;
-  if (row >= p.rows) return;
+__global__ void __launch_bounds__(1024) norm_rows_kernel(NormParams p) {
+  griddep_launch_dependents();
+  griddep_wait();
+  __shared__ double s_ss[32];
+  __shared__ float s_mx[32];
+  __shared__ float s_bc[2];
+  const int row = blockIdx.x;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int nt = blockDim.x, nwarps = (nt + 31) >> 5;
   const int D = p.D;
-  const int nv = NV > 0 ? NV : (D + 127) / 128;
-  auto live = [&](int j) { return NV > 0 ? true : (j < nv && 4 * lane + 128 * j < D); };
 
-  float4 v[CAP];
+  float4 v[NV];
   if (p.embed != nullptr) {
     const T* e = reinterpret_cast<const T*>(p.embed) + static_cast<size_t>(p.tokens[row]) * D;
     float* xo = p.x_out + static_cast<size_t>(row) * D;
 #pragma unroll
-    for (int j = 0; j < CAP; ++j)
-      if (live(j)) {
-        v[j] = load4_act<T>(e + 4 * lane + 128 * j);
-        *reinterpret_cast<float4*>(xo + 4 * lane + 128 * j) = v[j];
-      }
+    for (int j = 0; j < NV; ++j) {
+      v[j] = load4_act<T>(e + 4 * t + 4 * nt * j);
+      *reinterpret_cast<float4*>(xo + 4 * t + 4 * nt * j) = v[j];
+    }
   } else {
     const int src = p.row_index ? p.row_index[row] : row;
     const float* xr = p.x + static_cast<size_t>(src) * D;
 #pragma unroll
-    for (int j = 0; j < CAP; ++j)
-      if (live(j)) v[j] = *reinterpret_cast<const float4*>(xr + 4 * lane + 128 * j);
+    for (int j = 0; j < NV; ++j) v[j] = *reinterpret_cast<const float4*>(xr + 4 * t + 4 * nt * j);
   }
 
   if (p.w != nullptr) {
     double acc = 0.0;
 #pragma unroll
-    for (int j = 0; j < CAP; ++j)
-      if (live(j)) {
-        acc = __dadd_rn(acc, __dmul_rn((double)v[j].x, (double)v[j].x));
-        acc = __dadd_rn(acc, __dmul_rn((double)v[j].y, (double)v[j].y));
-        acc = __dadd_rn(acc, __dmul_rn((double)v[j].z, (double)v[j].z));
-        acc = __dadd_rn(acc, __dmul_rn((double)v[j].w, (double)v[j].w));
-      }
-    const double tot = warp_sum_f64(acc);
-    const double mean = __dadd_rn(__ddiv_rn(tot, (double)D), p.eps);
-    const float rrms = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(mean)));
+    for (int j = 0; j < NV; ++j) {
+      acc = __dadd_rn(acc, __dmul_rn((double)v[j].x, (double)v[j].x));
+      acc = __dadd_rn(acc, __dmul_rn((double)v[j].y, (double)v[j].y));
+      acc = __dadd_rn(acc, __dmul_rn((double)v[j].z, (double)v[j].z));
+      acc = __dadd_rn(acc, __dmul_rn((double)v[j].w, (double)v[j].w));
+    }
+    // threads of a partial last warp contribute 0.0 to the butterfly
+    acc = warp_sum_f64(acc);
+    if (lane == 0) s_ss[warp] = acc;
+    __syncthreads();
+    if (t == 0) {
+      double tot = s_ss[0];
+      for (int w = 1; w < nwarps; ++w) tot = __dadd_rn(tot, s_ss[w]);
+      const double mean = __dadd_rn(__ddiv_rn(tot, (double)D), p.eps);
+      s_bc[0] = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(mean)));
+    }
+    __syncthreads();
+    const float rrms = s_bc[0];
 #pragma unroll
-    for (int j = 0; j < CAP; ++j)
-      if (live(j)) {
-        const float4 w = *reinterpret_cast<const float4*>(p.w + 4 * lane + 128 * j);
-        v[j].x = __fmul_rn(__fmul_rn(v[j].x, rrms), w.x);
-        v[j].y = __fmul_rn(__fmul_rn(v[j].y, rrms), w.y);
-        v[j].z = __fmul_rn(__fmul_rn(v[j].z, rrms), w.z);
-        v[j].w = __fmul_rn(__fmul_rn(v[j].w, rrms), w.w);
-      }
+    for (int j = 0; j < NV; ++j) {
+      const float4 w = *reinterpret_cast<const float4*>(p.w + 4 * t + 4 * nt * j);
+      v[j].x = __fmul_rn(__fmul_rn(v[j].x, rrms), w.x);
+      v[j].y = __fmul_rn(__fmul_rn(v[j].y, rrms), w.y);
+      v[j].z = __fmul_rn(__fmul_rn(v[j].z, rrms), w.z);
+      v[j].w = __fmul_rn(__fmul_rn(v[j].w, rrms), w.w);
+    }
   }
 
   if constexpr (!QUANT) {
     T* o = reinterpret_cast<T*>(p.out) + static_cast<size_t>(row) * D;
 #pragma unroll
-    for (int j = 0; j < CAP; ++j)
-      if (live(j)) {
-        uint2 packed;
-        packed.x = ActTraits<T>::pack2(v[j].x, v[j].y);
-        packed.y = ActTraits<T>::pack2(v[j].z, v[j].w);
-        *reinterpret_cast<uint2*>(o + 4 * lane + 128 * j) = packed;
-      }
+    for (int j = 0; j < NV; ++j) {
+      uint2 packed;
+      packed.x = ActTraits<T>::pack2(v[j].x, v[j].y);
+      packed.y = ActTraits<T>::pack2(v[j].z, v[j].w);
+      *reinterpret_cast<uint2*>(o + 4 * t + 4 * nt * j) = packed;
+    }
   } else {
     float mx = 0.0f;
 #pragma unroll
-    for (int j = 0; j < CAP; ++j)
-      if (live(j)) mx = fmaxf(fmaxf(fmaxf(mx, fabsf(v[j].x)), fmaxf(fabsf(v[j].y), fabsf(v[j].z))), fabsf(v[j].w));
+    for (int j = 0; j < NV; ++j)
+      mx = fmaxf(fmaxf(fmaxf(mx, fabsf(v[j].x)), fmaxf(fabsf(v[j].y), fabsf(v[j].z))), fabsf(v[j].w));
     mx = warp_max(mx);
-    float sc = __fdiv_rn(mx, 127.0f);
-    if (sc == 0.0f) sc = 1.0f;
+    if (lane == 0) s_mx[warp] = mx;
+    __syncthreads();
+    if (t == 0) {
+      float m = s_mx[0];
+      for (int w = 1; w < nwarps; ++w) m = fmaxf(m, s_mx[w]);
+      float sc = __fdiv_rn(m, 127.0f);
+      if (sc == 0.0f) sc = 1.0f;
+      s_bc[1] = sc;
+      p.scale[row] = sc;
+    }
+    __syncthreads();
+    const float sc = s_bc[1];
     const float inv = __fdiv_rn(1.0f, sc);
     int8_t* qo = p.q + static_cast<size_t>(row) * D;
 #pragma unroll
-    for (int j = 0; j < CAP; ++j)
-      if (live(j)) {
-        char4 c;
-        c.x = quant_bridge_fast(v[j].x, sc, inv);
-        c.y = quant_bridge_fast(v[j].y, sc, inv);
-        c.z = quant_bridge_fast(v[j].z, sc, inv);
-        c.w = quant_bridge_fast(v[j].w, sc, inv);
-        *reinterpret_cast<char4*>(qo + 4 * lane + 128 * j) = c;
-      }
-    if (lane == 0) p.scale[row] = sc;
+    for (int j = 0; j < NV; ++j) {
+      char4 c;
+      c.x = quant_bridge_fast(v[j].x, sc, inv);
+      c.y = quant_bridge_fast(v[j].y, sc, inv);
+      c.z = quant_bridge_fast(v[j].z, sc, inv);
+      c.w = quant_bridge_fast(v[j].w, sc, inv);
+      *reinterpret_cast<char4*>(qo + 4 * t + 4 * nt * j) = c;
+    }
   }
 }
 

@@ -15,6 +15,12 @@
 // releases a stage when its MMAs have consumed it and signals the epilogue after the last.
 // Every mbarrier wait is bounded: on expiry the kernel records kDevWaitTimeout, skips the
 // remaining work and still reaches the TMEM deallocation.
+//
+// Split-K (residual epilogue only, p.k_splits > 1): the splits of one output tile are one
+// thread-block cluster along z.  Each CTA parks its partial accumulator tile in its own (now
+// idle) stage memory; after a cluster barrier CTA rank r sums token slice r of all ranks'
+// partials through distributed shared memory, in rank order, and runs the epilogue on it; a
+// second cluster barrier keeps every CTA's shared memory alive until its peers are done.
 #pragma once
 #include <cuda.h>
 
@@ -71,6 +77,29 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;\n" ::: "memory"); }
+// Thread-block cluster barrier (every thread of every CTA of the cluster arrives), with
+// release/acquire ordering of shared-memory writes across the cluster.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+  return r;
+}
+// 32-bit load from CTA `rank`'s shared memory at the address this CTA uses for `saddr`.
+// Not volatile: the loads only follow the cluster barrier (which orders them), so the
+// compiler may batch them.
+__device__ __forceinline__ uint32_t dsmem_addr(uint32_t saddr, uint32_t rank) {
+  uint32_t remote;
+  asm("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(remote) : "r"(saddr), "r"(rank));
+  return remote;
+}
+__device__ __forceinline__ uint32_t ld_dsmem(uint32_t remote) {
+  uint32_t v;
+  asm("ld.shared::cluster.u32 %0, [%1];\n" : "=r"(v) : "r"(remote));
+  return v;
+}
 
 // Shared-memory matrix descriptor for a K-major operand tile whose rows are 128 bytes,
 // written by TMA with 128-byte swizzle: 8-row core groups 1024 bytes apart (SBO), layout
@@ -120,7 +149,6 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   __shared__ uint32_t s_tmem;
   __shared__ int s_pos[BT], s_page[BT];
   __shared__ double s_ss[4][32];
-  __shared__ float s_tr[4][32 * 33];
   __shared__ unsigned long long s_best[4][32];
 
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
@@ -132,6 +160,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   const int kt_end = min(k_tiles, kt_begin + p.k_tiles_per_split);
   const int nkt = max(0, kt_end - kt_begin);
 
+  griddep_launch_dependents();
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(smem_u32(&full_bar[s]), 1);
@@ -153,7 +182,21 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
-      for (int i = 0; i < nkt; ++i) {
+      asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
+      asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
+      // The weights do not depend on the preceding kernel: stream the first stages' weight
+      // tiles while it drains, then wait for it before touching the activations.
+      const int pre = min(nkt, STAGES);
+      for (int i = 0; i < pre; ++i) {
+        const uint32_t st = sbase + i * STAGE_BYTES;
+        mbar_arrive_expect_tx(smem_u32(&full_bar[i]), STAGE_BYTES);
+        tma_load_2d(st, &tmW, (kt_begin + i) * (128 / ESZ), n0, smem_u32(&full_bar[i]));
+      }
+      griddep_wait();
+      for (int i = 0; i < pre; ++i)
+        tma_load_2d(sbase + i * STAGE_BYTES + A_BYTES, &tmX, (kt_begin + i) * (128 / ESZ), m0,
+                    smem_u32(&full_bar[i]));
+      for (int i = pre; i < nkt; ++i) {
         const int s = i % STAGES;
         const uint32_t par = ((i / STAGES) & 1) ^ 1;
         if (!mbar_wait_bounded(smem_u32(&empty_bar[s]), par)) {
@@ -193,6 +236,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     const int et = threadIdx.x - 64;        // 0..127 among epilogue threads
     const int nl = q * 32 + lane;           // channel within the tile
     const int n = n0 + nl;
+    griddep_wait();  // positions, scales and the residual come from earlier kernels
     if constexpr (EPI == EPI_QKV) {
       for (int j = et; j < BT; j += 128) {
         const int m = m0 + j;
@@ -206,12 +250,27 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       }
     }
     const float sw = (I8 && n < p.N) ? p.b_scale[n] : 1.0f;
+    // 32 x 33 transpose buffers of the epilogue warps live in the stage ring, which is idle
+    // once the accumulator is complete (every TMA write and MMA read has finished)
+    float(*s_tr)[32 * 33] = reinterpret_cast<float(*)[32 * 33]>(smem_raw + (sbase - smem_u32(smem_raw)));
     bool ok = nkt > 0 && mbar_wait_bounded(smem_u32(&accum_bar), 0);
     if (!ok && nkt > 0) failed = true;
     tc_fence_after();
     if constexpr (EPI == EPI_QKV) epi_bar();  // s_pos / s_page visible to all epilogue warps
     const int mcount = min(BT, p.M - m0);
-    for (int c0 = 0; c0 < BT; c0 += 32) {
+    const bool split = EPI == EPI_RESID && p.k_splits > 1;
+    if (split) {
+      // stage this split's partial tile [128 channels][BT tokens] (+1 column of padding)
+      uint32_t* part = reinterpret_cast<uint32_t*>(smem_raw + (sbase - smem_u32(smem_raw)));
+      for (int c0 = 0; c0 < BT; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) part[nl * (BT + 1) + c0 + j] = ok ? r[j] : 0u;
+      }
+    }
+    for (int c0 = 0; c0 < BT && !split; c0 += 32) {
       if (c0 >= mcount) break;  // uniform across the epilogue warps
       uint32_t r[32];
       tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, r);
@@ -385,6 +444,57 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         }
         __syncwarp();
       }
+    }
+  }
+  if constexpr (EPI == EPI_RESID) {
+    if (p.k_splits > 1) {
+      __syncwarp();
+      cluster_sync_all();  // every split's partial tile is in its shared memory
+      if (warp >= 2) {
+        const int q = warp & 3, nl = q * 32 + lane, n = n0 + nl;
+        const float sw = (I8 && n < p.N) ? p.b_scale[n] : 1.0f;
+        const uint32_t rank = cluster_rank();
+        const int S = p.k_splits;
+        const int per = BT / S;
+        uint32_t base[4];  // the partial tile of every rank (same offset in each CTA)
+#pragma unroll
+        for (int sr = 0; sr < 4; ++sr) base[sr] = sr < S ? dsmem_addr(sbase, sr) : 0u;
+        // token slice in batches of 8: issue the batch's remote loads of every rank, then sum
+        for (int jb = 0; jb < per; jb += 8) {
+          uint32_t raw[4][8];
+#pragma unroll
+          for (int sr = 0; sr < 4; ++sr)
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj)
+              if (sr < S && jb + jj < per)
+                raw[sr][jj] =
+                    ld_dsmem(base[sr] + 4u * static_cast<uint32_t>(nl * (BT + 1) + static_cast<int>(rank) * per + jb + jj));
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            const int j = static_cast<int>(rank) * per + jb + jj;
+            const int m = m0 + j;
+            if (jb + jj >= per || m >= p.M || n >= p.N) continue;
+            float v;
+            if constexpr (I8) {
+              int acc = 0;
+#pragma unroll
+              for (int sr = 0; sr < 4; ++sr)
+                if (sr < S) acc += static_cast<int>(raw[sr][jj]);
+              v = __fmul_rn(__fmul_rn(__int2float_rn(acc), p.a_scale[m]), sw);
+            } else {
+              float acc = 0.f;
+#pragma unroll
+              for (int sr = 0; sr < 4; ++sr)
+                if (sr < S) acc = __fadd_rn(acc, __uint_as_float(raw[sr][jj]));
+              v = acc;
+            }
+            const size_t idx = static_cast<size_t>(m) * p.ldo + n;
+            reinterpret_cast<float*>(p.out)[idx] = __fadd_rn(v, p.resid[idx]);
+          }
+        }
+      }
+      __syncwarp();
+      cluster_sync_all();  // peers may still be reading this CTA's partial tile
     }
   }
   if (failed && p.err) atomicExch(p.err, kDevWaitTimeout);

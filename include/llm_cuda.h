@@ -159,6 +159,15 @@ int llm_stories_decode_batch(llm_ctx *ctx, const int32_t *prompts, const int32_t
                              int max_new, float temperature, int32_t *out_tokens, int32_t *n_tokens,
                              int32_t *prompt_len, int32_t *stopped_on_eos);
 
+/* ---------------------------------------------------------------- execution options */
+#define LLM_OPT_CUDA_GRAPHS 1  /* replay each decode step as a captured CUDA graph (default 1)   */
+#define LLM_OPT_TCGEN05_GEMM 2 /* tcgen05 projections (default 1); 0 = warp-level mma.sync ones   */
+#define LLM_OPT_PDL 3          /* programmatic dependent launch between step kernels (default 0) */
+/* Set an execution option (value 0/1).  Results do not depend on the options beyond fp32
+ * summation order; cached graphs are dropped when an option changes.  No counterpart in the
+ * reference (its ANE runtime has no such switches). */
+int llm_set_option(llm_ctx *ctx, int option, int value);
+
 /* ---------------------------------------------------------------- introspection / timing */
 /* The context's CUDA stream (cudaStream_t) so callers can record events on it. */
 int llm_ctx_stream(llm_ctx *ctx, void **stream);

@@ -154,30 +154,38 @@ void oracle_quant_rows(const float *x, int rows, int cols, int8_t *q, float *sca
   for (int r = 0; r < rows; r++) scales[r] = quant_row(x + (size_t)r * cols, cols, q + (size_t)r * cols);
 }
 
-/* Sum of squares in the CUDA row kernel's order: lane l (0..31) owns the float4 groups
- * starting at 4*l + 128*j; it accumulates x*x in float64 (no fused multiply-add) in j-major,
- * component-minor order; the 32 partials are combined by an xor butterfly (16,8,4,2,1). */
+/* Sum of squares in the CUDA row kernel's order: the row is handled by T = n / (4*G)
+ * threads (G = 2 float4 groups per thread when n >= 512, else 1); thread t owns the groups
+ * starting at 4*t + 4*T*j (j = 0..G-1) and accumulates x*x in float64 (no fused
+ * multiply-add) j-major, component-minor; each 32-thread warp combines its partials by an
+ * xor butterfly (16, 8, 4, 2, 1); the warp totals are added in warp order. */
 static double sumsq_lane_order(const float *x, int n) {
-  double p[32];
-  for (int l = 0; l < 32; l++) {
-    double acc = 0.0;
-    for (int j = 0; 128 * j < n; j++)
-      for (int c = 0; c < 4; c++) {
-        int e = 128 * j + 4 * l + c;
-        if (e < n) {
-          double v = (double)x[e];
-          double sq = v * v;
-          acc = acc + sq;
-        }
-      }
-    p[l] = acc;
+  int G = n >= 512 ? 2 : 1;
+  int T = n / (4 * G);
+  int W = (T + 31) / 32;
+  double total = 0.0;
+  for (int w = 0; w < W; w++) {
+    double p[32];
+    for (int l = 0; l < 32; l++) {
+      int t = 32 * w + l;
+      double acc = 0.0;
+      if (t < T)
+        for (int j = 0; j < G; j++)
+          for (int c = 0; c < 4; c++) {
+            double v = (double)x[4 * t + 4 * T * j + c];
+            double sq = v * v;
+            acc = acc + sq;
+          }
+      p[l] = acc;
+    }
+    for (int k = 16; k >= 1; k >>= 1) {
+      double tt[32];
+      for (int l = 0; l < 32; l++) tt[l] = p[l] + p[l ^ k];
+      memcpy(p, tt, sizeof p);
+    }
+    total = w == 0 ? p[0] : total + p[0];
   }
-  for (int k = 16; k >= 1; k >>= 1) {
-    double t[32];
-    for (int l = 0; l < 32; l++) t[l] = p[l] + p[l ^ k];
-    memcpy(p, t, sizeof p);
-  }
-  return p[0];
+  return total;
 }
 
 static float rrms_from_sumsq(double sum, int n, double eps) {

@@ -117,7 +117,8 @@ float oracle_round_bf16(float x);
 /* Bridge quantiser applied per row (rows x cols); scales[rows]. */
 void oracle_quant_rows(const float *x, int rows, int cols, int8_t *q, float *scales);
 /* RMSNorm then per-row quantisation, with the float64 sum of squares taken in the order
- * the CUDA row kernel documents (32 lane partials over float4 groups, xor butterfly). */
+ * the CUDA row kernel documents (per-thread float4 groups, per-warp xor butterfly, warp
+ * totals in order; see sumsq_lane_order in oracle.c). */
 void oracle_norm_quant_rows_lane_order(const float *x, const float *w, int rows, int cols,
                                        double eps, int8_t *q, float *scales);
 /* Same lane-ordered RMSNorm without quantisation, output rounded per mode (F16/BF16/none). */

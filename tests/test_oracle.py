@@ -199,22 +199,29 @@ def test_quantiser_random_rows_match_numpy_restatement():
 
 def test_norm_quant_lane_order_matches_numpy():
     rng = np.random.default_rng(5)
-    for cols in (128, 768, 1024, 3072):
+    for cols in (128, 256, 768, 1024, 3072):
         x = rng.standard_normal((3, cols)).astype(np.float32)
         w = (1 + 0.2 * rng.standard_normal(cols)).astype(np.float32)
         q, s = O.norm_quant_rows(x, w, 1e-5)
+        G = 2 if cols >= 512 else 1
+        T = cols // (4 * G)
         for r in range(3):
-            parts = np.zeros(32)
-            for l in range(32):
-                acc = 0.0
-                for j in range(0, cols, 128):
-                    for c in range(4):
-                        e = j + 4 * l + c
-                        acc = acc + float(x[r, e]) * float(x[r, e])
-                parts[l] = acc
-            for k in (16, 8, 4, 2, 1):
-                parts = np.array([parts[i] + parts[i ^ k] for i in range(32)])
-            rr = f32(1.0 / math.sqrt(parts[0] / cols + 1e-5))
+            total = None
+            for wp in range((T + 31) // 32):
+                parts = np.zeros(32)
+                for l in range(32):
+                    t = 32 * wp + l
+                    acc = 0.0
+                    if t < T:
+                        for j in range(G):
+                            for c in range(4):
+                                e = 4 * t + 4 * T * j + c
+                                acc = acc + float(x[r, e]) * float(x[r, e])
+                    parts[l] = acc
+                for k in (16, 8, 4, 2, 1):
+                    parts = np.array([parts[i] + parts[i ^ k] for i in range(32)])
+                total = parts[0] if total is None else total + parts[0]
+            rr = f32(1.0 / math.sqrt(total / cols + 1e-5))
             y = ((x[r] * rr).astype(np.float32) * w).astype(np.float32)
             qq, ss = O.quant_rows(y[None, :])
             np.testing.assert_array_equal(q[r], qq[0])
