@@ -57,7 +57,8 @@ struct GemmParams {
   int layer, n_pages, max_pages_per_seq, n_heads, n_kv_heads, head_dim, qk_norm;
   double eps;
   // EPI_ARGMAX
-  unsigned long long* argmax_part;  // [N tiles][M]
+  unsigned long long* argmax_part;  // [M][argmax_parts]: one (value, index) key per channel tile
+  int argmax_parts;
   float* logits;                    // optional [M][ld_logits]
   int ld_logits;
   int* err;
@@ -341,7 +342,7 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(GemmParams p) {
       unsigned long long best = s_best[0][r];
 #pragma unroll
       for (int w = 1; w < WARPS_N; ++w) best = s_best[w][r] > best ? s_best[w][r] : best;
-      if (m0 + r < p.M) p.argmax_part[static_cast<size_t>(n_tile) * p.M + m0 + r] = best;
+      if (m0 + r < p.M) p.argmax_part[static_cast<size_t>(m0 + r) * p.argmax_parts + n_tile] = best;
     }
   } else if constexpr (EPI == EPI_QKV) {
     // Stage the dequantised tile in shared memory, then process whole heads per row.

@@ -112,7 +112,7 @@ extern "C" void llm_synth_normal(float* dst, uint64_t n, uint64_t seed, uint64_t
 namespace {
 
 struct FinishParams {
-  const unsigned long long* part;  // [n_tiles][M]
+  const unsigned long long* part;  // [M][n_tiles]
   int M, n_tiles;
   int* next;                       // [M]
   int* tok_io;                     // optional: tokens <- next
@@ -129,8 +129,10 @@ __global__ void __launch_bounds__(256) finish_kernel(FinishParams f) {
   const int row = blockIdx.x * 8 + threadIdx.x / 32, lane = threadIdx.x & 31;
   if (row >= f.M) return;
   unsigned long long best = 0ull;
+  const unsigned long long* pr = f.part + static_cast<size_t>(row) * f.n_tiles;
+#pragma unroll 4
   for (int t = lane; t < f.n_tiles; t += 32) {
-    const unsigned long long k = f.part[static_cast<size_t>(t) * f.M + row];
+    const unsigned long long k = pr[t];
     best = k > best ? k : best;
   }
 #pragma unroll
@@ -294,74 +296,84 @@ int make_kmajor_map(CUtensorMap* map, const void* ptr, int esz, bool bf16, int k
   return LLM_OK;
 }
 
-template <typename InT, typename OutT, int BT, int EPI>
-cudaError_t umma_launch_t(const CUtensorMap& tw, const CUtensorMap& tx, const GemmParams& p, dim3 grid, cudaStream_t s,
+template <typename InT, typename OutT, int BN, int EPI>
+cudaError_t umma_launch_t(const CUtensorMap& tx, const CUtensorMap& tw, const GemmParams& p, dim3 grid, cudaStream_t s,
                           bool prepare) {
-  // BT <= 128: ~96 KB of stages so two CTAs share an SM (a decode GEMM's tiles then run in a
-  // single wave); BT = 256 (lm_head, prefill): four 48 KB stages, one CTA per SM
-  constexpr int ST = BT >= 256 ? 4 : (BT >= 128 ? 3 : 4);
-  static_assert(umma_smem_bytes<BT, ST>() <= 200 * 1024, "stage ring exceeds the shared-memory budget");
-  constexpr int smem = umma_smem_bytes<BT, ST>();
-  auto k = umma_gemm_kernel<InT, OutT, BT, ST, EPI>;
+  constexpr int smem = umma_smem_bytes<BN>();
+  static_assert(smem <= 200 * 1024, "stage ring exceeds the shared-memory budget");
+  auto k = umma_gemm_kernel<InT, OutT, BN, EPI>;
   if (prepare) return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   (void)cudaGetLastError();  // launch errors below must be this launch's own
-  if (p.k_splits <= 1) return launch_pdl(k, grid, dim3(kUmmaThreads), smem, s, tw, tx, p);
-  // split-K: the splits of a tile form one cluster along z (see umma.cuh)
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(kUmmaThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = p.k_splits;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = t_use_pdl ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, k, tw, tx, p);
+  return launch_pdl(k, grid, dim3(kUmmaThreads), smem, s, tx, tw, p);
 }
 
-template <typename InT, typename OutT>
-cudaError_t umma_dispatch(const CUtensorMap& tw, const CUtensorMap& tx, const GemmParams& p, int epi, int bt, dim3 grid,
-                          cudaStream_t s, bool prepare) {
-#define LLM_UMMA_CASE(E)                                                                       \
-  case E:                                                                                      \
-    return bt == 64    ? umma_launch_t<InT, OutT, 64, E>(tw, tx, p, grid, s, prepare)         \
-           : bt == 128 ? umma_launch_t<InT, OutT, 128, E>(tw, tx, p, grid, s, prepare)        \
-                       : umma_launch_t<InT, OutT, 256, E>(tw, tx, p, grid, s, prepare);
+// Channel-tile widths each epilogue is built for (QKV: one head per tile; argmax: 256).
+bool umma_bn_supported(int epi, int bn) {
   switch (epi) {
-    LLM_UMMA_CASE(EPI_F32)
-    LLM_UMMA_CASE(EPI_S32)
-    LLM_UMMA_CASE(EPI_RESID)
-    LLM_UMMA_CASE(EPI_SWIGLU)
-    LLM_UMMA_CASE(EPI_QKV)
-    LLM_UMMA_CASE(EPI_ARGMAX)
+    case EPI_QKV: return bn == 64 || bn == 128;
+    case EPI_ARGMAX: return bn == 256;
+    case EPI_SWIGLU: return bn == 32 || bn == 64 || bn == 128 || bn == 256;
+    default: return bn == 16 || bn == 32 || bn == 64 || bn == 128 || bn == 256;
   }
-#undef LLM_UMMA_CASE
+}
+
+template <typename InT, typename OutT, int EPI>
+cudaError_t umma_dispatch_bn(const CUtensorMap& tx, const CUtensorMap& tw, const GemmParams& p, int bn, dim3 grid,
+                             cudaStream_t s, bool prepare) {
+  if constexpr (EPI == EPI_QKV) {
+    if (bn == 64) return umma_launch_t<InT, OutT, 64, EPI>(tx, tw, p, grid, s, prepare);
+    if (bn == 128) return umma_launch_t<InT, OutT, 128, EPI>(tx, tw, p, grid, s, prepare);
+  } else if constexpr (EPI == EPI_ARGMAX) {
+    if (bn == 256) return umma_launch_t<InT, OutT, 256, EPI>(tx, tw, p, grid, s, prepare);
+  } else {
+    if constexpr (EPI != EPI_SWIGLU)
+      if (bn == 16) return umma_launch_t<InT, OutT, 16, EPI>(tx, tw, p, grid, s, prepare);
+    if (bn == 32) return umma_launch_t<InT, OutT, 32, EPI>(tx, tw, p, grid, s, prepare);
+    if (bn == 64) return umma_launch_t<InT, OutT, 64, EPI>(tx, tw, p, grid, s, prepare);
+    if (bn == 128) return umma_launch_t<InT, OutT, 128, EPI>(tx, tw, p, grid, s, prepare);
+    if (bn == 256) return umma_launch_t<InT, OutT, 256, EPI>(tx, tw, p, grid, s, prepare);
+  }
   return cudaErrorInvalidValue;
 }
 
-cudaError_t umma_any(int act, bool in8, const CUtensorMap& tw, const CUtensorMap& tx, const GemmParams& p, int epi,
-                     int bt, dim3 grid, cudaStream_t s, bool prepare) {
-  if (in8) return act == 1 ? umma_dispatch<int8_t, __half>(tw, tx, p, epi, bt, grid, s, prepare)
-                           : umma_dispatch<int8_t, __nv_bfloat16>(tw, tx, p, epi, bt, grid, s, prepare);
-  return act == 1 ? umma_dispatch<__half, __half>(tw, tx, p, epi, bt, grid, s, prepare)
-                  : umma_dispatch<__nv_bfloat16, __nv_bfloat16>(tw, tx, p, epi, bt, grid, s, prepare);
+template <typename InT, typename OutT>
+cudaError_t umma_dispatch(const CUtensorMap& tx, const CUtensorMap& tw, const GemmParams& p, int epi, int bn, dim3 grid,
+                          cudaStream_t s, bool prepare) {
+  switch (epi) {
+    case EPI_F32: return umma_dispatch_bn<InT, OutT, EPI_F32>(tx, tw, p, bn, grid, s, prepare);
+    case EPI_S32: return umma_dispatch_bn<InT, OutT, EPI_S32>(tx, tw, p, bn, grid, s, prepare);
+    case EPI_RESID: return umma_dispatch_bn<InT, OutT, EPI_RESID>(tx, tw, p, bn, grid, s, prepare);
+    case EPI_SWIGLU: return umma_dispatch_bn<InT, OutT, EPI_SWIGLU>(tx, tw, p, bn, grid, s, prepare);
+    case EPI_QKV: return umma_dispatch_bn<InT, OutT, EPI_QKV>(tx, tw, p, bn, grid, s, prepare);
+    case EPI_ARGMAX: return umma_dispatch_bn<InT, OutT, EPI_ARGMAX>(tx, tw, p, bn, grid, s, prepare);
+  }
+  return cudaErrorInvalidValue;
 }
 
-// Token tile: the largest of 256/128/64 that still gives at least ~2/3 of the SMs a CTA
-// (small-N projections at decode split their tokens instead of idling most SMs).
-int umma_bt_for(int M, int N, int n_sm) {
-  const int nt = (N + 127) / 128;
-  for (int bt : {256, 128}) {
-    if (M <= bt / 2) continue;  // the next smaller tile already covers M
-    if (static_cast<long long>(nt) * ((M + bt - 1) / bt) * 3 >= 2LL * n_sm) return bt;
-  }
-  return 64;
+cudaError_t umma_any(int act, bool in8, const CUtensorMap& tx, const CUtensorMap& tw, const GemmParams& p, int epi,
+                     int bn, dim3 grid, cudaStream_t s, bool prepare) {
+  if (in8) return act == 1 ? umma_dispatch<int8_t, __half>(tx, tw, p, epi, bn, grid, s, prepare)
+                           : umma_dispatch<int8_t, __nv_bfloat16>(tx, tw, p, epi, bn, grid, s, prepare);
+  return act == 1 ? umma_dispatch<__half, __half>(tx, tw, p, epi, bn, grid, s, prepare)
+                  : umma_dispatch<__nv_bfloat16, __nv_bfloat16>(tx, tw, p, epi, bn, grid, s, prepare);
 }
+
+// Channel-tile width of a tcgen05 projection: QKV one head, argmax 256; otherwise the
+// narrowest tile that still keeps the grid within one CTA per SM (decode: the most SMs
+// streaming weights), or 256 when even that grid is larger (prefill).
+int umma_bn_for(int M, int N, int epi, int head_dim, int n_sm) {
+  if (epi == EPI_QKV) return head_dim;
+  if (epi == EPI_ARGMAX) return 256;
+  const long long tm = (M + kUmmaTokens - 1) / kUmmaTokens;
+  for (int bn : {16, 32, 64, 128, 256}) {
+    if (!umma_bn_supported(epi, bn)) continue;
+    if (tm * ((N + bn - 1) / bn) <= n_sm) return bn;
+  }
+  return 256;
+}
+
+// The greedy-argmax partials: one key per (row, lm_head channel tile).
+int argmax_tile_width(bool umma) { return umma ? 256 : 128; }
 
 struct GemmPlan {
   int bm = 128, splits = 1, kts = 1, tiles = 1;
@@ -481,7 +493,6 @@ struct llm_ctx {
   bool use_pdl = false;
   // cluster split-K of the residual projections: correct, but its DSMEM reduction measured
   // ~5x slower than the unsplit kernel (27.7 vs 4.0 us for Wo), so it is off by default
-  bool umma_cluster_splitk = false;
   std::map<std::tuple<const void*, int, int, int, int>, CUtensorMap> tmaps;
 
   // llm_profile_step: when non-null, enqueue_forward records an event after each launch
@@ -538,9 +549,10 @@ int prepare_kernels(llm_ctx* c) {
   CU(attn_any(c->act, c->cfg.head_dim, ap, c->stream, true));
   CUtensorMap dummy{};
   for (int e : epis)
-    for (int bt : {64, 128, 256}) {
-      CU(umma_any(c->act, false, dummy, dummy, gp, e, bt, dim3(1), c->stream, true));
-      if (c->in8) CU(umma_any(c->act, true, dummy, dummy, gp, e, bt, dim3(1), c->stream, true));
+    for (int bn : {16, 32, 64, 128, 256}) {
+      if (!umma_bn_supported(e, bn)) continue;
+      CU(umma_any(c->act, false, dummy, dummy, gp, e, bn, dim3(1), c->stream, true));
+      if (c->in8) CU(umma_any(c->act, true, dummy, dummy, gp, e, bn, dim3(1), c->stream, true));
     }
   return LLM_OK;
 }
@@ -924,24 +936,17 @@ const CUtensorMap* tmap(llm_ctx* c, const void* ptr, int esz, int k, int rows, i
 
 int gemm(llm_ctx* c, bool in8, int epi, GemmParams p) {
   const int esz = in8 ? 1 : 2;
+  p.argmax_parts = (p.N + argmax_tile_width(c->use_umma) - 1) / argmax_tile_width(c->use_umma);
   if (c->use_umma) {
-    const int bt = umma_bt_for(p.M, p.N, c->n_sm);
-    const CUtensorMap* tw = tmap(c, p.B, esz, p.K, p.N, 128);
-    const CUtensorMap* tx = tmap(c, p.A, esz, p.K, p.M, bt);
+    const int bn = umma_bn_for(p.M, p.N, epi, c->cfg.head_dim, c->n_sm);
+    const CUtensorMap* tx = tmap(c, p.A, esz, p.K, p.M, kUmmaTokens);
+    const CUtensorMap* tw = tmap(c, p.B, esz, p.K, p.N, bn);
     if (!tw || !tx) return LLM_ERR_CUDA;
-    const int k_tiles = p.K * esz / 128;
-    const int tiles = ((p.N + 127) / 128) * ((p.M + bt - 1) / bt);
-    // residual projections with few output tiles split K over a cluster of 2 or 4 CTAs
-    int splits = 1;
-    if (epi == EPI_RESID && c->umma_cluster_splitk)
-      while (splits < 4 && tiles * splits * 3 < 2 * c->n_sm && k_tiles % (2 * splits) == 0 &&
-             k_tiles / (2 * splits) >= 2 && bt % (2 * splits) == 0)
-        splits *= 2;
-    p.k_splits = splits;
-    p.k_tiles_per_split = k_tiles / splits;
+    p.k_splits = 1;
+    p.k_tiles_per_split = p.K * esz / 128;
     p.err = c->d_err;
-    dim3 grid((p.N + 127) / 128, (p.M + bt - 1) / bt, splits);
-    CU(umma_any(c->act, in8, *tw, *tx, p, epi, bt, grid, c->stream, false));
+    dim3 grid((p.M + kUmmaTokens - 1) / kUmmaTokens, (p.N + bn - 1) / bn, 1);
+    CU(umma_any(c->act, in8, *tx, *tw, p, epi, bn, grid, c->stream, false));
     return LLM_OK;
   }
   GemmPlan pl = plan_gemm(p.M, p.N, p.K, esz, c->n_sm, 0, c->ws_floats);
@@ -1140,7 +1145,7 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
     FinishParams f{};
     f.part = c->argmax_part;
     f.M = NF;
-    f.n_tiles = (k.vocab + 127) / 128;
+    f.n_tiles = (k.vocab + argmax_tile_width(c->use_umma) - 1) / argmax_tile_width(c->use_umma);
     f.next = c->d_next;
     f.tok_io = rs.tok_io;
     f.pos_io = rs.pos_io;
@@ -1764,7 +1769,7 @@ int debug_gemm(int device, bool in8, int act, const void* hA, const void* hB, si
   CU(cudaMalloc(&dws.p, ws_cap * 4));
   CU(cudaMalloc(&dcnt.p, 65536 * 4));
   CU(cudaMemset(dcnt.p, 0, 65536 * 4));
-  GemmPlan pl = plan_gemm(M, N, K, in8 ? 1 : 2, prop.multiProcessorCount, splits, ws_cap);
+  GemmPlan pl = plan_gemm(M, N, K, in8 ? 1 : 2, prop.multiProcessorCount, umma_path ? 0 : splits, ws_cap);
   GemmParams p{};
   p.A = dA.p;
   p.B = dB.p;
@@ -1778,19 +1783,21 @@ int debug_gemm(int device, bool in8, int act, const void* hA, const void* hB, si
   p.out = dC.p;
   p.ldo = N;
   if (umma_path) {
-    const int bt = umma_bt_for(M, N, prop.multiProcessorCount);
+    // splits: -1 = the model's channel tile, -bn = that tile width
+    const int bn = splits <= -2 ? -splits : umma_bn_for(M, N, epi, 0, prop.multiProcessorCount);
+    if (!umma_bn_supported(epi, bn)) return fail(LLM_ERR_INVALID, "unsupported tcgen05 channel tile %d", bn);
     CUtensorMap tw{}, tx{};
-    RC(make_kmajor_map(&tw, dB.p, static_cast<int>(esz), act == 2, K, N, 128));
-    RC(make_kmajor_map(&tx, dA.p, static_cast<int>(esz), act == 2, K, M, bt));
+    RC(make_kmajor_map(&tx, dA.p, static_cast<int>(esz), act == 2, K, M, kUmmaTokens));
+    RC(make_kmajor_map(&tw, dB.p, static_cast<int>(esz), act == 2, K, N, bn));
     DevBuf derr;
     CU(cudaMalloc(&derr.p, 4));
     CU(cudaMemset(derr.p, 0, 4));
     p.k_splits = 1;
     p.k_tiles_per_split = K * static_cast<int>(esz) / 128;
     p.err = static_cast<int*>(derr.p);
-    dim3 grid((N + 127) / 128, (M + bt - 1) / bt, 1);
-    CU(umma_any(act, in8, tw, tx, p, epi, bt, grid, 0, true));
-    CU(umma_any(act, in8, tw, tx, p, epi, bt, grid, 0, false));
+    dim3 grid((M + kUmmaTokens - 1) / kUmmaTokens, (N + bn - 1) / bn, 1);
+    CU(umma_any(act, in8, tx, tw, p, epi, bn, grid, 0, true));
+    CU(umma_any(act, in8, tx, tw, p, epi, bn, grid, 0, false));
     CU(cudaDeviceSynchronize());
     int herr = 0;
     CU(cudaMemcpy(&herr, derr.p, 4, cudaMemcpyDeviceToHost));
@@ -1808,8 +1815,9 @@ int debug_gemm(int device, bool in8, int act, const void* hA, const void* hB, si
 
 extern "C" int llm_debug_gemm_i8(int device, const int8_t* A, const int8_t* B, int M, int N, int K, int splits, int32_t* C) {
   if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0 || K % 128) return fail(LLM_ERR_INVALID, "bad arguments (K %% 128 == 0)");
-  // splits < 0 selects the tcgen05 kernel, otherwise the warp-level kernel with that split
-  return debug_gemm(device, true, 2, A, B, 1, M, N, K, splits < 0 ? 0 : splits, EPI_S32, C, splits < 0);
+  // splits < 0 selects the tcgen05 kernel (-1: the model's channel tile, -bn: tile width bn),
+  // otherwise the warp-level kernel with that split (0: its automatic plan)
+  return debug_gemm(device, true, 2, A, B, 1, M, N, K, splits, EPI_S32, C, splits < 0);
 }
 
 extern "C" int llm_debug_gemm_f16(int device, int dtype, const float* A, const float* B, int M, int N, int K, int splits,
@@ -1838,5 +1846,5 @@ extern "C" int llm_debug_gemm_f16(int device, int dtype, const float* A, const f
   std::vector<uint16_t> ha(na), hb(nb);
   CU(cudaMemcpy(ha.data(), hA.p, na * 2, cudaMemcpyDeviceToHost));
   CU(cudaMemcpy(hb.data(), hB.p, nb * 2, cudaMemcpyDeviceToHost));
-  return debug_gemm(device, false, act, ha.data(), hb.data(), 2, M, N, K, splits < 0 ? 0 : splits, EPI_F32, C, splits < 0);
+  return debug_gemm(device, false, act, ha.data(), hb.data(), 2, M, N, K, splits, EPI_F32, C, splits < 0);
 }

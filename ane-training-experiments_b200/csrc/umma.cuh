@@ -1,26 +1,29 @@
 // umma.cuh -- tcgen05 (5th-generation tensor core) GEMM for the token loop's projections.
 //
-//   D[n, m] = sum_k W[n, k] * X[m, k]     (W = weights [N_out x K], X = activations [M x K])
+//   D[m, n] = sum_k X[m, k] * W[n, k]     (X = activations [M x K], W = weights [N x K])
 //
-// The weight tile is the UMMA "A" operand (M_umma = 128 output channels) and the token tile
-// the "B" operand (N_umma = BT tokens, up to 256), so at decode one CTA covers every token
-// of the step and each weight byte is streamed from HBM once.  Both operands are K-major
-// 128-byte-swizzled tiles written by TMA (cp.async.bulk.tensor, no multicast); the fp32/s32
-// accumulator lives in tensor memory.
+// Token-major tiles: the UMMA "A" operand is a 128-token tile of X and the "B" operand a
+// BN-channel tile of W (BN = 16..256), both K-major and 128-byte swizzled, written by TMA
+// (cp.async.bulk.tensor, no multicast).  The fp32/s32 accumulator lives in tensor memory
+// with TMEM lane = token and column = output channel, so in the epilogue every thread owns
+// one token and walks that token's channels in registers: QK-norm, RoPE, SwiGLU pairing and
+// the greedy argmax are per-thread loops over contiguous channels, and every store is a
+// contiguous run of one output row.
+//
+// Decode shapes (a few hundred tokens) are latency-bound per SM, so the host picks BN such
+// that the grid is about one CTA per SM and every CTA streams its share of W through a
+// ~192 KB stage ring (4..11 stages) with all stages in flight.  Grid x = token tile (fastest,
+// so the CTAs that share a weight tile run side by side and the second one reads it from
+// L2), y = channel tile.
 //
 // Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM allocator + MMA issuer
 // (one elected thread), warps 2..5 = epilogue.  Epilogue warp w reads TMEM lanes
-// 32*(w%4)..+31, i.e. thread = output channel, and walks the token columns 32 at a time.
-// A STAGES-deep ring of (full, empty) mbarriers connects producer and MMA; tcgen05.commit
-// releases a stage when its MMAs have consumed it and signals the epilogue after the last.
-// Every mbarrier wait is bounded: on expiry the kernel records kDevWaitTimeout, skips the
-// remaining work and still reaches the TMEM deallocation.
-//
-// Split-K (residual epilogue only, p.k_splits > 1): the splits of one output tile are one
-// thread-block cluster along z.  Each CTA parks its partial accumulator tile in its own (now
-// idle) stage memory; after a cluster barrier CTA rank r sums token slice r of all ranks'
-// partials through distributed shared memory, in rank order, and runs the epilogue on it; a
-// second cluster barrier keeps every CTA's shared memory alive until its peers are done.
+// 32*(w%4)..+31.  A STAGES-deep ring of (full, empty) mbarriers connects producer and MMA;
+// tcgen05.commit releases a stage when its MMAs have consumed it and signals the epilogue
+// after the last.  Everything the epilogue needs besides the accumulator (token scales and
+// positions, channel scales, norm weights, residual rows, RoPE rows) is loaded while the
+// mainloop runs.  Every mbarrier wait is bounded: on expiry the kernel records
+// kDevWaitTimeout, skips the remaining work and still reaches the TMEM deallocation.
 #pragma once
 #include <cuda.h>
 
@@ -77,29 +80,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;\n" ::: "memory"); }
-// Thread-block cluster barrier (every thread of every CTA of the cluster arrives), with
-// release/acquire ordering of shared-memory writes across the cluster.
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
-}
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
-  return r;
-}
-// 32-bit load from CTA `rank`'s shared memory at the address this CTA uses for `saddr`.
-// Not volatile: the loads only follow the cluster barrier (which orders them), so the
-// compiler may batch them.
-__device__ __forceinline__ uint32_t dsmem_addr(uint32_t saddr, uint32_t rank) {
-  uint32_t remote;
-  asm("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(remote) : "r"(saddr), "r"(rank));
-  return remote;
-}
-__device__ __forceinline__ uint32_t ld_dsmem(uint32_t remote) {
-  uint32_t v;
-  asm("ld.shared::cluster.u32 %0, [%1];\n" : "=r"(v) : "r"(remote));
-  return v;
-}
+__device__ __forceinline__ void prefetch_l2(const void* ptr) { asm volatile("prefetch.global.L2 [%0];\n" ::"l"(ptr)); }
 
 // Shared-memory matrix descriptor for a K-major operand tile whose rows are 128 bytes,
 // written by TMA with 128-byte swizzle: 8-row core groups 1024 bytes apart (SBO), layout
@@ -127,38 +108,52 @@ __host__ __device__ constexpr uint32_t umma_idesc(int m, int n) {
 }
 
 constexpr int kUmmaThreads = 192;
+constexpr int kUmmaTokens = 128;  // token rows per tile (UMMA M)
 
-template <int BT, int STAGES>
+// Stage ring of ~192 KB: one CTA per SM, all stages in flight.
+template <int BN>
+constexpr int umma_stages() {
+  return (192 * 1024) / ((kUmmaTokens + BN) * 128) > 11 ? 11 : (192 * 1024) / ((kUmmaTokens + BN) * 128);
+}
+template <int BN>
 constexpr int umma_smem_bytes() {
-  return STAGES * (128 + BT) * 128 + 1024;  // + alignment slack
+  return umma_stages<BN>() * (kUmmaTokens + BN) * 128 + 1024;  // + alignment slack
+}
+template <int BN>
+constexpr uint32_t umma_tmem_cols() {
+  return BN < 32 ? 32u : static_cast<uint32_t>(BN);
 }
 
-template <typename InT, typename OutT, int BT, int STAGES, int EPI>
+// Monotone 32-bit key of a float (the high half of argmax_key): unsigned order of the keys
+// is the order of the values, with distinct keys for distinct bit patterns.
+__device__ __forceinline__ uint32_t float_key_fast(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return u ^ (static_cast<uint32_t>(static_cast<int>(u) >> 31) | 0x80000000u);
+}
+
+template <typename InT, typename OutT, int BN, int EPI>
 __global__ void __launch_bounds__(kUmmaThreads, 1)
-    umma_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, GemmParams p) {
+    umma_gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, GemmParams p) {
   constexpr bool I8 = sizeof(InT) == 1;
-  constexpr int A_BYTES = 128 * 128;
-  constexpr int B_BYTES = BT * 128;
+  constexpr int STAGES = umma_stages<BN>();
+  constexpr int A_BYTES = kUmmaTokens * 128;
+  constexpr int B_BYTES = BN * 128;
   constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  constexpr uint32_t TMEM_COLS = BT < 32 ? 32 : BT;
+  constexpr uint32_t TMEM_COLS = umma_tmem_cols<BN>();
   constexpr int ESZ = sizeof(InT);
   constexpr int KSTEP_BYTES = 32;  // one UMMA consumes 32 bytes of K (16 x 16-bit or 32 x 8-bit)
+  constexpr int NCH = (BN + 31) / 32;  // 32-column chunks of the accumulator
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES], accum_bar;
   __shared__ uint32_t s_tmem;
-  __shared__ int s_pos[BT], s_page[BT];
-  __shared__ double s_ss[4][32];
-  __shared__ unsigned long long s_best[4][32];
+  __shared__ float s_bsc[BN];   // per-channel weight scales (int8)
+  __shared__ float s_nw[BN];    // QK-norm weights of this tile's head
 
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_tile = blockIdx.x, m_tile = blockIdx.y;
-  const int n0 = n_tile * 128, m0 = m_tile * BT;
-  const int k_tiles = p.K * ESZ / 128;
-  const int kt_begin = blockIdx.z * p.k_tiles_per_split;
-  const int kt_end = min(k_tiles, kt_begin + p.k_tiles_per_split);
-  const int nkt = max(0, kt_end - kt_begin);
+  const int tok0 = blockIdx.x * kUmmaTokens, ch0 = blockIdx.y * BN;
+  const int nkt = p.K * ESZ / 128;
 
   griddep_launch_dependents();
   if (threadIdx.x == 0) {
@@ -182,20 +177,19 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
-      asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
       asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
-      // The weights do not depend on the preceding kernel: stream the first stages' weight
-      // tiles while it drains, then wait for it before touching the activations.
+      asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
+      // The weights do not depend on the preceding kernel: start streaming the first
+      // stages' weight tiles while it drains, then wait for it before the activations.
       const int pre = min(nkt, STAGES);
       for (int i = 0; i < pre; ++i) {
         const uint32_t st = sbase + i * STAGE_BYTES;
         mbar_arrive_expect_tx(smem_u32(&full_bar[i]), STAGE_BYTES);
-        tma_load_2d(st, &tmW, (kt_begin + i) * (128 / ESZ), n0, smem_u32(&full_bar[i]));
+        tma_load_2d(st + A_BYTES, &tmW, i * (128 / ESZ), ch0, smem_u32(&full_bar[i]));
       }
       griddep_wait();
       for (int i = 0; i < pre; ++i)
-        tma_load_2d(sbase + i * STAGE_BYTES + A_BYTES, &tmX, (kt_begin + i) * (128 / ESZ), m0,
-                    smem_u32(&full_bar[i]));
+        tma_load_2d(sbase + i * STAGE_BYTES, &tmX, i * (128 / ESZ), tok0, smem_u32(&full_bar[i]));
       for (int i = pre; i < nkt; ++i) {
         const int s = i % STAGES;
         const uint32_t par = ((i / STAGES) & 1) ^ 1;
@@ -204,16 +198,16 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
           break;
         }
         const uint32_t st = sbase + s * STAGE_BYTES;
-        const int kx = (kt_begin + i) * (128 / ESZ);  // element coordinate of the K slice
+        const int kx = i * (128 / ESZ);  // element coordinate of the K slice
         mbar_arrive_expect_tx(smem_u32(&full_bar[s]), STAGE_BYTES);
-        tma_load_2d(st, &tmW, kx, n0, smem_u32(&full_bar[s]));
-        tma_load_2d(st + A_BYTES, &tmX, kx, m0, smem_u32(&full_bar[s]));
+        tma_load_2d(st + A_BYTES, &tmW, kx, ch0, smem_u32(&full_bar[s]));
+        tma_load_2d(st, &tmX, kx, tok0, smem_u32(&full_bar[s]));
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc<InT>(128, BT);
+      constexpr uint32_t idesc = umma_idesc<InT>(kUmmaTokens, BN);
       for (int i = 0; i < nkt; ++i) {
         const int s = i % STAGES;
         if (!mbar_wait_bounded(smem_u32(&full_bar[s]), (i / STAGES) & 1)) {
@@ -232,269 +226,252 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     }
   } else {
     // ---------------------------------------------------------------- epilogue (warps 2..5)
-    const int q = warp & 3;                 // TMEM lane quadrant
-    const int et = threadIdx.x - 64;        // 0..127 among epilogue threads
-    const int nl = q * 32 + lane;           // channel within the tile
-    const int n = n0 + nl;
+    const int q = warp & 3;              // TMEM lane quadrant
+    const int et = threadIdx.x - 64;     // 0..127 among epilogue threads
+    const int tl = q * 32 + lane;        // token within the tile (= TMEM lane)
+    const int tok = tok0 + tl;
+    const bool tok_ok = tok < p.M;
+    const int tokc = tok_ok ? tok : p.M - 1;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(q * 32) << 16);
     griddep_wait();  // positions, scales and the residual come from earlier kernels
+
+    // ---- loads that only depend on earlier kernels, overlapped with the mainloop
+    float a_s = 1.0f;
+    if constexpr (I8) a_s = p.a_scale[tokc];
+    for (int j = et; j < BN; j += 128) {
+      const int ch = ch0 + j;
+      if constexpr (I8) s_bsc[j] = ch < p.N ? p.b_scale[ch] : 0.0f;
+    }
+    float rs[32];  // residual of the first chunk
+    if constexpr (EPI == EPI_RESID) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        rs[j] = (j < BN && tok_ok && ch0 + j < p.N) ? p.resid[static_cast<size_t>(tok) * p.ldo + ch0 + j] : 0.f;
+    }
+    int region = 0, head = 0, pos = 0, page = 0;
+    const float* cs_row = nullptr;
+    const float* sn_row = nullptr;
     if constexpr (EPI == EPI_QKV) {
-      for (int j = et; j < BT; j += 128) {
-        const int m = m0 + j;
-        int pos = 0, page = 0;
-        if (m < p.M) {
-          pos = p.positions[m];
-          page = p.block_table[static_cast<size_t>(p.seq_ids[m]) * p.max_pages_per_seq + (pos >> 4)];
-        }
-        s_pos[j] = pos;
-        s_page[j] = page;
+      const int hd = p.head_dim;  // == BN
+      const int q_dim = p.n_heads * hd, kv_dim = p.n_kv_heads * hd;
+      if (ch0 < q_dim) { region = 0; head = ch0 / hd; }
+      else if (ch0 < q_dim + kv_dim) { region = 1; head = (ch0 - q_dim) / hd; }
+      else { region = 2; head = (ch0 - q_dim - kv_dim) / hd; }
+      if (tok_ok) {
+        pos = p.positions[tok];
+        if (region > 0) page = p.block_table[static_cast<size_t>(p.seq_ids[tok]) * p.max_pages_per_seq + (pos >> 4)];
+      }
+      cs_row = p.rope_cos + static_cast<size_t>(pos) * (hd / 2);
+      sn_row = p.rope_sin + static_cast<size_t>(pos) * (hd / 2);
+      for (int b = 0; b < hd * 2; b += 128) {
+        prefetch_l2(reinterpret_cast<const uint8_t*>(cs_row) + b);
+        prefetch_l2(reinterpret_cast<const uint8_t*>(sn_row) + b);
+      }
+      if (region < 2 && p.qk_norm) {
+        const float* nw = region == 0 ? p.q_norm : p.k_norm;
+        for (int j = et; j < BN; j += 128) s_nw[j] = nw[j];
       }
     }
-    const float sw = (I8 && n < p.N) ? p.b_scale[n] : 1.0f;
-    // 32 x 33 transpose buffers of the epilogue warps live in the stage ring, which is idle
-    // once the accumulator is complete (every TMA write and MMA read has finished)
-    float(*s_tr)[32 * 33] = reinterpret_cast<float(*)[32 * 33]>(smem_raw + (sbase - smem_u32(smem_raw)));
+
     bool ok = nkt > 0 && mbar_wait_bounded(smem_u32(&accum_bar), 0);
     if (!ok && nkt > 0) failed = true;
     tc_fence_after();
-    if constexpr (EPI == EPI_QKV) epi_bar();  // s_pos / s_page visible to all epilogue warps
-    const int mcount = min(BT, p.M - m0);
-    const bool split = EPI == EPI_RESID && p.k_splits > 1;
-    if (split) {
-      // stage this split's partial tile [128 channels][BT tokens] (+1 column of padding)
-      uint32_t* part = reinterpret_cast<uint32_t*>(smem_raw + (sbase - smem_u32(smem_raw)));
-      for (int c0 = 0; c0 < BT; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) part[nl * (BT + 1) + c0 + j] = ok ? r[j] : 0u;
-      }
-    }
-    for (int c0 = 0; c0 < BT && !split; c0 += 32) {
-      if (c0 >= mcount) break;  // uniform across the epilogue warps
+    epi_bar();  // s_bsc / s_nw visible to all epilogue threads
+
+    // dequantised chunk c (columns 32c..32c+31 of this token's row)
+    auto load_chunk = [&](int c, float (&v)[32]) {
       uint32_t r[32];
-      tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, r);
+      tmem_ld32(trow + c * 32, r);
       tmem_wait_ld();
-      float v[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        if constexpr (I8) {
-          const int m = min(m0 + c0 + j, p.M - 1);
-          v[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), p.a_scale[m]), sw);
-        } else {
-          v[j] = __uint_as_float(r[j]);
+        if constexpr (I8) v[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), a_s), s_bsc[(c * 32 + j) % BN]);
+        else v[j] = __uint_as_float(r[j]);
+        if (!ok) v[j] = 0.f;
+      }
+    };
+
+    if constexpr (EPI == EPI_S32) {
+      for (int c = 0; c < NCH; ++c) {
+        uint32_t r[32];
+        tmem_ld32(trow + c * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int ch = ch0 + c * 32 + j;
+          if (c * 32 + j < BN && tok_ok && ch < p.N)
+            reinterpret_cast<int*>(p.out)[static_cast<size_t>(tok) * p.ldo + ch] = ok ? static_cast<int>(r[j]) : 0;
         }
       }
-      if (!ok) {
+    } else if constexpr (EPI == EPI_F32) {
+      for (int c = 0; c < NCH; ++c) {
+        float v[32];
+        load_chunk(c, v);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = 0.f;
+        for (int j = 0; j < 32; ++j) {
+          const int ch = ch0 + c * 32 + j;
+          if (c * 32 + j < BN && tok_ok && ch < p.N) reinterpret_cast<float*>(p.out)[static_cast<size_t>(tok) * p.ldo + ch] = v[j];
+        }
       }
-      if constexpr (EPI == EPI_S32 || EPI == EPI_F32 || EPI == EPI_RESID) {
-        // out may alias resid (in-place residual): read the whole chunk before any store
-        float rs[32];
-        if constexpr (EPI == EPI_RESID) {
+    } else if constexpr (EPI == EPI_RESID) {
+      // out may alias resid (in-place residual): every element is read before it is written,
+      // by the same thread
+      for (int c = 0; c < NCH; ++c) {
+        float v[32];
+        load_chunk(c, v);
+        if (c > 0) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            const int m = m0 + c0 + j;
-            rs[j] = (m < p.M && n < p.N) ? p.resid[static_cast<size_t>(m) * p.ldo + n] : 0.f;
+            const int ch = ch0 + c * 32 + j;
+            rs[j] = (tok_ok && ch < p.N) ? p.resid[static_cast<size_t>(tok) * p.ldo + ch] : 0.f;
           }
         }
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const int m = m0 + c0 + j;
-          if (m < p.M && n < p.N) {
-            const size_t idx = static_cast<size_t>(m) * p.ldo + n;
-            if constexpr (EPI == EPI_S32) reinterpret_cast<int*>(p.out)[idx] = static_cast<int>(r[j]);
-            else if constexpr (EPI == EPI_F32) reinterpret_cast<float*>(p.out)[idx] = v[j];
-            else reinterpret_cast<float*>(p.out)[idx] = __fadd_rn(v[j], rs[j]);
+          const int ch = ch0 + c * 32 + j;
+          if (c * 32 + j < BN && tok_ok && ch < p.N)
+            reinterpret_cast<float*>(p.out)[static_cast<size_t>(tok) * p.ldo + ch] = __fadd_rn(v[j], rs[j]);
+        }
+      }
+    } else if constexpr (EPI == EPI_SWIGLU) {
+      // interleaved rows: channel 2i is W1 row i (gate), 2i+1 is W3 row i (up)
+      const int F = p.N / 2;
+      for (int c = 0; c < NCH; ++c) {
+        float v[32];
+        load_chunk(c, v);
+        float g[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float h1 = v[2 * i], up = v[2 * i + 1];
+          g[i] = __fmul_rn(__fdiv_rn(h1, __fadd_rn(1.0f, expf(-h1))), up);
+        }
+        const int j0 = (ch0 + c * 32) / 2;  // first output channel of the chunk
+        if (tok_ok) {
+          if (p.swiglu_f32) {
+            float* dst = reinterpret_cast<float*>(p.out) + static_cast<size_t>(tok) * F + j0;
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (c * 32 + 2 * i < BN && j0 + i < F) dst[i] = g[i];
+          } else if (c * 32 + 32 <= BN && j0 + 16 <= F && (F % 8) == 0) {
+            uint4 pk[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              pk[h].x = ActTraits<OutT>::pack2(g[8 * h + 0], g[8 * h + 1]);
+              pk[h].y = ActTraits<OutT>::pack2(g[8 * h + 2], g[8 * h + 3]);
+              pk[h].z = ActTraits<OutT>::pack2(g[8 * h + 4], g[8 * h + 5]);
+              pk[h].w = ActTraits<OutT>::pack2(g[8 * h + 6], g[8 * h + 7]);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<OutT*>(p.out) + static_cast<size_t>(tok) * F + j0);
+            dst[0] = pk[0];
+            dst[1] = pk[1];
+          } else {
+            OutT* dst = reinterpret_cast<OutT*>(p.out) + static_cast<size_t>(tok) * F + j0;
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (c * 32 + 2 * i < BN && j0 + i < F) dst[i] = ActTraits<OutT>::from_f(g[i]);
           }
         }
-      } else if constexpr (EPI == EPI_SWIGLU) {
-        // rows interleaved (W1[j], W3[j]): lane 2i holds the gate, lane 2i+1 the up value of
-        // channel pair i for 32 tokens.  The even lane finishes tokens 0..15, the odd lane
-        // tokens 16..31, each receiving the missing operand from its neighbour.
-        const int F = p.N / 2;
-        const bool odd = lane & 1;
+      }
+    } else if constexpr (EPI == EPI_ARGMAX) {
+      // (key desc, channel asc) over this token's BN channels: two interleaved running
+      // maxima (even / odd columns) break the dependency chain, then merge.
+      uint32_t bk[2] = {0u, 0u};
+      int bi[2] = {ch0, ch0};
+      for (int c = 0; c < NCH; ++c) {
+        float v[32];
+        load_chunk(c, v);
+        if (p.logits && tok_ok) {
+          float* dst = p.logits + static_cast<size_t>(tok) * p.ld_logits + ch0 + c * 32;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float sent = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[j + 16], 1);
-          const float h1 = odd ? sent : v[j];
-          const float up = odd ? v[j + 16] : sent;
-          const int m = m0 + c0 + j + (odd ? 16 : 0);
-          const int ch = n & ~1;
-          if (m < p.M && ch < p.N) {
-            const float gv = __fmul_rn(__fdiv_rn(h1, __fadd_rn(1.0f, expf(-h1))), up);
-            const size_t idx = static_cast<size_t>(m) * F + (ch >> 1);
-            if (p.swiglu_f32) reinterpret_cast<float*>(p.out)[idx] = gv;
-            else reinterpret_cast<OutT*>(p.out)[idx] = ActTraits<OutT>::from_f(gv);
+          for (int j = 0; j < 32; ++j)
+            if (c * 32 + j < BN && ch0 + c * 32 + j < p.N) dst[j] = v[j];
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int ch = ch0 + c * 32 + j;
+          const uint32_t k = (c * 32 + j < BN && ch < p.N) ? float_key_fast(v[j]) : 0u;
+          if (k > bk[j & 1]) {
+            bk[j & 1] = k;
+            bi[j & 1] = ch;
           }
         }
-      } else if constexpr (EPI == EPI_ARGMAX) {
-        if (p.logits) {
+      }
+      const int w = (bk[1] > bk[0] || (bk[1] == bk[0] && bi[1] < bi[0])) ? 1 : 0;
+      if (tok_ok)
+        p.argmax_part[static_cast<size_t>(tok) * p.argmax_parts + blockIdx.y] =
+            (static_cast<unsigned long long>(bk[w]) << 32) | (0xffffffffu - static_cast<uint32_t>(bi[w]));
+    } else if constexpr (EPI == EPI_QKV) {
+      // One head per tile (BN == head_dim): QK-norm over the whole head (sum of squares in
+      // f64), RoPE on adjacent pairs, then the head's row is stored to q or to its K/V page.
+      const int hd = BN;
+      float rr = 1.0f;
+      if (region < 2 && p.qk_norm) {
+        double ss = 0.0;
+        for (int c = 0; c < NCH; ++c) {
+          float v[32];
+          load_chunk(c, v);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int m = m0 + c0 + j;
-            if (n < p.N && m < p.M) p.logits[static_cast<size_t>(m) * p.ld_logits + n] = v[j];
-          }
+          for (int j = 0; j < 32; ++j) ss = __dadd_rn(ss, __dmul_rn((double)v[j], (double)v[j]));
         }
-        // transpose the 32 channels x 32 tokens block so thread `lane` scans token lane's
-        // 32 channels in ascending order (first maximum wins), then combine the 4 warps
-        float* tb = s_tr[q];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) tb[j * 33 + lane] = v[j];
-        __syncwarp();
-        unsigned long long best = 0ull;
-        const int nbase = n0 + q * 32;
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          if (nbase + c < p.N) {
-            const unsigned long long k = argmax_key(tb[lane * 33 + c], nbase + c);
-            best = k > best ? k : best;
-          }
+        rr = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)hd), p.eps))));
+      }
+      const int slot = pos & 15;
+      OutT* kv_base = nullptr;
+      if (region > 0 && tok_ok) {
+        if (page < 0 || page >= p.n_pages) {
+          if (p.err) atomicExch(p.err, kDevBadPage);
+        } else {
+          const size_t blk =
+              ((static_cast<size_t>(p.layer) * p.n_pages + page) * p.n_kv_heads + head) * 2 + (region - 1);
+          kv_base = reinterpret_cast<OutT*>(p.kv_pool) + blk * 16 * hd + slot * hd;
         }
-        s_best[q][lane] = best;
-        epi_bar();
-        if (et < 32) {
-          unsigned long long b = s_best[0][et];
-#pragma unroll
-          for (int w = 1; w < 4; ++w) b = s_best[w][et] > b ? s_best[w][et] : b;
-          const int m = m0 + c0 + et;
-          if (m < p.M) p.argmax_part[static_cast<size_t>(n_tile) * p.M + m] = b;
-        }
-        epi_bar();
-      } else if constexpr (EPI == EPI_QKV) {
-        // Transpose the warp's 32 channels x 32 tokens block through shared memory so each
-        // thread owns one token's 32 consecutive channels of a head.
-        const int hd = p.head_dim;
-        const int q_dim = p.n_heads * hd, kv_dim = p.n_kv_heads * hd;
-        int region, head0;
-        if (n0 < q_dim) { region = 0; head0 = n0 / hd; }
-        else if (n0 < q_dim + kv_dim) { region = 1; head0 = (n0 - q_dim) / hd; }
-        else { region = 2; head0 = (n0 - q_dim - kv_dim) / hd; }
-        float* tb = s_tr[q];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) tb[j * 33 + lane] = v[j];
-        __syncwarp();
+      }
+      for (int c = 0; c < NCH; ++c) {
         float x[32];
-#pragma unroll
-        for (int c = 0; c < 32; ++c) x[c] = tb[lane * 33 + c];
-        const int tok = c0 + lane;              // this thread's token within the tile
-        const int m = m0 + tok;
-        const int cbase = q * 32;               // first channel of this warp within the tile
-        const int head = head0 + cbase / hd;
-        const int d0 = cbase % hd;              // first head dimension held by this thread
-        const int wph = hd / 32;                // warps per head
-        if (region < 2 && p.qk_norm) {
-          double ss = 0.0;
-#pragma unroll
-          for (int c = 0; c < 32; ++c) ss = __dadd_rn(ss, __dmul_rn((double)x[c], (double)x[c]));
-          s_ss[q][lane] = ss;
-          epi_bar();
-          const int qh0 = (q / wph) * wph;
-          double tot = 0.0;
-          for (int w = 0; w < wph; ++w) tot = __dadd_rn(tot, s_ss[qh0 + w][lane]);
-          const float rr = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(tot, (double)hd), p.eps))));
-          const float* nw = region == 0 ? p.q_norm : p.k_norm;
-#pragma unroll
-          for (int c = 0; c < 32; ++c) x[c] = __fmul_rn(__fmul_rn(x[c], rr), nw[d0 + c]);
-          epi_bar();
-        }
-        const int pos = s_pos[tok];
+        load_chunk(c, x);
+        const int d0 = c * 32;  // first head dimension of the chunk
         if (region < 2) {
-          const float* cs = p.rope_cos + static_cast<size_t>(pos) * (hd / 2) + d0 / 2;
-          const float* sn = p.rope_sin + static_cast<size_t>(pos) * (hd / 2) + d0 / 2;
+          if (p.qk_norm) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) x[j] = __fmul_rn(__fmul_rn(x[j], rr), s_nw[d0 + j]);
+          }
+          float cs[16], sn[16];
+#pragma unroll
+          for (int i = 0; i < 16; i += 4) {
+            const float4 a = *reinterpret_cast<const float4*>(cs_row + d0 / 2 + i);
+            const float4 b = *reinterpret_cast<const float4*>(sn_row + d0 / 2 + i);
+            cs[i] = a.x; cs[i + 1] = a.y; cs[i + 2] = a.z; cs[i + 3] = a.w;
+            sn[i] = b.x; sn[i + 1] = b.y; sn[i + 2] = b.z; sn[i + 3] = b.w;
+          }
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float c = cs[i], s = sn[i];
             const float a0 = x[2 * i], a1 = x[2 * i + 1];
-            x[2 * i] = __fsub_rn(__fmul_rn(a0, c), __fmul_rn(a1, s));
-            x[2 * i + 1] = __fadd_rn(__fmul_rn(a0, s), __fmul_rn(a1, c));
+            x[2 * i] = __fsub_rn(__fmul_rn(a0, cs[i]), __fmul_rn(a1, sn[i]));
+            x[2 * i + 1] = __fadd_rn(__fmul_rn(a0, sn[i]), __fmul_rn(a1, cs[i]));
           }
         }
-        if (m < p.M && n0 + cbase < p.N) {
-          uint4 pk[4];
+        uint4 pk[4];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            pk[c].x = ActTraits<OutT>::pack2(x[8 * c + 0], x[8 * c + 1]);
-            pk[c].y = ActTraits<OutT>::pack2(x[8 * c + 2], x[8 * c + 3]);
-            pk[c].z = ActTraits<OutT>::pack2(x[8 * c + 4], x[8 * c + 5]);
-            pk[c].w = ActTraits<OutT>::pack2(x[8 * c + 6], x[8 * c + 7]);
-          }
-          if (region == 0) {
-            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<OutT*>(p.q_out) +
-                                                  (static_cast<size_t>(m) * p.n_heads + head) * hd + d0);
-#pragma unroll
-            for (int c = 0; c < 4; ++c) dst[c] = pk[c];
-          } else {
-            const int page = s_page[tok];
-            if (page < 0 || page >= p.n_pages) {
-              if (p.err) atomicExch(p.err, kDevBadPage);
-            } else {
-              const int slot = pos & 15;
-              const size_t blk =
-                  ((static_cast<size_t>(p.layer) * p.n_pages + page) * p.n_kv_heads + head) * 2 + (region - 1);
-              OutT* base = reinterpret_cast<OutT*>(p.kv_pool) + blk * 16 * hd + slot * hd;
-#pragma unroll
-              for (int c = 0; c < 4; ++c) {
-                const int chunk = ((d0 >> 3) + c) ^ (slot & 7);
-                *reinterpret_cast<uint4*>(base + chunk * 8) = pk[c];
-              }
-            }
-          }
+        for (int h = 0; h < 4; ++h) {
+          pk[h].x = ActTraits<OutT>::pack2(x[8 * h + 0], x[8 * h + 1]);
+          pk[h].y = ActTraits<OutT>::pack2(x[8 * h + 2], x[8 * h + 3]);
+          pk[h].z = ActTraits<OutT>::pack2(x[8 * h + 4], x[8 * h + 5]);
+          pk[h].w = ActTraits<OutT>::pack2(x[8 * h + 6], x[8 * h + 7]);
         }
-        __syncwarp();
-      }
-    }
-  }
-  if constexpr (EPI == EPI_RESID) {
-    if (p.k_splits > 1) {
-      __syncwarp();
-      cluster_sync_all();  // every split's partial tile is in its shared memory
-      if (warp >= 2) {
-        const int q = warp & 3, nl = q * 32 + lane, n = n0 + nl;
-        const float sw = (I8 && n < p.N) ? p.b_scale[n] : 1.0f;
-        const uint32_t rank = cluster_rank();
-        const int S = p.k_splits;
-        const int per = BT / S;
-        uint32_t base[4];  // the partial tile of every rank (same offset in each CTA)
+        if (!tok_ok) continue;
+        if (region == 0) {
+          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<OutT*>(p.q_out) +
+                                                (static_cast<size_t>(tok) * p.n_heads + head) * hd + d0);
 #pragma unroll
-        for (int sr = 0; sr < 4; ++sr) base[sr] = sr < S ? dsmem_addr(sbase, sr) : 0u;
-        // token slice in batches of 8: issue the batch's remote loads of every rank, then sum
-        for (int jb = 0; jb < per; jb += 8) {
-          uint32_t raw[4][8];
+          for (int h = 0; h < 4; ++h) dst[h] = pk[h];
+        } else if (kv_base) {
 #pragma unroll
-          for (int sr = 0; sr < 4; ++sr)
-#pragma unroll
-            for (int jj = 0; jj < 8; ++jj)
-              if (sr < S && jb + jj < per)
-                raw[sr][jj] =
-                    ld_dsmem(base[sr] + 4u * static_cast<uint32_t>(nl * (BT + 1) + static_cast<int>(rank) * per + jb + jj));
-#pragma unroll
-          for (int jj = 0; jj < 8; ++jj) {
-            const int j = static_cast<int>(rank) * per + jb + jj;
-            const int m = m0 + j;
-            if (jb + jj >= per || m >= p.M || n >= p.N) continue;
-            float v;
-            if constexpr (I8) {
-              int acc = 0;
-#pragma unroll
-              for (int sr = 0; sr < 4; ++sr)
-                if (sr < S) acc += static_cast<int>(raw[sr][jj]);
-              v = __fmul_rn(__fmul_rn(__int2float_rn(acc), p.a_scale[m]), sw);
-            } else {
-              float acc = 0.f;
-#pragma unroll
-              for (int sr = 0; sr < 4; ++sr)
-                if (sr < S) acc = __fadd_rn(acc, __uint_as_float(raw[sr][jj]));
-              v = acc;
-            }
-            const size_t idx = static_cast<size_t>(m) * p.ldo + n;
-            reinterpret_cast<float*>(p.out)[idx] = __fadd_rn(v, p.resid[idx]);
+          for (int h = 0; h < 4; ++h) {
+            const int chunk = ((d0 >> 3) + h) ^ (slot & 7);
+            *reinterpret_cast<uint4*>(kv_base + chunk * 8) = pk[h];
           }
         }
       }
-      __syncwarp();
-      cluster_sync_all();  // peers may still be reading this CTA's partial tile
     }
   }
   if (failed && p.err) atomicExch(p.err, kDevWaitTimeout);

@@ -64,6 +64,8 @@ static int g_threads = 0;
  * far a correct implementation that merely sums in another order can drift. */
 static int g_attn_reverse = 0;
 void oracle_set_attn_reverse(int on) { g_attn_reverse = on; }
+static int g_matvec_reverse = 0;
+void oracle_set_matvec_reverse(int on) { g_matvec_reverse = on; }
 void oracle_set_threads(int n) {
   g_threads = n;
 #ifdef _OPENMP
@@ -431,7 +433,10 @@ static void matvec_f32(float *out, const float *mat, const float *in, int rows, 
   for (int r = 0; r < rows; r++) {
     const float *row = mat + (size_t)r * cols;
     float sum = 0.0f;
-    for (int c = 0; c < cols; c++) sum += row[c] * in[c];
+    if (g_matvec_reverse)
+      for (int c = cols - 1; c >= 0; c--) sum += row[c] * in[c];
+    else
+      for (int c = 0; c < cols; c++) sum += row[c] * in[c];
     out[r] = sum;
   }
 }

@@ -131,6 +131,8 @@ float oracle_dequant(int32_t acc, float sa, float sw);
 
 /* Test-only: 1 = sum the attention PV products in reverse position order (emulation modes). */
 void oracle_set_attn_reverse(int on);
+/* Test-only: 1 = sum every f32 matVec (fp32 / fp16 / bf16 modes) in reverse column order. */
+void oracle_set_matvec_reverse(int on);
 /* Thread count used by row-parallel loops (OpenMP); 0 = library default. */
 void oracle_set_threads(int n);
 int oracle_get_threads(void);

@@ -80,6 +80,7 @@ def lib() -> C.CDLL:
         "oracle_dequant": (C.c_float, [C.c_int32, C.c_float, C.c_float]),
         "oracle_set_threads": (None, [C.c_int]),
         "oracle_set_attn_reverse": (None, [C.c_int]),
+        "oracle_set_matvec_reverse": (None, [C.c_int]),
         "oracle_get_threads": (C.c_int, []),
     }
     for n, (r, a) in sig.items():
@@ -238,6 +239,10 @@ def round_bf16(x: float) -> float:
 
 def set_attn_reverse(on: bool):
     lib().oracle_set_attn_reverse(int(on))
+
+
+def set_matvec_reverse(on: bool):
+    lib().oracle_set_matvec_reverse(int(on))
 
 
 def set_threads(n: int):

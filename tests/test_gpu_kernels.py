@@ -77,7 +77,8 @@ def test_quantiser_rounding_boundaries_bit_exact():
 
 
 def dev_gemm_i8(A, B, splits):
-    """splits < 0: the tcgen05 kernel; otherwise the warp-level kernel with that split."""
+    """splits < 0: the tcgen05 kernel (-1 the model's channel tile, -bn tile width bn);
+    otherwise the warp-level kernel with that split."""
     M, K = A.shape
     N = B.shape[0]
     Cm = np.zeros((M, N), np.int32)
@@ -88,7 +89,9 @@ def dev_gemm_i8(A, B, splits):
 
 @pytest.mark.parametrize("M,N,K", [(1, 128, 128), (7, 384, 768), (64, 1000, 1024), (256, 1024, 3072),
                                    (130, 4096, 1024), (300, 256, 2048)])
-@pytest.mark.parametrize("splits", [-1, 0, 1, 3], ids=["tcgen05", "mma-auto", "mma-1", "mma-3"])
+@pytest.mark.parametrize("splits", [-1, -16, -32, -64, -128, -256, 0, 1, 3],
+                         ids=["tcgen05", "tcgen05-n16", "tcgen05-n32", "tcgen05-n64", "tcgen05-n128", "tcgen05-n256",
+                              "mma-auto", "mma-1", "mma-3"])
 def test_gemm_i8_bit_exact(M, N, K, splits):
     rng = np.random.default_rng(M * 7 + N + K + splits)
     A = rng.integers(-128, 128, (M, K), dtype=np.int8)
@@ -107,7 +110,8 @@ def round_to(x, dtype):
 @pytest.mark.parametrize("dtype", [_abi.LLM_DTYPE_F16, _abi.LLM_DTYPE_BF16])
 @pytest.mark.parametrize("M,N,K,splits", [(1, 128, 64, 0), (64, 2304, 768, 0), (129, 1000, 1024, 2), (256, 1024, 3072, 0),
                                           (1, 128, 64, -1), (64, 2304, 768, -1), (129, 1000, 1024, -1),
-                                          (256, 1024, 3072, -1), (600, 384, 256, -1)])
+                                          (256, 1024, 3072, -1), (600, 384, 256, -1), (256, 1024, 2048, -16),
+                                          (129, 1000, 1024, -32), (300, 2048, 512, -256)])
 def test_gemm_16bit_matches_fp32_reference(dtype, M, N, K, splits):
     rng = np.random.default_rng(M + N + K)
     A = rng.standard_normal((M, K)).astype(np.float32)
