@@ -1575,11 +1575,25 @@ extern "C" int llm_memory_bytes(llm_ctx* c, uint64_t* weights, uint64_t* kv_pool
   return LLM_OK;
 }
 
+// Writes gen_pos0[i] + offset into d_pos (the generate loop's position state) and waits.
+int set_gen_positions(llm_ctx* c, int offset) {
+  int32_t* h = c->h_pin;
+  for (int i = 0; i < c->gen_n; ++i) h[i] = c->gen_pos0[i] + offset;
+  CU(cudaMemcpyAsync(c->d_pos, h, c->gen_n * 4, cudaMemcpyHostToDevice, c->stream));
+  CU(cudaStreamSynchronize(c->stream));
+  return LLM_OK;
+}
+
 extern "C" int llm_time_attention(llm_ctx* c, int iters, double* us_per_launch, double* bytes_per_launch) {
   RC(check_ready(c));
   if (c->gen_n <= 0) return fail(LLM_ERR_STATE, "llm_generate_begin not called");
+  if (c->gen_steps_done <= 0) return fail(LLM_ERR_STATE, "no generate step has run yet");
   if (iters <= 0) return fail(LLM_ERR_INVALID, "iters must be positive");
   RC(set_device(c));
+  // Time the attention of the last executed step: its positions (pos0 + done - 1) have their
+  // K/V written and their pages reserved.  d_pos (the next position) is restored afterwards.
+  CU(cudaStreamSynchronize(c->stream));
+  RC(set_gen_positions(c, c->gen_steps_done - 1));
   const llm_model_config& k = c->cfg;
   AttnParams ap{};
   ap.q = c->qbuf;
@@ -1619,14 +1633,15 @@ extern "C" int llm_time_attention(llm_ctx* c, int iters, double* us_per_launch, 
   CU(cudaEventElapsedTime(&ms, e0, e1));
   cudaEventDestroy(e0);
   cudaEventDestroy(e1);
+  RC(set_gen_positions(c, c->gen_steps_done));
   const double launches = static_cast<double>(iters) * k.n_layers;
   if (us_per_launch) *us_per_launch = ms * 1e3 / launches;
   if (bytes_per_launch) {
-    // K and V of every cached position of the context (positions pos0 + steps_done,
+    // K and V of every cached position of the context (positions 0 .. pos0 + done - 1,
     // inclusive), the q rows read and the attention rows written
     double b = 0;
     const double per_tok = 2.0 * c->kv_dim * act_bytes(c);
-    for (int i = 0; i < c->gen_n; ++i) b += per_tok * (c->gen_pos0[i] + c->gen_steps_done + 1);
+    for (int i = 0; i < c->gen_n; ++i) b += per_tok * (c->gen_pos0[i] + c->gen_steps_done);
     b += static_cast<double>(c->gen_n) * c->q_dim * act_bytes(c);
     b += static_cast<double>(c->gen_n) * c->q_dim * (c->in8 ? 4.0 : static_cast<double>(act_bytes(c)));
     *bytes_per_launch = b;
@@ -1637,9 +1652,12 @@ extern "C" int llm_time_attention(llm_ctx* c, int iters, double* us_per_launch, 
 extern "C" int llm_profile_step(llm_ctx* c, int iters, char* report, size_t report_len, double* step_us) {
   RC(check_ready(c));
   if (c->gen_n <= 0) return fail(LLM_ERR_STATE, "llm_generate_begin not called");
+  if (c->gen_steps_done >= c->gen_max_steps)
+    return fail(LLM_ERR_STATE, "no reserved generate step left to profile (reserve one more in llm_generate_begin)");
   if (iters <= 0) return fail(LLM_ERR_INVALID, "iters must be positive");
   RC(set_device(c));
-  // eager launches with an event after each one; tokens/positions are not advanced
+  // Eager launches of the next step (its position is reserved; the K/V it writes there are
+  // rewritten by the real step), with an event after each one; tokens/positions are not advanced.
   RowsSpec rs;
   rs.R = c->gen_n;
   rs.n_blocks = c->gen_n;

@@ -177,13 +177,15 @@ int llm_step_kernel_count(llm_ctx *ctx, int n, int *count);
 /* Device bytes held by the context (weights, KV pool, buffers, workspace). */
 int llm_memory_bytes(llm_ctx *ctx, uint64_t *weights, uint64_t *kv_pool, uint64_t *other);
 /* Time `iters` back-to-back launches of the attention kernel of every layer for the
- * current generate batch (after llm_generate_begin) with CUDA events on the context
- * stream; returns the mean duration of one launch in microseconds and the algorithmic
- * bytes one launch reads and writes. */
+ * current generate batch at the positions of its last executed step (at least one
+ * llm_generate_steps step must have run) with CUDA events on the context stream; returns
+ * the mean duration of one launch in microseconds and the algorithmic bytes one launch
+ * reads and writes.  The generate state is left as it was. */
 int llm_time_attention(llm_ctx *ctx, int iters, double *us_per_launch, double *bytes_per_launch);
 
 /* Run `iters` decode steps of the current generate batch eagerly with a CUDA event after
- * every launch (tokens and positions are not advanced) and write a per-kernel table
+ * every launch (tokens and positions are not advanced; the next step must still be within
+ * the steps reserved by llm_generate_begin, since it writes K/V there) and write a per-kernel table
  * (count per step, us per launch, us per step, share) into report.  step_us receives the
  * eager step time (launch gaps included). */
 int llm_profile_step(llm_ctx *ctx, int iters, char *report, size_t report_len, double *step_us);
