@@ -44,13 +44,20 @@ EXPORTS = [
     "llm_seq_release", "llm_prefill", "llm_decode_step", "llm_generate_begin",
     "llm_generate_steps", "llm_generate_end", "llm_generate", "llm_stories_decode",
     "llm_stories_decode_batch", "llm_ctx_stream", "llm_synchronize", "llm_step_kernel_count",
-    "llm_memory_bytes", "llm_time_attention", "llm_profile_step", "llm_debug_norm_quant", "llm_debug_gemm_i8",
+    "llm_memory_bytes", "llm_time_attention", "llm_profile_step", "llm_trace_step", "llm_debug_norm_quant", "llm_debug_gemm_i8",
     "llm_debug_gemm_f16", "llm_debug_read_kv", "llm_gemm_i8_splitk_noalloc", "llm_set_option",
 ]
 
 LLM_OPT_CUDA_GRAPHS = 1
 LLM_OPT_TCGEN05_GEMM = 2
 LLM_OPT_PDL = 3
+LLM_OPT_OVERLAP = 4
+LLM_OPT_OVERLAP_RING_KB = 5
+LLM_OPT_ATTN_SPLITS = 6
+LLM_OPT_ATTN_CHAIN = 7
+LLM_OPT_MICRO_BATCHES = 8
+LLM_OPT_OVERLAP_GRAPHS = 9
+LLM_OPT_CHAIN_PDL = 10
 
 
 class LLMError(RuntimeError):
@@ -116,6 +123,7 @@ def lib() -> C.CDLL:
         "llm_memory_bytes": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
         "llm_time_attention": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
         "llm_profile_step": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.c_size_t, C.POINTER(C.c_double)]),
+        "llm_trace_step": (C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t, C.POINTER(C.c_double)]),
         "llm_debug_norm_quant": (C.c_int, [C.c_int, _FP, _FP, C.c_int, C.c_int, C.c_double, C.POINTER(C.c_int8), _FP]),
         "llm_debug_gemm_i8": (C.c_int, [C.c_int, C.POINTER(C.c_int8), C.POINTER(C.c_int8), C.c_int, C.c_int, C.c_int, C.c_int, i32p]),
         "llm_debug_gemm_f16": (C.c_int, [C.c_int, C.c_int, _FP, _FP, C.c_int, C.c_int, C.c_int, C.c_int, _FP]),

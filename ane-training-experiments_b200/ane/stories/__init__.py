@@ -373,6 +373,13 @@ class Engine:
         _abi.check(_abi.lib().llm_profile_step(self.h, iters, buf, len(buf), C.byref(us)))
         return buf.value.decode(), us.value
 
+    def trace_step(self):
+        """Launch timeline (device globaltimer) of the next decode step of the generate batch."""
+        buf = C.create_string_buffer(1 << 17)
+        us = C.c_double()
+        _abi.check(_abi.lib().llm_trace_step(self.h, buf, len(buf), C.byref(us)))
+        return buf.value.decode(), us.value
+
     def read_kv(self, layer: int, seq: int, pos: int):
         k = np.zeros(self.cfg.kv_dim, np.float32)
         v = np.zeros(self.cfg.kv_dim, np.float32)

@@ -48,6 +48,7 @@ struct AttnParams {
   float* q8_scale;            // [rows]
   int* row_counters;          // [rows]
   int* err;
+  TraceRec* trace;            // llm_trace_step
 };
 
 constexpr int kAttnWarps = 4;
@@ -133,6 +134,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(AttnParams p) {
   __shared__ float s_wmax[kAttnWarps];
 
   griddep_launch_dependents();
+  trace_start(p.trace);
   griddep_wait();
   const int blk = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -371,6 +373,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(AttnParams p) {
   }
   if (!multi) {
     attn_quant_rows<HD>(p, r0, nq, group, s_rowlast, s_wmax);
+    trace_end(p.trace);
     return;
   }
   __threadfence();
@@ -380,7 +383,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(AttnParams p) {
     s_last = prev == p.splits - 1;
   }
   __syncthreads();
-  if (!s_last) return;
+  if (!s_last) {
+    trace_end(p.trace);
+    return;
+  }
   __threadfence();
   const float* base = p.ws + (static_cast<size_t>(blk) * p.n_kv_heads + kvh) * p.splits * 8 * (HD + 2);
   for (int i = threadIdx.x; i < ncols * HD; i += kAttnWarps * 32) {
@@ -403,6 +409,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(AttnParams p) {
   }
   if (threadIdx.x == 0) p.counters[blk * p.n_kv_heads + kvh] = 0;
   attn_quant_rows<HD>(p, r0, nq, group, s_rowlast, s_wmax);
+  trace_end(p.trace);
 }
 
 }  // namespace llm

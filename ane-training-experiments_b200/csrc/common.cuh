@@ -149,6 +149,31 @@ __device__ __forceinline__ void griddep_launch_dependents() {
 }
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 
+// Launch timeline record (llm_trace_step): globaltimer nanoseconds of the first and the last
+// CTA start and of the last CTA end, and the number of CTAs that finished.  Thread 0 of each
+// CTA records; a null pointer records nothing.
+struct TraceRec {
+  unsigned long long first_start, last_start, last_end, ctas;
+};
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void trace_start(TraceRec* r) {
+  if (r != nullptr && threadIdx.x == 0) {
+    const unsigned long long t = global_ns();
+    atomicMin(&r->first_start, t);
+    atomicMax(&r->last_start, t);
+  }
+}
+__device__ __forceinline__ void trace_end(TraceRec* r) {
+  if (r != nullptr && threadIdx.x == 0) {
+    atomicMax(&r->last_end, global_ns());
+    atomicAdd(&r->ctas, 1ull);
+  }
+}
+
 // ----------------------------------------------------------------------------- misc
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll

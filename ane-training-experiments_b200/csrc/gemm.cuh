@@ -62,6 +62,10 @@ struct GemmParams {
   float* logits;                    // optional [M][ld_logits]
   int ld_logits;
   int* err;
+  // tcgen05 GEMM: stage-ring depth (0 = the kernel's maximum); fewer stages need less shared
+  // memory, which lets a GEMM CTA share an SM with an attention CTA
+  int stages;
+  TraceRec* trace;  // llm_trace_step (tcgen05 GEMM only)
 };
 
 template <typename InT> struct GemmAcc { using type = float; };

@@ -177,6 +177,13 @@ __global__ void f32_to_act_kernel(const float* src, T* dst, size_t n) {
 // Launch with programmatic stream serialisation (see griddep_* in common.cuh) unless the
 // calling context disabled it (llm_set_option LLM_OPT_PDL); the flag is per host thread.
 thread_local bool t_use_pdl = true;
+// Scheduling priority of the next launches (0 = the stream's own).  The overlapped decode
+// schedule raises it for the projection and row kernels so their CTAs are dispatched ahead of
+// the other micro-batch's pending attention CTAs.
+thread_local int t_prio = 0;
+// When set, the next launch records this event once all its CTAs have begun execution
+// (launch completion); the overlapped schedule chains the micro-batches' attention launches on it.
+thread_local cudaEvent_t t_lc_event = nullptr;
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
   cudaLaunchConfig_t cfg{};
@@ -184,11 +191,26 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[3];
+  int na = 0;
+  if (t_lc_event != nullptr) {
+    attr[na].id = cudaLaunchAttributeLaunchCompletionEvent;
+    attr[na].val.launchCompletionEvent.event = t_lc_event;
+    attr[na].val.launchCompletionEvent.flags = 0;
+    ++na;
+  }
+  if (t_use_pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (t_prio != 0) {
+    attr[na].id = cudaLaunchAttributePriority;
+    attr[na].val.priority = t_prio;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = t_use_pdl ? 1 : 0;
+  cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 template <typename InT, typename OutT, int BM, int EPI>
@@ -304,7 +326,7 @@ cudaError_t umma_launch_t(const CUtensorMap& tx, const CUtensorMap& tw, const Ge
   auto k = umma_gemm_kernel<InT, OutT, BN, EPI>;
   if (prepare) return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   (void)cudaGetLastError();  // launch errors below must be this launch's own
-  return launch_pdl(k, grid, dim3(kUmmaThreads), smem, s, tx, tw, p);
+  return launch_pdl(k, grid, dim3(kUmmaThreads), umma_smem_bytes_for<BN>(p.stages), s, tx, tw, p);
 }
 
 // Channel-tile widths each epilogue is built for (QKV: one head per tile; argmax: 256).
@@ -410,6 +432,12 @@ GemmPlan plan_gemm(int M, int N, int K, int esz, int n_sm, int force_splits, siz
 
 }  // namespace
 
+// Micro-batches of the overlapped decode schedule: at most kMaxParts, each >= 32 rows.
+constexpr int kMaxParts = 4;
+constexpr int kOverlapMinPartRows = 32;
+// Split-attention tile counters (device array length).
+constexpr int kCounters = 65536;
+
 // ============================================================================ context
 struct LayerW {
   void* wqkv = nullptr;  // [(q_dim + 2 kv_dim) x D]
@@ -491,8 +519,25 @@ struct llm_ctx {
   // programmatic dependent launch between the step's kernels: off by default, it measured
   // 2% slower on the Qwen3 W8A8 decode step (9.47 vs 9.28 ms at 256 sequences)
   bool use_pdl = false;
-  // cluster split-K of the residual projections: correct, but its DSMEM reduction measured
-  // ~5x slower than the unsplit kernel (27.7 vs 4.0 us for Wo), so it is off by default
+  // Overlapped decode: the batch runs as two micro-batches on two streams whose attention
+  // launches alternate, so one micro-batch's projections and row kernels (latency-bound)
+  // run while the other's attention (HBM-bound) streams the KV cache.
+  bool overlap = true;
+  int overlap_ring_kb = 100;  // tcgen05 stage ring in overlap mode: fits beside an attention CTA
+  int attn_splits = 0;        // decode attention splits per sequence (0 = chosen per batch)
+  // how one micro-batch's attention launch waits for the other's: 0 = its completion,
+  // 1 = all of its CTAs having started (launch-completion event)
+  int attn_chain = 1;
+  // llm_trace_step: per-launch timeline records (device) and their labels (host)
+  bool tracing = false;
+  TraceRec* d_trace = nullptr;
+  std::vector<std::string> trace_labels;
+  int micro_batches = 4;      // micro-batches of the overlapped schedule (2..kMaxParts)
+  bool overlap_graphs = false;  // capture overlapped steps in CUDA graphs (eager launches measured faster)
+  bool chain_pdl = false;       // overlap mode: programmatic dependent launch within projection chains
+  cudaStream_t xstream[3] = {nullptr, nullptr, nullptr};  // micro-batches 1.. (0 runs on `stream`)
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr, ev_att[4] = {nullptr, nullptr, nullptr, nullptr};
+  int prio_hi = 0;  // greatest stream priority of the device
   std::map<std::tuple<const void*, int, int, int, int>, CUtensorMap> tmaps;
 
   // llm_profile_step: when non-null, enqueue_forward records an event after each launch
@@ -602,6 +647,16 @@ extern "C" int llm_ctx_create(const llm_model_config* cfg, int dtype, int device
   c->n_sm = prop.multiProcessorCount;
   if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess)
     return bail(fail(LLM_ERR_CUDA, "stream create failed"));
+  for (cudaStream_t& xs : c->xstream)
+    if (cudaStreamCreateWithFlags(&xs, cudaStreamNonBlocking) != cudaSuccess)
+      return bail(fail(LLM_ERR_CUDA, "stream create failed"));
+  for (cudaEvent_t* e : {&c->ev_fork, &c->ev_join, &c->ev_att[0], &c->ev_att[1], &c->ev_att[2], &c->ev_att[3]})
+    if (cudaEventCreateWithFlags(e, cudaEventDisableTiming) != cudaSuccess)
+      return bail(fail(LLM_ERR_CUDA, "event create failed"));
+  {
+    int least = 0, greatest = 0;
+    if (cudaDeviceGetStreamPriorityRange(&least, &greatest) == cudaSuccess) c->prio_hi = greatest;
+  }
   // RoPE tables in float64, as ane/stories/infer.go:97-107
   const int half = k.head_dim / 2;
   std::vector<float> hc(static_cast<size_t>(k.max_seq) * half), hs(hc.size());
@@ -632,6 +687,12 @@ extern "C" int llm_ctx_destroy(llm_ctx* c) {
   for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
   for (void* p : c->allocs) cudaFree(p);
   if (c->h_pin) cudaFreeHost(c->h_pin);
+  for (cudaStream_t xs : c->xstream)
+    if (xs) cudaStreamSynchronize(xs);
+  for (cudaEvent_t e : {c->ev_fork, c->ev_join, c->ev_att[0], c->ev_att[1], c->ev_att[2], c->ev_att[3]})
+    if (e) cudaEventDestroy(e);
+  for (cudaStream_t xs : c->xstream)
+    if (xs) cudaStreamDestroy(xs);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
   return LLM_OK;
@@ -827,8 +888,8 @@ extern "C" int llm_kv_alloc(llm_ctx* c, int max_seqs, int max_pos, int page_toke
     RC(dalloc_t(c, p, R * 4, o));
   c->ws_floats = 16u << 20;  // 64 MB split-K / split-attention workspace
   RC(dalloc_t(c, &c->ws, c->ws_floats * 4, o));
-  RC(dalloc_t(c, &c->counters, 65536 * 4, o));
-  CU(cudaMemset(c->counters, 0, 65536 * 4));
+  RC(dalloc_t(c, &c->counters, kCounters * 4, o));
+  CU(cudaMemset(c->counters, 0, kCounters * 4));
   RC(dalloc_t(c, &c->row_counters, static_cast<size_t>(R) * 4, o));
   CU(cudaMemset(c->row_counters, 0, static_cast<size_t>(R) * 4));
   c->h_pin_ints = static_cast<size_t>(R) * 8;
@@ -897,6 +958,11 @@ int validate_row(llm_ctx* c, int seq, int tok, int pos) {
 }
 
 int attn_splits_for(const llm_ctx* c, int n_blocks, int max_ctx) {
+  if (c->attn_splits > 0) {  // fixed by llm_set_option, bounded by the pages and the workspace
+    int s = std::min(c->attn_splits, std::max(1, (max_ctx + 15) / 16));
+    while (s > 1 && static_cast<size_t>(n_blocks) * c->cfg.n_kv_heads * s * 8 * (c->cfg.head_dim + 2) > c->ws_floats / kMaxParts) --s;
+    return s;
+  }
   const int ctas = n_blocks * c->cfg.n_kv_heads;
   const int target = 2 * c->n_sm;
   if (ctas >= target) return 1;
@@ -904,8 +970,9 @@ int attn_splits_for(const llm_ctx* c, int n_blocks, int max_ctx) {
   int s = (target + ctas - 1) / ctas;
   s = std::min(s, std::max(1, pages / 4));
   s = std::min(s, 64);
-  const size_t need = static_cast<size_t>(n_blocks) * c->cfg.n_kv_heads * s * 8 * (c->cfg.head_dim + 2);
-  while (s > 1 && need > c->ws_floats) --s;
+  // the workspace is divided between the micro-batches of the overlapped schedule
+  auto need = [&](int sp) { return static_cast<size_t>(n_blocks) * c->cfg.n_kv_heads * sp * 8 * (c->cfg.head_dim + 2); };
+  while (s > 1 && need(s) > c->ws_floats / kMaxParts) --s;
   return std::max(1, s);
 }
 
@@ -934,11 +1001,14 @@ const CUtensorMap* tmap(llm_ctx* c, const void* ptr, int esz, int k, int rows, i
   return &c->tmaps.emplace(key, m).first->second;
 }
 
-int gemm(llm_ctx* c, bool in8, int epi, GemmParams p) {
+// ring_kb > 0: cap the tcgen05 stage ring at that many KB of shared memory.
+int gemm(llm_ctx* c, bool in8, int epi, GemmParams p, cudaStream_t stream = nullptr, int ring_kb = 0) {
+  if (!stream) stream = c->stream;
   const int esz = in8 ? 1 : 2;
   p.argmax_parts = (p.N + argmax_tile_width(c->use_umma) - 1) / argmax_tile_width(c->use_umma);
   if (c->use_umma) {
     const int bn = umma_bn_for(p.M, p.N, epi, c->cfg.head_dim, c->n_sm);
+    if (ring_kb > 0) p.stages = std::max(2, (ring_kb * 1024 - 1024) / ((kUmmaTokens + bn) * 128));
     const CUtensorMap* tx = tmap(c, p.A, esz, p.K, p.M, kUmmaTokens);
     const CUtensorMap* tw = tmap(c, p.B, esz, p.K, p.N, bn);
     if (!tw || !tx) return LLM_ERR_CUDA;
@@ -946,7 +1016,7 @@ int gemm(llm_ctx* c, bool in8, int epi, GemmParams p) {
     p.k_tiles_per_split = p.K * esz / 128;
     p.err = c->d_err;
     dim3 grid((p.M + kUmmaTokens - 1) / kUmmaTokens, (p.N + bn - 1) / bn, 1);
-    CU(umma_any(c->act, in8, *tx, *tw, p, epi, bn, grid, c->stream, false));
+    CU(umma_any(c->act, in8, *tx, *tw, p, epi, bn, grid, stream, false));
     return LLM_OK;
   }
   GemmPlan pl = plan_gemm(p.M, p.N, p.K, esz, c->n_sm, 0, c->ws_floats);
@@ -955,15 +1025,36 @@ int gemm(llm_ctx* c, bool in8, int epi, GemmParams p) {
   p.ws = c->ws;
   p.counters = c->counters;
   p.err = c->d_err;
-  CU(gemm_any(c->act, in8, p, epi, pl.bm, pl.grid, c->stream, false));
+  CU(gemm_any(c->act, in8, p, epi, pl.bm, pl.grid, stream, false));
   return LLM_OK;
 }
 
+// Rows [r0, r0 + n) of a forward pass, enqueued on stream s.  idx selects the half of the
+// split workspace a micro-batch's attention may use.
+struct Part {
+  int r0 = 0, n = 0, idx = 0;
+  cudaStream_t s = nullptr;
+};
+
+
+// Micro-batches a decode step over R rows runs as (1 = the single-stream schedule): up to
+// LLM_OPT_MICRO_BATCHES, each at least kOverlapMinPartRows rows.
+int overlap_parts(const llm_ctx* c, int R, bool decode_rows) {
+  if (!c->overlap || !c->use_umma || !decode_rows) return 1;
+  const int k = std::min(std::min(c->micro_batches, kMaxParts), R / kOverlapMinPartRows);
+  return k >= 2 ? k : 1;
+}
+bool overlap_applies(const llm_ctx* c, int R, bool decode_rows) { return overlap_parts(c, R, decode_rows) > 1; }
+// Launch timeline records one traced step may use.
+constexpr size_t kTraceCap = 1024;
+
 int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
   t_use_pdl = c->use_pdl;
+  t_prio = 0;
   const llm_model_config& k = c->cfg;
   const int R = rs.R, D = k.dim, F = k.hidden, Q = c->q_dim, KV = c->kv_dim;
   const bool i8 = c->in8;
+  const size_t ab = act_bytes(c);
   cudaStream_t s = c->stream;
   auto mark = [&](const char* name) -> int {
     if (!c->trace) return LLM_OK;
@@ -975,158 +1066,269 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
   };
   RC(mark("start"));
 
-  auto norm = [&](const float* x, const float* w, bool embed, int rows, const int* row_index, void* out_act, int8_t* q,
-                  float* sc) -> int {
-    NormParams np{};
-    np.x = x;
-    np.row_index = row_index;
-    np.embed = embed ? c->embed : nullptr;
-    np.tokens = c->d_tok;
-    np.x_out = c->x;
-    np.w = w;
-    np.D = D;
-    np.rows = rows;
-    np.eps = k.norm_eps;
-    np.out = out_act;
-    np.q = q;
-    np.scale = sc;
-    CU(norm_any(c->act, q != nullptr, np, s));
+  // Decode batches (one query row per attention block) split into micro-batches on their own
+  // streams whose attention launches form a chain: part 0 (layer l), part 1 (l), ..., part k-1
+  // (l), part 0 (l + 1), ...  Each attention launch may start once every CTA of the previous
+  // one in the chain has started, so consecutive attention launches fill each other's tail
+  // waves, and everything a micro-batch runs between two of its attention launches (Wo, norm,
+  // W1/W3, W2, norm, QKV: latency-bound) runs while the others' attention streams the KV
+  // cache.  The split workspace is divided between the micro-batches.
+  const bool decode_rows = rs.d_blk_row0 == nullptr && rs.n_blocks == R;
+  const int kparts = overlap_parts(c, R, decode_rows);
+  const bool overlap = kparts > 1 && !c->trace;
+  Part parts[kMaxParts];
+  int np = 1;
+  if (overlap) {
+    // near-equal parts of whole 16-row groups; the last part takes the remainder rows
+    const int units = R / 16;
+    int r0 = 0;
+    for (int h = 0; h < kparts; ++h) {
+      const int u = units / kparts + (h < units % kparts ? 1 : 0);
+      const int n = h == kparts - 1 ? R - r0 : 16 * u;
+      parts[h] = {r0, n, h, h == 0 ? c->stream : c->xstream[h - 1]};
+      r0 += n;
+    }
+    np = kparts;
+    CU(cudaEventRecord(c->ev_fork, c->stream));
+    for (int h = 1; h < np; ++h) CU(cudaStreamWaitEvent(parts[h].s, c->ev_fork, 0));
+  } else {
+    parts[0] = {0, R, 0, c->stream};
+  }
+  const int ring_kb = overlap ? c->overlap_ring_kb : 0;
+  const int prio = overlap ? c->prio_hi : 0;
+  // programmatic dependent launch inside a micro-batch's projection chain (not for attention)
+  const bool chain_pdl = c->use_pdl || (overlap && c->chain_pdl);
+  auto bytes = [](const void* base, size_t off) -> void* {
+    return const_cast<uint8_t*>(static_cast<const uint8_t*>(base)) + off;
+  };
+  // timeline record of the next launch (llm_trace_step), nullptr when not tracing
+  auto tr = [&](const char* name, int l, const Part& P) -> TraceRec* {
+    if (!c->tracing || c->trace_labels.size() >= kTraceCap) return nullptr;
+    char buf[64];
+    snprintf(buf, sizeof buf, "%s L%d %c", name, l, np > 1 ? "ABCD"[P.idx] : '-');
+    c->trace_labels.emplace_back(buf);
+    return c->d_trace + (c->trace_labels.size() - 1);
+  };
+
+  auto norm = [&](const Part& P, const float* x, const float* w, bool embed, void* out_act, int8_t* q, float* sc,
+                  TraceRec* trace) -> int {
+    NormParams np_{};
+    np_.trace = trace;
+    np_.x = x ? x + static_cast<size_t>(P.r0) * D : nullptr;
+    np_.row_index = nullptr;
+    np_.embed = embed ? c->embed : nullptr;
+    np_.tokens = c->d_tok + P.r0;
+    np_.x_out = c->x + static_cast<size_t>(P.r0) * D;
+    np_.w = w;
+    np_.D = D;
+    np_.rows = P.n;
+    np_.eps = k.norm_eps;
+    np_.out = out_act ? bytes(out_act, static_cast<size_t>(P.r0) * D * ab) : nullptr;
+    np_.q = q ? q + static_cast<size_t>(P.r0) * D : nullptr;
+    np_.scale = sc ? sc + P.r0 : nullptr;
+    t_prio = prio;
+    t_use_pdl = chain_pdl;
+    CU(norm_any(c->act, q != nullptr, np_, P.s));
     return LLM_OK;
   };
-  auto quant_rows = [&](const float* x, int cols, int8_t* q, float* sc) -> int {
-    NormParams np{};
-    np.x = x;
-    np.w = nullptr;
-    np.D = cols;
-    np.rows = R;
-    np.q = q;
-    np.scale = sc;
-    CU(norm_any(c->act, true, np, s));
+  // attention-side norm input of layer l for part P (the residual stream x)
+  auto norm_in = [&](const Part& P, const float* w, bool embed, int l) -> int {
+    return norm(P, embed ? nullptr : c->x, w, embed, i8 ? nullptr : c->xn, i8 ? c->xq : nullptr, c->xs,
+                tr(embed ? "embed+norm" : "norm(att)", l, P));
+  };
+
+  auto qkv = [&](const Part& P, int l) -> int {
+    const LayerW& L = c->layers[l];
+    GemmParams p{};
+    p.A = i8 ? bytes(c->xq, static_cast<size_t>(P.r0) * D) : bytes(c->xn, static_cast<size_t>(P.r0) * D * ab);
+    p.B = L.wqkv;
+    p.M = P.n;
+    p.N = Q + 2 * KV;
+    p.K = D;
+    p.a_scale = c->xs + P.r0;
+    p.b_scale = L.sqkv;
+    p.q_out = bytes(c->qbuf, static_cast<size_t>(P.r0) * Q * ab);
+    p.kv_pool = c->kv_pool;
+    p.block_table = c->d_block_table;
+    p.seq_ids = c->d_seq + P.r0;
+    p.positions = c->d_pos + P.r0;
+    p.q_norm = L.q_norm;
+    p.k_norm = L.k_norm;
+    p.rope_cos = c->rope_cos;
+    p.rope_sin = c->rope_sin;
+    p.layer = l;
+    p.n_pages = c->n_pages;
+    p.max_pages_per_seq = c->max_pages_per_seq;
+    p.n_heads = k.n_heads;
+    p.n_kv_heads = k.n_kv_heads;
+    p.head_dim = k.head_dim;
+    p.qk_norm = k.qk_norm;
+    p.eps = k.norm_eps;
+    p.trace = tr("qkv", l, P);
+    t_prio = prio;
+    t_use_pdl = chain_pdl;
+    return gemm(c, i8, EPI_QKV, p, P.s, ring_kb);
+  };
+
+  auto attention = [&](const Part& P, int l) -> int {
+    AttnParams ap{};
+    ap.q = bytes(c->qbuf, static_cast<size_t>(P.r0) * Q * ab);
+    ap.kv_pool = c->kv_pool;
+    ap.block_table = c->d_block_table;
+    ap.max_pages_per_seq = c->max_pages_per_seq;
+    ap.seq_ids = c->d_seq + P.r0;
+    ap.positions = c->d_pos + P.r0;
+    ap.blk_row0 = rs.d_blk_row0;
+    ap.blk_nq = rs.d_blk_nq;
+    ap.n_blocks = overlap ? P.n : rs.n_blocks;
+    ap.n_heads = k.n_heads;
+    ap.n_kv_heads = k.n_kv_heads;
+    ap.layer = l;
+    ap.n_pages = c->n_pages;
+    ap.splits = rs.attn_splits;
+    ap.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(k.head_dim)));
+    ap.out = bytes(c->attn, static_cast<size_t>(P.r0) * Q * (i8 ? 4 : ab));
+    ap.out_f32 = i8 ? 1 : 0;
+    ap.ws = c->ws + P.idx * (c->ws_floats / kMaxParts);
+    ap.counters = c->counters + P.idx * (kCounters / kMaxParts);
+    ap.err = c->d_err;
+    ap.trace = tr("attention", l, P);
+    if (i8) {  // per-token quantisation of the output fused into the attention kernel
+      ap.q8 = c->aq + static_cast<size_t>(P.r0) * Q;
+      ap.q8_scale = c->as + P.r0;
+      ap.row_counters = c->row_counters + P.r0;
+    }
+    t_prio = 0;
+    t_use_pdl = c->use_pdl;
+    // overlapped schedule: this launch's "all CTAs started" event gates the other micro-batch's
+    // next attention launch, which then fills the tail wave of this one
+    t_lc_event = overlap && c->attn_chain == 1 ? c->ev_att[P.idx] : nullptr;
+    const cudaError_t e = attn_any(c->act, k.head_dim, ap, P.s, false);
+    t_lc_event = nullptr;
+    CU(e);
     return LLM_OK;
   };
 
-  // layer 0 attention norm fused with the embedding gather
-  RC(norm(nullptr, c->layers[0].rms_att, true, R, nullptr, i8 ? nullptr : c->xn, i8 ? c->xq : nullptr, c->xs));
-  RC(mark("embed+norm"));
-  for (int l = 0; l < k.n_layers; ++l) {
+  // Wo + residual, FFN norm, W1/W3 + SiLU gate (+ quantiser), W2 + residual, next layer's norm
+  auto post_attention = [&](const Part& P, int l) -> int {
     const LayerW& L = c->layers[l];
-    {  // QKV + QK-norm + RoPE + paged KV write
-      GemmParams p{};
-      p.A = i8 ? static_cast<const void*>(c->xq) : c->xn;
-      p.B = L.wqkv;
-      p.M = R;
-      p.N = Q + 2 * KV;
-      p.K = D;
-      p.a_scale = c->xs;
-      p.b_scale = L.sqkv;
-      p.q_out = c->qbuf;
-      p.kv_pool = c->kv_pool;
-      p.block_table = c->d_block_table;
-      p.seq_ids = c->d_seq;
-      p.positions = c->d_pos;
-      p.q_norm = L.q_norm;
-      p.k_norm = L.k_norm;
-      p.rope_cos = c->rope_cos;
-      p.rope_sin = c->rope_sin;
-      p.layer = l;
-      p.n_pages = c->n_pages;
-      p.max_pages_per_seq = c->max_pages_per_seq;
-      p.n_heads = k.n_heads;
-      p.n_kv_heads = k.n_kv_heads;
-      p.head_dim = k.head_dim;
-      p.qk_norm = k.qk_norm;
-      p.eps = k.norm_eps;
-      RC(gemm(c, i8, EPI_QKV, p));
-      RC(mark("qkv_gemm+rope+kv_write"));
-    }
-    {  // attention over the paged cache
-      AttnParams ap{};
-      ap.q = c->qbuf;
-      ap.kv_pool = c->kv_pool;
-      ap.block_table = c->d_block_table;
-      ap.max_pages_per_seq = c->max_pages_per_seq;
-      ap.seq_ids = c->d_seq;
-      ap.positions = c->d_pos;
-      ap.blk_row0 = rs.d_blk_row0;
-      ap.blk_nq = rs.d_blk_nq;
-      ap.n_blocks = rs.n_blocks;
-      ap.n_heads = k.n_heads;
-      ap.n_kv_heads = k.n_kv_heads;
-      ap.layer = l;
-      ap.n_pages = c->n_pages;
-      ap.splits = rs.attn_splits;
-      ap.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(k.head_dim)));
-      ap.out = c->attn;
-      ap.out_f32 = i8 ? 1 : 0;
-      ap.ws = c->ws;
-      ap.counters = c->counters;
-      ap.err = c->d_err;
-      if (i8) {  // per-token quantisation of the output fused into the attention kernel
-        ap.q8 = c->aq;
-        ap.q8_scale = c->as;
-        ap.row_counters = c->row_counters;
-      }
-      CU(attn_any(c->act, k.head_dim, ap, s, false));
-      RC(mark(i8 ? "attention+quant" : "attention"));
-    }
     {  // Wo + residual
       GemmParams p{};
-      p.A = i8 ? static_cast<const void*>(c->aq) : c->attn;
+      p.A = i8 ? bytes(c->aq, static_cast<size_t>(P.r0) * Q) : bytes(c->attn, static_cast<size_t>(P.r0) * Q * ab);
       p.B = L.wo;
-      p.M = R;
+      p.M = P.n;
       p.N = D;
       p.K = Q;
-      p.a_scale = c->as;
+      p.a_scale = c->as + P.r0;
       p.b_scale = L.so;
-      p.out = c->x;
-      p.resid = c->x;
+      p.out = c->x + static_cast<size_t>(P.r0) * D;
+      p.resid = c->x + static_cast<size_t>(P.r0) * D;
       p.ldo = D;
-      RC(gemm(c, i8, EPI_RESID, p));
+      p.trace = tr("wo", l, P);
+      t_prio = prio;
+      t_use_pdl = chain_pdl;
+      RC(gemm(c, i8, EPI_RESID, p, P.s, ring_kb));
       RC(mark("wo_gemm+resid"));
     }
-    RC(norm(c->x, L.rms_ffn, false, R, nullptr, i8 ? nullptr : c->xn, i8 ? c->xq : nullptr, c->xs));
+    RC(norm(P, c->x, L.rms_ffn, false, i8 ? nullptr : c->xn, i8 ? c->xq : nullptr, c->xs, tr("norm(ffn)", l, P)));
     RC(mark("norm"));
     {  // W1/W3 + SiLU gate
       GemmParams p{};
-      p.A = i8 ? static_cast<const void*>(c->xq) : c->xn;
+      p.A = i8 ? bytes(c->xq, static_cast<size_t>(P.r0) * D) : bytes(c->xn, static_cast<size_t>(P.r0) * D * ab);
       p.B = L.w13;
-      p.M = R;
+      p.M = P.n;
       p.N = 2 * F;
       p.K = D;
-      p.a_scale = c->xs;
+      p.a_scale = c->xs + P.r0;
       p.b_scale = L.s13;
-      p.out = c->gbuf;
+      p.out = bytes(c->gbuf, static_cast<size_t>(P.r0) * F * (i8 ? 4 : ab));
       p.swiglu_f32 = i8 ? 1 : 0;
-      RC(gemm(c, i8, EPI_SWIGLU, p));
+      p.trace = tr("w13", l, P);
+      t_prio = prio;
+      t_use_pdl = chain_pdl;
+      RC(gemm(c, i8, EPI_SWIGLU, p, P.s, ring_kb));
       RC(mark("w13_gemm+swiglu"));
     }
-    if (i8) {
-      RC(quant_rows(static_cast<const float*>(c->gbuf), F, c->gq, c->gs));
+    if (i8) {  // per-token quantisation of the SwiGLU output
+      NormParams np_{};
+      np_.x = static_cast<const float*>(c->gbuf) + static_cast<size_t>(P.r0) * F;
+      np_.w = nullptr;
+      np_.D = F;
+      np_.rows = P.n;
+      np_.q = c->gq + static_cast<size_t>(P.r0) * F;
+      np_.scale = c->gs + P.r0;
+      np_.trace = tr("quant(g)", l, P);
+      t_prio = prio;
+      t_use_pdl = chain_pdl;
+      CU(norm_any(c->act, true, np_, P.s));
       RC(mark("quant(g)"));
     }
     {  // W2 + residual
       GemmParams p{};
-      p.A = i8 ? static_cast<const void*>(c->gq) : c->gbuf;
+      p.A = i8 ? bytes(c->gq, static_cast<size_t>(P.r0) * F) : bytes(c->gbuf, static_cast<size_t>(P.r0) * F * ab);
       p.B = L.w2;
-      p.M = R;
+      p.M = P.n;
       p.N = D;
       p.K = F;
-      p.a_scale = c->gs;
+      p.a_scale = c->gs + P.r0;
       p.b_scale = L.s2;
-      p.out = c->x;
-      p.resid = c->x;
+      p.out = c->x + static_cast<size_t>(P.r0) * D;
+      p.resid = c->x + static_cast<size_t>(P.r0) * D;
       p.ldo = D;
-      RC(gemm(c, i8, EPI_RESID, p));
+      p.trace = tr("w2", l, P);
+      t_prio = prio;
+      t_use_pdl = chain_pdl;
+      RC(gemm(c, i8, EPI_RESID, p, P.s, ring_kb));
       RC(mark("w2_gemm+resid"));
     }
     if (l + 1 < k.n_layers) {
-      RC(norm(c->x, c->layers[l + 1].rms_att, false, R, nullptr, i8 ? nullptr : c->xn, i8 ? c->xq : nullptr, c->xs));
+      RC(norm_in(P, c->layers[l + 1].rms_att, false, l + 1));
       RC(mark("norm"));
     }
+    return LLM_OK;
+  };
+
+  // layer 0 attention norm fused with the embedding gather
+  for (int h = 0; h < np; ++h) RC(norm_in(parts[h], c->layers[0].rms_att, true, 0));
+  RC(mark("embed+norm"));
+  for (int l = 0; l < k.n_layers; ++l) {
+    for (int h = 0; h < np; ++h) {
+      const Part& P = parts[h];
+      if (l == 0 || !overlap) RC(qkv(P, l));  // later layers: enqueued by post_attention's tail below
+      RC(mark("qkv_gemm+rope+kv_write"));
+      if (overlap && (h > 0 || l > 0))  // chain: after the previous part's attention launch
+        CU(cudaStreamWaitEvent(P.s, c->ev_att[(h + np - 1) % np], 0));
+      RC(attention(P, l));
+      RC(mark(i8 ? "attention+quant" : "attention"));
+      if (overlap && c->attn_chain == 0) CU(cudaEventRecord(c->ev_att[h], P.s));
+    }
+    for (int h = 0; h < np; ++h) {
+      RC(post_attention(parts[h], l));
+      if (overlap && l + 1 < k.n_layers) RC(qkv(parts[h], l + 1));
+    }
+  }
+  t_prio = 0;
+  t_use_pdl = c->use_pdl;
+  for (int h = 1; h < np; ++h) {
+    CU(cudaEventRecord(c->ev_join, parts[h].s));
+    CU(cudaStreamWaitEvent(c->stream, c->ev_join, 0));
   }
   // final norm on the rows whose next token is wanted, tied/untied lm_head + argmax
   const int NF = rs.d_final ? rs.n_final : R;
-  RC(norm(c->x, c->rms_final, false, NF, rs.d_final, c->xf, nullptr, nullptr));
+  {
+    NormParams np_{};
+    np_.x = c->x;
+    np_.row_index = rs.d_final;
+    np_.tokens = c->d_tok;
+    np_.x_out = c->x;
+    np_.w = c->rms_final;
+    np_.D = D;
+    np_.rows = NF;
+    np_.eps = k.norm_eps;
+    np_.out = c->xf;
+    np_.trace = tr("final_norm", k.n_layers, parts[0]);
+    CU(norm_any(c->act, false, np_, s));
+  }
   RC(mark("final_norm"));
   {
     GemmParams p{};
@@ -1138,6 +1340,7 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
     p.argmax_part = c->argmax_part;
     p.logits = rs.d_logits;
     p.ld_logits = k.vocab;
+    p.trace = tr("lm_head", k.n_layers, parts[0]);
     RC(gemm(c, false, EPI_ARGMAX, p));
     RC(mark("lm_head+argmax"));
   }
@@ -1185,7 +1388,9 @@ int run_step(llm_ctx* c, int n, int splits, int mode) {
     rs.gen_out = c->d_gen_out;
     rs.gen_cap = c->gen_max_steps;
   }
-  if (!c->use_graphs) return enqueue_forward(c, rs);
+  // overlapped micro-batch steps launch eagerly unless LLM_OPT_OVERLAP_GRAPHS: their
+  // cross-stream schedule measured faster from eager launches than from a replayed graph
+  if (!c->use_graphs || (overlap_applies(c, n, true) && !c->overlap_graphs)) return enqueue_forward(c, rs);
   GraphKey key{n, splits, mode};
   auto it = c->graphs.find(key);
   if (it == c->graphs.end()) {
@@ -1531,6 +1736,43 @@ extern "C" int llm_set_option(llm_ctx* c, int option, int value) {
     case LLM_OPT_CUDA_GRAPHS: flag = &c->use_graphs; break;
     case LLM_OPT_TCGEN05_GEMM: flag = &c->use_umma; break;
     case LLM_OPT_PDL: flag = &c->use_pdl; break;
+    case LLM_OPT_OVERLAP: flag = &c->overlap; break;
+    case LLM_OPT_OVERLAP_GRAPHS: flag = &c->overlap_graphs; break;
+    case LLM_OPT_CHAIN_PDL: flag = &c->chain_pdl; break;
+    case LLM_OPT_ATTN_CHAIN:
+      if (value < 0 || value > 1) return fail(LLM_ERR_INVALID, "attention chain mode %d out of range [0, 1]", value);
+      if (c->attn_chain != value) {
+        RC(set_device(c));
+        CU(cudaStreamSynchronize(c->stream));
+        for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
+        c->graphs.clear();
+        c->attn_chain = value;
+      }
+      return LLM_OK;
+    case LLM_OPT_MICRO_BATCHES:
+      if (value < 2 || value > kMaxParts) return fail(LLM_ERR_INVALID, "micro-batches %d out of range [2, %d]", value, kMaxParts);
+      if (c->micro_batches != value) {
+        RC(set_device(c));
+        CU(cudaStreamSynchronize(c->stream));
+        for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
+        c->graphs.clear();
+        c->micro_batches = value;
+      }
+      return LLM_OK;
+    case LLM_OPT_ATTN_SPLITS:
+      if (value < 0 || value > 64) return fail(LLM_ERR_INVALID, "attention splits %d out of range [0, 64]", value);
+      c->attn_splits = value;  // applies from the next llm_generate_begin / step
+      return LLM_OK;
+    case LLM_OPT_OVERLAP_RING_KB:
+      if (value < 16 || value > 200) return fail(LLM_ERR_INVALID, "ring size %d KB out of range [16, 200]", value);
+      if (c->overlap_ring_kb != value) {
+        RC(set_device(c));
+        CU(cudaStreamSynchronize(c->stream));
+        for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
+        c->graphs.clear();
+        c->overlap_ring_kb = value;
+      }
+      return LLM_OK;
     default: return fail(LLM_ERR_INVALID, "unknown option %d", option);
   }
   if (*flag != (value != 0)) {
@@ -1561,9 +1803,11 @@ extern "C" int llm_step_kernel_count(llm_ctx* c, int n, int* count) {
   if (!c || !count) return fail(LLM_ERR_INVALID, "nil argument");
   // embed+norm, per layer: qkv, attention, wo, norm, w13, w2 (+ the SwiGLU quant kernel for int8)
   // + the next layer's norm, then final norm, lm_head, finish
+  // + the next layer's norm, then final norm, lm_head, finish; the overlapped schedule runs the
+  // per-row part once per micro-batch
   const int per_layer = 6 + (c->in8 ? 1 : 0);
-  *count = 1 + c->cfg.n_layers * per_layer + (c->cfg.n_layers - 1) + 3;
-  (void)n;
+  const int parts = overlap_parts(c, n, true);
+  *count = parts * (1 + c->cfg.n_layers * per_layer + (c->cfg.n_layers - 1)) + 3;
   return LLM_OK;
 }
 
@@ -1704,6 +1948,57 @@ extern "C" int llm_profile_step(llm_ctx* c, int iters, char* report, size_t repo
     report[n] = 0;
   }
   if (step_us) *step_us = total / iters;
+  return check_device_error(c);
+}
+
+extern "C" int llm_trace_step(llm_ctx* c, char* report, size_t report_len, double* step_us) {
+  RC(check_ready(c));
+  if (c->gen_n <= 0) return fail(LLM_ERR_STATE, "llm_generate_begin not called");
+  if (c->gen_steps_done >= c->gen_max_steps)
+    return fail(LLM_ERR_STATE, "no reserved generate step left to trace (reserve one more in llm_generate_begin)");
+  RC(set_device(c));
+  if (!c->d_trace) RC(dalloc_t(c, &c->d_trace, kTraceCap * sizeof(TraceRec), &c->bytes_other));
+  std::vector<TraceRec> h(kTraceCap);
+  for (auto& r : h) r = TraceRec{~0ull, 0ull, 0ull, 0ull};
+  CU(cudaStreamSynchronize(c->stream));
+  CU(cudaMemcpy(c->d_trace, h.data(), kTraceCap * sizeof(TraceRec), cudaMemcpyHostToDevice));
+  // The next step of the generate batch (its position is reserved), launched eagerly in the
+  // current schedule; tokens and positions are not advanced.
+  RowsSpec rs;
+  rs.R = c->gen_n;
+  rs.n_blocks = c->gen_n;
+  rs.attn_splits = c->gen_splits;
+  c->trace_labels.clear();
+  c->tracing = true;
+  int rc = enqueue_forward(c, rs);
+  c->tracing = false;
+  if (rc) return rc;
+  CU(cudaStreamSynchronize(c->stream));
+  CU(cudaMemcpy(h.data(), c->d_trace, kTraceCap * sizeof(TraceRec), cudaMemcpyDeviceToHost));
+  unsigned long long t0 = ~0ull, t1 = 0;
+  for (size_t i = 0; i < c->trace_labels.size(); ++i)
+    if (h[i].ctas) {
+      t0 = std::min(t0, h[i].first_start);
+      t1 = std::max(t1, h[i].last_end);
+    }
+  std::string out;
+  char line[160];
+  snprintf(line, sizeof line, "%-22s %10s %10s %10s %10s %6s\n", "launch", "start_us", "spread_us", "end_us", "dur_us", "ctas");
+  out += line;
+  for (size_t i = 0; i < c->trace_labels.size(); ++i) {
+    const TraceRec& r = h[i];
+    if (!r.ctas) continue;
+    snprintf(line, sizeof line, "%-22s %10.2f %10.2f %10.2f %10.2f %6llu\n", c->trace_labels[i].c_str(),
+             (r.first_start - t0) * 1e-3, (r.last_start - r.first_start) * 1e-3, (r.last_end - t0) * 1e-3,
+             (r.last_end - r.first_start) * 1e-3, r.ctas);
+    out += line;
+  }
+  if (report && report_len) {
+    const size_t n = std::min(report_len - 1, out.size());
+    memcpy(report, out.data(), n);
+    report[n] = 0;
+  }
+  if (step_us) *step_us = t1 > t0 ? (t1 - t0) * 1e-3 : 0.0;
   return check_device_error(c);
 }
 

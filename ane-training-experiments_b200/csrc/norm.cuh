@@ -24,6 +24,7 @@ struct NormParams {
   void* out;               // [rows][D] act type (when !QUANT)
   int8_t* q;               // [rows][D] (QUANT)
   float* scale;            // [rows]    (QUANT)
+  TraceRec* trace;         // llm_trace_step
 };
 
 // Convert 4 activation-type values to float.
@@ -48,6 +49,7 @@ __host__ __device__ constexpr int norm_threads(int D) { return D / (4 * norm_gro
 template <typename T, bool QUANT, int NV>
 __global__ void __launch_bounds__(1024) norm_rows_kernel(NormParams p) {
   griddep_launch_dependents();
+  trace_start(p.trace);
   griddep_wait();
   __shared__ double s_ss[32];
   __shared__ float s_mx[32];
@@ -143,6 +145,7 @@ __global__ void __launch_bounds__(1024) norm_rows_kernel(NormParams p) {
       *reinterpret_cast<char4*>(qo + 4 * t + 4 * nt * j) = c;
     }
   }
+  trace_end(p.trace);
 }
 
 // Weight conversion: fp32 rows -> act type (rounded) or int8 with per-row scales.

@@ -119,6 +119,11 @@ template <int BN>
 constexpr int umma_smem_bytes() {
   return umma_stages<BN>() * (kUmmaTokens + BN) * 128 + 1024;  // + alignment slack
 }
+// Dynamic shared memory of a launch with `stages` ring stages (0 = the maximum).
+template <int BN>
+constexpr int umma_smem_bytes_for(int stages) {
+  return (stages > 0 && stages < umma_stages<BN>() ? stages : umma_stages<BN>()) * (kUmmaTokens + BN) * 128 + 1024;
+}
 template <int BN>
 constexpr uint32_t umma_tmem_cols() {
   return BN < 32 ? 32u : static_cast<uint32_t>(BN);
@@ -135,7 +140,8 @@ template <typename InT, typename OutT, int BN, int EPI>
 __global__ void __launch_bounds__(kUmmaThreads, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, GemmParams p) {
   constexpr bool I8 = sizeof(InT) == 1;
-  constexpr int STAGES = umma_stages<BN>();
+  constexpr int MAX_STAGES = umma_stages<BN>();
+  const int STAGES = p.stages > 0 && p.stages < MAX_STAGES ? p.stages : MAX_STAGES;
   constexpr int A_BYTES = kUmmaTokens * 128;
   constexpr int B_BYTES = BN * 128;
   constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -145,7 +151,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   constexpr int NCH = (BN + 31) / 32;  // 32-column chunks of the accumulator
 
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES], accum_bar;
+  __shared__ __align__(8) uint64_t full_bar[MAX_STAGES], empty_bar[MAX_STAGES], accum_bar;
   __shared__ uint32_t s_tmem;
   __shared__ float s_bsc[BN];   // per-channel weight scales (int8)
   __shared__ float s_nw[BN];    // QK-norm weights of this tile's head
@@ -156,6 +162,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
   const int nkt = p.K * ESZ / 128;
 
   griddep_launch_dependents();
+  trace_start(p.trace);
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(smem_u32(&full_bar[s]), 1);
@@ -481,6 +488,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
   }
+  trace_end(p.trace);
 }
 
 }  // namespace llm

@@ -163,6 +163,20 @@ int llm_stories_decode_batch(llm_ctx *ctx, const int32_t *prompts, const int32_t
 #define LLM_OPT_CUDA_GRAPHS 1  /* replay each decode step as a captured CUDA graph (default 1)   */
 #define LLM_OPT_TCGEN05_GEMM 2 /* tcgen05 projections (default 1); 0 = warp-level mma.sync ones   */
 #define LLM_OPT_PDL 3          /* programmatic dependent launch between step kernels (default 0) */
+#define LLM_OPT_OVERLAP 4      /* decode batches of >= 64 sequences run as micro-batches (of >= 32
+                                  sequences, at most LLM_OPT_MICRO_BATCHES) on their own streams
+                                  whose attention launches form a chain, overlapping one
+                                  micro-batch's projections with the others' attention (default 1) */
+#define LLM_OPT_OVERLAP_RING_KB 5 /* shared memory (KB) of a projection's stage ring in overlap
+                                     mode, so it fits beside an attention CTA (default 100)     */
+#define LLM_OPT_ATTN_SPLITS 6  /* decode attention splits per sequence; 0 = chosen per batch (default) */
+#define LLM_OPT_MICRO_BATCHES 8 /* most micro-batches of the overlapped schedule, 2..4 (default 4)  */
+#define LLM_OPT_OVERLAP_GRAPHS 9 /* capture overlapped steps in CUDA graphs (default 0: eager launches,
+                                    measured faster for this schedule)                          */
+#define LLM_OPT_CHAIN_PDL 10    /* overlap mode: programmatic dependent launch between the kernels of a
+                                    micro-batch's projection chain (attention excluded)        */
+#define LLM_OPT_ATTN_CHAIN 7   /* overlap mode: a micro-batch's attention launch starts once every CTA of
+                                  the other's has started (1, default) or once it completed (0)  */
 /* Set an execution option (value 0/1).  Results do not depend on the options beyond fp32
  * summation order; cached graphs are dropped when an option changes.  No counterpart in the
  * reference (its ANE runtime has no such switches). */
@@ -189,6 +203,13 @@ int llm_time_attention(llm_ctx *ctx, int iters, double *us_per_launch, double *b
  * (count per step, us per launch, us per step, share) into report.  step_us receives the
  * eager step time (launch gaps included). */
 int llm_profile_step(llm_ctx *ctx, int iters, char *report, size_t report_len, double *step_us);
+
+/* Launch timeline of the next decode step of the current generate batch, run eagerly in the
+ * current schedule (overlapped micro-batches included; tokens and positions are not advanced,
+ * the step must be within the reserved ones): one report line per launch with its first CTA
+ * start, the spread of CTA start times, the last CTA end (microseconds from the step's first
+ * CTA, device globaltimer) and its CTA count.  step_us receives first start to last end. */
+int llm_trace_step(llm_ctx *ctx, char *report, size_t report_len, double *step_us);
 
 /* ---------------------------------------------------------------- allocation-free entry point */
 /* No counterpart in the reference.  Split-K int8 GEMM C[M,N] = A[M,K] . B[N,K]^T with int32
