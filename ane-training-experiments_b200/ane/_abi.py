@@ -30,6 +30,9 @@ LLM_DTYPE_BF16 = 2
 LLM_DTYPE_W8A8_F16 = 3
 LLM_DTYPE_W8A8_BF16 = 4
 
+LLM_WEIGHTS_LLAMA2C = 1
+LLM_WEIGHTS_CHECKPOINT = 2
+
 DTYPES = {
     "fp16": LLM_DTYPE_F16,
     "bf16": LLM_DTYPE_BF16,
@@ -39,7 +42,7 @@ DTYPES = {
 
 # every symbol include/llm_cuda.h declares
 EXPORTS = [
-    "llm_last_error", "llm_ctx_create", "llm_ctx_destroy", "llm_load_weights_f32",
+    "llm_last_error", "llm_ctx_create", "llm_ctx_destroy", "llm_load_weights_f32", "llm_load_weights_file",
     "llm_load_weights_synthetic", "llm_synth_normal", "llm_synth_stream", "llm_kv_alloc",
     "llm_seq_release", "llm_prefill", "llm_decode_step", "llm_generate_begin",
     "llm_generate_steps", "llm_generate_end", "llm_generate", "llm_stories_decode",
@@ -122,6 +125,7 @@ def lib() -> C.CDLL:
         "llm_step_kernel_count": (C.c_int, [C.c_void_p, C.c_int, i32p]),
         "llm_memory_bytes": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
         "llm_time_attention": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
+        "llm_load_weights_file": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int]),
         "llm_profile_step": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.c_size_t, C.POINTER(C.c_double)]),
         "llm_trace_step": (C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t, C.POINTER(C.c_double)]),
         "llm_debug_norm_quant": (C.c_int, [C.c_int, _FP, _FP, C.c_int, C.c_int, C.c_double, C.POINTER(C.c_int8), _FP]),

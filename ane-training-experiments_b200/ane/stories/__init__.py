@@ -200,48 +200,126 @@ def LoadPretrained(path: str, cfg: Optional[ModelConfig] = None):
                     VocabSize=vocab if shared else -vocab, SeqLen=seq)
 
 
-class Tokenizer:
-    """ane/stories/tokenizer.go:11-69 (decode only)."""
+@dataclass
+class TrainMeta:
+    """ane/stories/ckpt.go:24-35."""
 
-    def __init__(self, vocab: List[str]):
-        self.vocab = vocab
+    Step: int = 0
+    TotalSteps: int = 0
+    LR: float = 0.0
+    Loss: float = 0.0
+    CumCompile: float = 0.0
+    CumTrain: float = 0.0
+    CumWall: float = 0.0
+    CumSteps: int = 0
+    CumBatches: int = 0
+    AdamT: int = 0
+
+
+CKPT_MAGIC = 0x424C5A54  # ane/stories/ckpt.go:12
+
+
+def LoadCheckpoint(path: str, mw: "ModelWeights", opt=None) -> TrainMeta:
+    """ane/stories/ckpt.go:237-447 for inference: fills mw's weights from a v2/v3 checkpoint
+    and skips the optimizer moments (only opt=None is supported: training is out of scope).
+    The header's layers/vocab/dim/hidden/heads must match mw.Config."""
+    if opt is not None:
+        raise ValueError("optimizer state is not loaded by the inference path")
+    cfg = mw.Config
+    with open(path, "rb") as f:
+        def rd(n, what):
+            b = f.read(n)
+            if len(b) != n:
+                raise ValueError(f"read {what}: " + ("EOF" if not b else "unexpected EOF"))
+            return b
+        magic, ver = struct.unpack("<ii", rd(8, "checkpoint header"))
+        if magic != CKPT_MAGIC or ver not in (2, 3):
+            raise ValueError(f"bad checkpoint header magic={magic & 0xffffffff:x} version={ver}")
+        step, total, n_layers, vocab, dim, hidden, heads, _seq = struct.unpack("<8i", rd(32, "checkpoint header"))
+        if (n_layers, vocab, dim, hidden, heads) != (cfg.n_layers, cfg.vocab, cfg.dim, cfg.hidden, cfg.n_heads):
+            raise ValueError("checkpoint config mismatch")
+        lr, loss = struct.unpack("<ff", rd(8, "checkpoint header"))
+        cc, ct, cw = struct.unpack("<3d", rd(24, "checkpoint header"))
+        cs, cb, at, _, _, _ = struct.unpack("<6i", rd(24, "checkpoint header"))
+
+        def rdf(arr, what):
+            arr[...] = np.frombuffer(rd(arr.nbytes, what), dtype="<f4").reshape(arr.shape)
+
+        for i, L in enumerate(mw.Layers):
+            for attr in ("Wq", "Wk", "Wv", "Wo", "W1", "W2", "W3", "RMSAtt", "RMSFFN"):
+                rdf(getattr(L, attr), f"{attr.lower()}[{i}]")
+        per_layer = sum(getattr(mw.Layers[0], a).size for a in ("Wq", "Wk", "Wv", "Wo", "W1", "W2", "W3"))
+        skip = len(mw.Layers) * (2 * per_layer + 4 * cfg.dim)
+        rd(4 * skip, "layer optimizer state")
+        rdf(mw.RMSFinal, "rms_final")
+        rd(4 * 2 * cfg.dim, "rms_final optimizer state")
+        rdf(mw.Embed, "embed")
+        rd(4 * 2 * mw.Embed.size, "embed optimizer state")
+    return TrainMeta(step, total, lr, loss, cc, ct, cw, cs, cb, at)
+
+
+class Tokenizer:
+    """ane/stories/tokenizer.go:11-69 (decode only).
+
+    Pieces are kept as the file's raw bytes, as Go strings are.  DecodeBytes returns exactly
+    the bytes Go's Decode returns; Decode returns them as a str through the surrogateescape
+    error handler, so bytes that are not UTF-8 (single <0xHH> bytes) survive a round trip:
+    ``Decode(i).encode("utf-8", "surrogateescape") == DecodeBytes(i)``."""
+
+    def __init__(self, vocab: List[bytes]):
+        self.vocab = [v if isinstance(v, bytes) else v.encode("utf-8") for v in vocab]
+
+    def DecodeBytes(self, id: int) -> bytes:
+        if id < 0 or id >= len(self.vocab):
+            return b""
+        s = self.vocab[id]
+        if len(s) >= 5 and s[:3] == b"<0x" and s[-1:] == b">":
+            b = _decode_hex_token_byte(s)
+            if b is not None:
+                return bytes([b])
+        return s
 
     def Decode(self, id: int) -> str:
-        if id < 0 or id >= len(self.vocab):
-            return ""
-        s = self.vocab[id]
-        if len(s) >= 5 and s.startswith("<0x") and s.endswith(">"):
-            try:
-                return bytes([int(s[3:-1], 16)]).decode("latin-1")
-            except ValueError:
-                return s
-        return s
+        return self.DecodeBytes(id).decode("utf-8", "surrogateescape")
+
+
+def _decode_hex_token_byte(s: bytes) -> Optional[int]:
+    """tokenizer.go:71-101: exactly "<0xHH>" with hex digits of either case."""
+    if len(s) != 6:
+        return None
+    hexdigits = b"0123456789abcdefABCDEF"
+    if s[3] not in hexdigits or s[4] not in hexdigits:
+        return None
+    return int(s[3:5], 16)
 
 
 def LoadTokenizer(path: str, vocab_size: int = Vocab) -> Tokenizer:
-    """ane/stories/tokenizer.go:16-55."""
+    """ane/stories/tokenizer.go:16-55: int32 max token length, then per token a float32
+    score, an int32 byte length (0 <= n <= 8 * max) and the bytes; Vocab entries."""
     with open(path, "rb") as f:
         b = f.read(4)
         if len(b) != 4:
-            raise ValueError("read tokenizer header: EOF")
+            raise ValueError("read tokenizer header: " + ("EOF" if not b else "unexpected EOF"))
         (max_len,) = struct.unpack("<i", b)
         if max_len <= 0:
             raise ValueError(f"bad tokenizer header: max token len={max_len}")
         vocab = []
         for i in range(vocab_size):
             b = f.read(4)
-            if len(b) != 4:
+            if len(b) == 0:
                 raise ValueError(f"unexpected EOF at token {i}")
+            if len(b) != 4:
+                raise ValueError(f"read token[{i}] score: unexpected EOF")
             b = f.read(4)
             if len(b) != 4:
-                raise ValueError(f"read token[{i}] length: EOF")
+                raise ValueError(f"read token[{i}] length: " + ("EOF" if not b else "unexpected EOF"))
             (n,) = struct.unpack("<i", b)
             if n < 0 or n > max_len * 8:
                 raise ValueError(f"bad token[{i}] length={n}")
-            s = f.read(n)
-            if len(s) != n:
-                raise ValueError(f"read token[{i}] bytes: EOF")
-            vocab.append(s.decode("utf-8", errors="replace"))
+            piece = f.read(n)
+            if len(piece) != n:
+                raise ValueError(f"read token[{i}] bytes: " + ("EOF" if not piece else "unexpected EOF"))
+            vocab.append(piece)
     return Tokenizer(vocab)
 
 
@@ -282,6 +360,12 @@ class Engine:
         cw, keep = w.c_struct()
         _abi.check(_abi.lib().llm_load_weights_f32(self.h, C.byref(cw)))
         del keep
+        return self
+
+    def load_file(self, path: str, fmt: str = "llama2c") -> "Engine":
+        """Stream a llama2.c .bin ("llama2c") or a training checkpoint ("checkpoint") to the device."""
+        code = {"llama2c": _abi.LLM_WEIGHTS_LLAMA2C, "checkpoint": _abi.LLM_WEIGHTS_CHECKPOINT}[fmt]
+        _abi.check(_abi.lib().llm_load_weights_file(self.h, str(path).encode(), code))
         return self
 
     def load_synthetic(self, seed: int, out_proj_scale: float = 1.0) -> "Engine":
@@ -444,7 +528,9 @@ class Decoder:
         res = []
         for i in range(n):
             toks = out[i, : ntok[i]].tolist()
-            text = "".join(tok.Decode(t) for t in toks[plen[i]:]) if tok is not None else ""
+            # infer.go:185-187: generatedText += tok.Decode(next), as bytes (Go strings)
+            text = (b"".join(tok.DecodeBytes(t) for t in toks[plen[i]:]).decode("utf-8", "surrogateescape")
+                    if tok is not None else "")
             res.append(DecodeResult(toks, int(plen[i]), text, bool(eos[i])))
         return res
 

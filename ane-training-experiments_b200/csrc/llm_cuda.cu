@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <array>
+#include <cerrno>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -727,13 +729,47 @@ int upload_f32(llm_ctx* c, float** dst, const float* src, size_t n, float fill) 
   return LLM_OK;
 }
 
-// Tensor source: either caller fp32 pointers or the synthetic generator.
+// A weight file read tensor by tensor: byte offset of every tensor, the file's norm weights
+// (read whole), and a reader that pulls one matrix into host memory on demand.
+struct FileTensors {
+  FILE* f = nullptr;
+  std::string path;
+  // offsets (bytes) of kind 0..6 = wq,wk,wv,wo,w1,w2,w3 per layer, embed
+  std::vector<std::array<int64_t, 7>> off;
+  int64_t embed_off = 0;
+  std::vector<std::vector<float>> rms_att, rms_ffn;
+  std::vector<float> rms_final;
+  std::vector<llm_layer_weights_f32> layer_norms;
+  ~FileTensors() {
+    if (f) fclose(f);
+  }
+  int read_at(int64_t off, float* dst, size_t n, const char* what) {
+    if (fseeko(f, off, SEEK_SET) != 0) return fail(LLM_ERR_INVALID, "read %s: seek failed", what);
+    const size_t got = fread(dst, 4, n, f);
+    if (got != n) return fail(LLM_ERR_INVALID, "read %s: %s", what, got == 0 ? "EOF" : "unexpected EOF");
+    return LLM_OK;
+  }
+};
+
+// Tensor source: caller fp32 pointers, a weight file, or the synthetic generator.
 struct Source {
   const llm_model_weights_f32* w = nullptr;
+  FileTensors* file = nullptr;
+  int file_rc = LLM_OK;
   uint64_t seed = 0;
   float out_scale = 1.f;
-  std::vector<float> host;  // synthetic scratch
+  std::vector<float> host;  // synthetic / file scratch
   const float* get(int layer, int kind, size_t n) {
+    if (file) {
+      static const char* names[9] = {"wq", "wk", "wv", "wo", "w1", "w2", "w3", "embed", "lm_head"};
+      if (kind == 8) return nullptr;
+      host.resize(n);
+      char what[32];
+      snprintf(what, sizeof what, kind == 7 ? "%s" : "%s[%d]", names[kind], layer);
+      const int64_t off = kind == 7 ? file->embed_off : file->off[layer][kind];
+      file_rc = file->read_at(off, host.data(), n, what);
+      return file_rc ? nullptr : host.data();
+    }
     if (w) {
       if (kind == 7) return w->embed;
       if (kind == 8) return w->lm_head;
@@ -769,7 +805,7 @@ int load_weights(llm_ctx* c, Source& src) {
   int rc;
   if ((rc = dalloc(c, &c->embed, static_cast<size_t>(V) * D * ab, &c->bytes_weights))) return cleanup(rc);
   const float* e = src.get(0, 7, static_cast<size_t>(V) * D);
-  if (!e) return cleanup(fail(LLM_ERR_INVALID, "nil embed"));
+  if (!e) return cleanup(src.file_rc ? src.file_rc : fail(LLM_ERR_INVALID, "nil embed"));
   if ((rc = upload_convert(c, dtmp, e, V, D, c->embed, nullptr, false, 1, 0))) return cleanup(rc);
   if (k.tied_embed) {
     c->lm_head = c->embed;
@@ -779,7 +815,8 @@ int load_weights(llm_ctx* c, Source& src) {
     if ((rc = dalloc(c, &c->lm_head, static_cast<size_t>(V) * D * ab, &c->bytes_weights))) return cleanup(rc);
     if ((rc = upload_convert(c, dtmp, lh, V, D, c->lm_head, nullptr, false, 1, 0))) return cleanup(rc);
   }
-  if ((rc = upload_f32(c, &c->rms_final, src.w ? src.w->rms_final : nullptr, D, 1.f))) return cleanup(rc);
+  const float* rms_final = src.w ? src.w->rms_final : (src.file ? src.file->rms_final.data() : nullptr);
+  if ((rc = upload_f32(c, &c->rms_final, rms_final, D, 1.f))) return cleanup(rc);
   c->layers.resize(k.n_layers);
   const int NQKV = Q + 2 * KV;
   for (int l = 0; l < k.n_layers; ++l) {
@@ -796,7 +833,7 @@ int load_weights(llm_ctx* c, Source& src) {
     }
     auto part = [&](int kind, int rows, int cols, void* base, float* sbase, int row_off, int mul, int add) -> int {
       const float* s = src.get(l, kind, static_cast<size_t>(rows) * cols);
-      if (!s) return fail(LLM_ERR_INVALID, "nil weight (layer %d, tensor %d)", l, kind);
+      if (!s) return src.file_rc ? src.file_rc : fail(LLM_ERR_INVALID, "nil weight (layer %d, tensor %d)", l, kind);
       uint8_t* dst = static_cast<uint8_t*>(base) + static_cast<size_t>(row_off) * cols * wb;
       float* ds = sbase ? sbase + row_off : nullptr;
       return upload_convert(c, dtmp, s, rows, cols, dst, ds, c->in8, mul, add);
@@ -808,7 +845,8 @@ int load_weights(llm_ctx* c, Source& src) {
     if ((rc = part(4, F, D, L.w13, L.s13, 0, 2, 0))) return cleanup(rc);
     if ((rc = part(6, F, D, L.w13, L.s13, 0, 2, 1))) return cleanup(rc);
     if ((rc = part(5, D, F, L.w2, L.s2, 0, 1, 0))) return cleanup(rc);
-    const llm_layer_weights_f32* lw = src.w ? &src.w->layers[l] : nullptr;
+    const llm_layer_weights_f32* lw =
+        src.w ? &src.w->layers[l] : (src.file ? &src.file->layer_norms[l] : nullptr);
     if ((rc = upload_f32(c, &L.rms_att, lw ? lw->rms_att : nullptr, D, 1.f))) return cleanup(rc);
     if ((rc = upload_f32(c, &L.rms_ffn, lw ? lw->rms_ffn : nullptr, D, 1.f))) return cleanup(rc);
     if (k.qk_norm) {
@@ -828,6 +866,127 @@ extern "C" int llm_load_weights_f32(llm_ctx* c, const llm_model_weights_f32* w) 
   if (!c || !w || !w->layers || !w->embed || !w->rms_final) return fail(LLM_ERR_INVALID, "nil context or weights");
   Source s;
   s.w = w;
+  return load_weights(c, s);
+}
+
+namespace {
+
+// ane/stories/weights.go:49-122: header of 7 int32 (dim, hidden, layers, heads, kv_heads,
+// vocab, seq_len; vocab < 0 = the file also holds an unshared classifier, which the reference
+// does not read), embed, then each kind for all layers: rms_att, wq, wk, wv, wo, rms_ffn, w1,
+// w2, w3, then rms_final.  The classifier is the embedding (infer.go:243).
+int scan_llama2c(const llm_ctx* c, FileTensors& ft) {
+  const llm_model_config& k = c->cfg;
+  int32_t h[7];
+  if (fread(h, 4, 7, ft.f) != 7) return fail(LLM_ERR_INVALID, "read config: unexpected EOF");
+  const int Q = c->q_dim, KV = c->kv_dim, D = k.dim, F = k.hidden, L = k.n_layers;
+  if (h[0] != D || h[1] != F || h[2] != L)
+    return fail(LLM_ERR_INVALID, "config mismatch: got dim=%d hidden=%d layers=%d", h[0], h[1], h[2]);
+  if (h[3] != k.n_heads || h[4] != k.n_kv_heads || std::abs(h[5]) != k.vocab)
+    return fail(LLM_ERR_INVALID, "config mismatch: got heads=%d kv_heads=%d vocab=%d", h[3], h[4], std::abs(h[5]));
+  if (!k.tied_embed) return fail(LLM_ERR_UNSUPPORTED, "llama2.c weight files are read with the embedding as classifier (tied)");
+  int64_t o = 28;
+  ft.embed_off = o;
+  o += 4ll * k.vocab * D;
+  const int64_t rms_att = o;
+  o += 4ll * L * D;
+  ft.off.assign(L, {});
+  const int64_t sizes[7] = {4ll * Q * D, 4ll * KV * D, 4ll * KV * D, 4ll * D * Q, 4ll * F * D, 4ll * D * F, 4ll * F * D};
+  // wq, wk, wv, wo
+  for (int kind = 0; kind < 4; ++kind)
+    for (int l = 0; l < L; ++l) {
+      ft.off[l][kind] = o;
+      o += sizes[kind];
+    }
+  const int64_t rms_ffn = o;
+  o += 4ll * L * D;
+  // w1, w2, w3 (file order)
+  for (int kind : {4, 5, 6})
+    for (int l = 0; l < L; ++l) {
+      ft.off[l][kind] = o;
+      o += sizes[kind];
+    }
+  const int64_t rms_final = o;
+  ft.rms_att.assign(L, std::vector<float>(D));
+  ft.rms_ffn.assign(L, std::vector<float>(D));
+  ft.rms_final.resize(D);
+  char what[32];
+  for (int l = 0; l < L; ++l) {
+    snprintf(what, sizeof what, "rms_att[%d]", l);
+    RC(ft.read_at(rms_att + 4ll * l * D, ft.rms_att[l].data(), D, what));
+    snprintf(what, sizeof what, "rms_ffn[%d]", l);
+    RC(ft.read_at(rms_ffn + 4ll * l * D, ft.rms_ffn[l].data(), D, what));
+  }
+  RC(ft.read_at(rms_final, ft.rms_final.data(), D, "rms_final"));
+  return LLM_OK;
+}
+
+// ane/stories/ckpt.go:237-447 with no optimizer state wanted: a 96-byte header (magic
+// 0x424C5A54, version 2 or 3, step, total steps, layers, vocab, dim, hidden, heads, seq, lr,
+// loss, three f64 timers, three int32 counters, three int32 pads), then per layer wq, wk, wv,
+// wo, w1, w2, w3, rms_att, rms_ffn; then every layer's Adam moments (skipped), rms_final, its
+// moments (skipped), embed.
+int scan_checkpoint(const llm_ctx* c, FileTensors& ft) {
+  const llm_model_config& k = c->cfg;
+  int32_t h[10];
+  if (fread(h, 4, 2, ft.f) != 2) return fail(LLM_ERR_INVALID, "read checkpoint header: unexpected EOF");
+  if (h[0] != 0x424C5A54 || (h[1] != 2 && h[1] != 3))
+    return fail(LLM_ERR_INVALID, "bad checkpoint header magic=%x version=%d", static_cast<unsigned>(h[0]), h[1]);
+  if (fread(h + 2, 4, 8, ft.f) != 8) return fail(LLM_ERR_INVALID, "read checkpoint header: unexpected EOF");
+  if (h[4] != k.n_layers || h[5] != k.vocab || h[6] != k.dim || h[7] != k.hidden || h[8] != k.n_heads)
+    return fail(LLM_ERR_INVALID, "checkpoint config mismatch");
+  if (!k.tied_embed) return fail(LLM_ERR_UNSUPPORTED, "checkpoints hold one embedding, used as the classifier (tied)");
+  const int Q = c->q_dim, KV = c->kv_dim, D = k.dim, F = k.hidden, L = k.n_layers;
+  const int64_t sizes[7] = {4ll * Q * D, 4ll * KV * D, 4ll * KV * D, 4ll * D * Q, 4ll * F * D, 4ll * D * F, 4ll * F * D};
+  int64_t o = 96;
+  ft.off.assign(L, {});
+  ft.rms_att.assign(L, std::vector<float>(D));
+  ft.rms_ffn.assign(L, std::vector<float>(D));
+  char what[32];
+  for (int l = 0; l < L; ++l) {
+    for (int kind = 0; kind < 7; ++kind) {
+      ft.off[l][kind] = o;
+      o += sizes[kind];
+    }
+    snprintf(what, sizeof what, "rms_att[%d]", l);
+    RC(ft.read_at(o, ft.rms_att[l].data(), D, what));
+    o += 4ll * D;
+    snprintf(what, sizeof what, "rms_ffn[%d]", l);
+    RC(ft.read_at(o, ft.rms_ffn[l].data(), D, what));
+    o += 4ll * D;
+  }
+  int64_t layer_opt = 0;
+  for (int kind = 0; kind < 7; ++kind) layer_opt += 2 * sizes[kind];
+  layer_opt += 4 * 4ll * D;
+  o += L * layer_opt;
+  ft.rms_final.resize(D);
+  RC(ft.read_at(o, ft.rms_final.data(), D, "rms_final"));
+  o += 4ll * D + 2 * 4ll * D;
+  ft.embed_off = o;
+  return LLM_OK;
+}
+
+}  // namespace
+
+extern "C" int llm_load_weights_file(llm_ctx* c, const char* path, int format) {
+  if (!c || !path) return fail(LLM_ERR_INVALID, "nil context or path");
+  if (format != LLM_WEIGHTS_LLAMA2C && format != LLM_WEIGHTS_CHECKPOINT)
+    return fail(LLM_ERR_INVALID, "unknown weight file format %d", format);
+  if (c->weights_loaded) return fail(LLM_ERR_STATE, "weights already loaded");
+  if (c->cfg.qk_norm) return fail(LLM_ERR_UNSUPPORTED, "weight files carry no QK-norm weights");
+  FileTensors ft;
+  ft.path = path;
+  ft.f = fopen(path, "rb");
+  if (!ft.f) return fail(LLM_ERR_INVALID, "open %s: %s", path, strerror(errno));
+  RC(format == LLM_WEIGHTS_LLAMA2C ? scan_llama2c(c, ft) : scan_checkpoint(c, ft));
+  ft.layer_norms.resize(c->cfg.n_layers);
+  for (int l = 0; l < c->cfg.n_layers; ++l) {
+    ft.layer_norms[l] = llm_layer_weights_f32{};
+    ft.layer_norms[l].rms_att = ft.rms_att[l].data();
+    ft.layer_norms[l].rms_ffn = ft.rms_ffn[l].data();
+  }
+  Source s;
+  s.file = &ft;
   return load_weights(c, s);
 }
 

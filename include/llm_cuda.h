@@ -94,6 +94,20 @@ int llm_ctx_destroy(llm_ctx *ctx);
  * blob staging of model.CompileOptions.WeightBlob (ane/model/model_other.go:13-24). */
 int llm_load_weights_f32(llm_ctx *ctx, const llm_model_weights_f32 *w);
 
+/* Weight file formats of llm_load_weights_file. */
+#define LLM_WEIGHTS_LLAMA2C 1    /* llama2.c .bin: ane/stories/weights.go:49-122 (LoadPretrained)     */
+#define LLM_WEIGHTS_CHECKPOINT 2 /* training checkpoint v2/v3: ane/stories/ckpt.go:237-447
+                                    (LoadCheckpoint with no optimizer state)                      */
+
+/* Stream the weights of a file to the device tensor by tensor (one matrix in host memory at a
+ * time; rounding / int8 quantisation on the device as llm_load_weights_f32).  The header must
+ * match the context's configuration; errors use the reference's texts ("config mismatch: got
+ * dim=%d hidden=%d layers=%d", "bad checkpoint header magic=%x version=%d", "checkpoint config
+ * mismatch", "read <tensor>: unexpected EOF").  Both formats use the embedding as the
+ * classifier, as ane/stories/infer.go:243 does, so the configuration must be tied and without
+ * QK-norm.  Replaces stories.LoadPretrained / stories.LoadCheckpoint + NewDecoder's copy. */
+int llm_load_weights_file(llm_ctx *ctx, const char *path, int format);
+
 /* Seeded synthetic weights, generated on the host by llm_synth_normal (streams below):
  * matrices N(0, 0.02); Wo and W2 additionally x out_proj_scale (Stories: 1/sqrt(2*12));
  * RMSNorm and QK-norm weights 1.  Stands in for stories.RandomInit (ane/stories/weights.go:124-153),
