@@ -362,6 +362,10 @@ class Engine:
         del keep
         return self
 
+    def set_sampling(self, temperature: float, seed: int, reset_draws: bool = True) -> None:
+        """Temperature sampling for the following steps (<= 1e-6: greedy); see llm_set_sampling."""
+        _abi.check(_abi.lib().llm_set_sampling(self.h, float(temperature), int(seed) & (2**64 - 1), int(reset_draws)))
+
     def load_file(self, path: str, fmt: str = "llama2c") -> "Engine":
         """Stream a llama2.c .bin ("llama2c") or a training checkpoint ("checkpoint") to the device."""
         code = {"llama2c": _abi.LLM_WEIGHTS_LLAMA2C, "checkpoint": _abi.LLM_WEIGHTS_CHECKPOINT}[fmt]
@@ -489,6 +493,9 @@ class Decoder:
         self.engine = engine
         self.maxSeq = maxSeq
         self.seed = seed
+        # infer.go:131: the decoder's generator, seeded once; its draws persist across Decode
+        # calls (per sequence slot on the device) until a Decode with a non-zero Seed reseeds
+        engine.set_sampling(0.0, seed, True)
 
     def ResetCache(self) -> None:
         """infer.go:62-71."""
@@ -505,7 +512,7 @@ class Decoder:
         return lg[0]
 
     def Decode(self, tok: Optional[Tokenizer], opts: DecodeOptions) -> DecodeResult:
-        """infer.go:136-202 (greedy)."""
+        """infer.go:136-202 (greedy, or temperature sampling with the device generator)."""
         return self.DecodeBatch(tok, opts, [opts.PromptTokens])[0]
 
     def DecodeBatch(self, tok: Optional[Tokenizer], opts: DecodeOptions, prompts: List[List[int]]) -> List[DecodeResult]:
@@ -515,6 +522,9 @@ class Decoder:
             raise LLMError(_abi.LLM_ERR_INVALID, f"batch {n} exceeds the decoder's {self.engine.max_batch} slots")
         if opts.Temperature < 0:
             opts = DecodeOptions(opts.MaxNewTokens, 0.0, opts.Seed, opts.PromptTokens)
+        if opts.Seed != 0:  # infer.go:150-152
+            self.seed = opts.Seed
+            self.engine.set_sampling(0.0, opts.Seed, True)
         lens = _abi.i32([len(p) for p in prompts])
         flat = _abi.i32([t for p in prompts for t in p] or [0])
         out = np.zeros((n, self.maxSeq), np.int32)

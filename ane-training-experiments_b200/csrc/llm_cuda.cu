@@ -23,6 +23,7 @@
 #include "common.cuh"
 #include "gemm.cuh"
 #include "norm.cuh"
+#include "sample.cuh"
 #include "umma.cuh"
 
 using namespace llm;
@@ -122,6 +123,7 @@ struct FinishParams {
   const int* gen_start;            // optional with gen_out
   int* gen_out;                    // [cap][M]
   int gen_cap;
+  const int* sampled;              // optional [M]: tokens drawn by sample_kernel replace the argmax
 };
 
 // Greedy token per row: max over the lm_head tiles' (value, first index) partials.
@@ -143,7 +145,7 @@ __global__ void __launch_bounds__(256) finish_kernel(FinishParams f) {
     best = other > best ? other : best;
   }
   if (lane == 0) {
-    const int idx = argmax_key_index(best);
+    const int idx = f.sampled ? f.sampled[row] : argmax_key_index(best);
     f.next[row] = idx;
     if (f.tok_io) f.tok_io[row] = idx;
     if (f.gen_out) {
@@ -530,6 +532,12 @@ struct llm_ctx {
   // how one micro-batch's attention launch waits for the other's: 0 = its completion,
   // 1 = all of its CTAs having started (launch-completion event)
   int attn_chain = 1;
+  // temperature sampling (llm_set_sampling): temperature <= 1e-6 = greedy
+  float sample_temp = 0.f;
+  double sample_inv_t = 0.0;
+  uint64_t sample_seed = 0;
+  unsigned long long* d_draws = nullptr;  // [max_seqs] draws so far per sequence slot
+  int* d_sampled = nullptr;               // [max_rows]
   // llm_trace_step: per-launch timeline records (device) and their labels (host)
   bool tracing = false;
   TraceRec* d_trace = nullptr;
@@ -1043,8 +1051,11 @@ extern "C" int llm_kv_alloc(llm_ctx* c, int max_seqs, int max_pos, int page_toke
   RC(dalloc_t(c, &c->gs, R * 4, o));
   RC(dalloc(c, &c->xf, R * D * ab, o));
   RC(dalloc_t(c, &c->argmax_part, ((V + 127) / 128) * R * 8, o));
-  for (int** p : {&c->d_seq, &c->d_tok, &c->d_pos, &c->d_next, &c->d_gen_start, &c->d_blk_row0, &c->d_blk_nq, &c->d_final})
+  for (int** p : {&c->d_seq, &c->d_tok, &c->d_pos, &c->d_next, &c->d_gen_start, &c->d_blk_row0, &c->d_blk_nq, &c->d_final,
+                   &c->d_sampled})
     RC(dalloc_t(c, p, R * 4, o));
+  RC(dalloc_t(c, &c->d_draws, static_cast<size_t>(max_seqs) * 8, o));
+  CU(cudaMemset(c->d_draws, 0, static_cast<size_t>(max_seqs) * 8));
   c->ws_floats = 16u << 20;  // 64 MB split-K / split-attention workspace
   RC(dalloc_t(c, &c->ws, c->ws_floats * 4, o));
   RC(dalloc_t(c, &c->counters, kCounters * 4, o));
@@ -1149,6 +1160,7 @@ struct RowsSpec {
   const int* gen_start = nullptr;
   int* gen_out = nullptr;
   int gen_cap = 0;
+  bool sample = false;  // draw the next token with sample_kernel (temperature sampling)
 };
 
 const CUtensorMap* tmap(llm_ctx* c, const void* ptr, int esz, int k, int rows, int box) {
@@ -1204,6 +1216,8 @@ int overlap_parts(const llm_ctx* c, int R, bool decode_rows) {
   return k >= 2 ? k : 1;
 }
 bool overlap_applies(const llm_ctx* c, int R, bool decode_rows) { return overlap_parts(c, R, decode_rows) > 1; }
+// Temperature sampling replaces the greedy argmax (sampleFromLogits, infer.go:347-349).
+bool sampling_on(const llm_ctx* c) { return c->sample_temp > 1e-6f; }
 // Launch timeline records one traced step may use.
 constexpr size_t kTraceCap = 1024;
 
@@ -1497,11 +1511,26 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
     p.N = k.vocab;
     p.K = D;
     p.argmax_part = c->argmax_part;
-    p.logits = rs.d_logits;
+    p.logits = rs.d_logits ? rs.d_logits : (rs.sample ? c->logits : nullptr);
     p.ld_logits = k.vocab;
     p.trace = tr("lm_head", k.n_layers, parts[0]);
     RC(gemm(c, false, EPI_ARGMAX, p));
     RC(mark("lm_head+argmax"));
+  }
+  if (rs.sample) {
+    SampleParams sp{};
+    sp.logits = rs.d_logits ? rs.d_logits : c->logits;
+    sp.rows = NF;
+    sp.V = k.vocab;
+    sp.ld = k.vocab;
+    sp.inv_t = c->sample_inv_t;
+    sp.row_index = rs.d_final;
+    sp.seq_ids = c->d_seq;
+    sp.seed = c->sample_seed;
+    sp.draws = c->d_draws;
+    sp.out = c->d_sampled;
+    CU(launch_pdl(sample_kernel, dim3(NF), dim3(kSampleThreads), 0, s, sp));
+    RC(mark("sample"));
   }
   {
     FinishParams f{};
@@ -1514,6 +1543,7 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
     f.gen_start = rs.gen_start;
     f.gen_out = rs.gen_out;
     f.gen_cap = rs.gen_cap;
+    f.sampled = rs.sample ? c->d_sampled : nullptr;
     CU(launch_pdl(finish_kernel, dim3((NF + 7) / 8), dim3(256), 0, s, f));
     RC(mark("finish"));
   }
@@ -1539,6 +1569,7 @@ int run_step(llm_ctx* c, int n, int splits, int mode) {
   rs.R = n;
   rs.n_blocks = n;
   rs.attn_splits = splits;
+  rs.sample = sampling_on(c);
   if (mode == 1) rs.d_logits = c->logits;
   if (mode == 2) {
     rs.tok_io = c->d_tok;
@@ -1550,7 +1581,7 @@ int run_step(llm_ctx* c, int n, int splits, int mode) {
   // overlapped micro-batch steps launch eagerly unless LLM_OPT_OVERLAP_GRAPHS: their
   // cross-stream schedule measured faster from eager launches than from a replayed graph
   if (!c->use_graphs || (overlap_applies(c, n, true) && !c->overlap_graphs)) return enqueue_forward(c, rs);
-  GraphKey key{n, splits, mode};
+  GraphKey key{n, splits, mode | (rs.sample ? 8 : 0)};
   auto it = c->graphs.find(key);
   if (it == c->graphs.end()) {
     cudaGraph_t g = nullptr;
@@ -1598,7 +1629,7 @@ extern "C" int llm_decode_step(llm_ctx* c, const int32_t* seq_ids, const int32_t
   CU(cudaMemcpyAsync(c->d_seq, h, n * 4, cudaMemcpyHostToDevice, c->stream));
   CU(cudaMemcpyAsync(c->d_tok, h + n, n * 4, cudaMemcpyHostToDevice, c->stream));
   CU(cudaMemcpyAsync(c->d_pos, h + 2 * n, n * 4, cudaMemcpyHostToDevice, c->stream));
-  if (logits) RC(ensure_logits(c, n));
+  if (logits || sampling_on(c)) RC(ensure_logits(c, n));
   // splits sized for the largest context this graph shape is likely to see: round up to a
   // power-of-two page count so graphs are reused across steps
   int pages = (max_ctx + 15) / 16, p2 = 1;
@@ -1638,7 +1669,7 @@ extern "C" int llm_prefill(llm_ctx* c, const int32_t* seq_ids, const int32_t* to
     off += lens[i];
   }
   RC(upload_dirty(c, dirty));
-  if (logits) RC(ensure_logits(c, nseq));
+  if (logits || sampling_on(c)) RC(ensure_logits(c, nseq));
   const int Rmax = c->max_rows;
   size_t r = 0;
   while (r < rows.size()) {
@@ -1687,6 +1718,7 @@ extern "C" int llm_prefill(llm_ctx* c, const int32_t* seq_ids, const int32_t* to
     rs.d_final = c->d_final;
     rs.n_final = nf;
     rs.d_logits = logits ? c->logits : nullptr;
+    rs.sample = sampling_on(c) && nf > 0;
     if (nf > 0) {
       RC(enqueue_forward(c, rs));
       std::vector<int> nxt(nf);
@@ -1732,6 +1764,7 @@ extern "C" int llm_generate_begin(llm_ctx* c, const int32_t* seq_ids, const int3
     max_ctx = std::max(max_ctx, positions[i] + max_steps);
   }
   RC(upload_dirty(c, dirty));
+  if (sampling_on(c)) RC(ensure_logits(c, n));
   const size_t need = static_cast<size_t>(max_steps) * n;
   if (need > c->gen_out_cap) {
     if (c->d_gen_out) {
@@ -1812,9 +1845,16 @@ extern "C" int llm_stories_decode_batch(llm_ctx* c, const int32_t* prompts, cons
   if (!out_tokens || !n_tokens || !prompt_len || !stopped_on_eos || (!prompts && nseq > 0) || !prompt_lens)
     return fail(LLM_ERR_INVALID, "nil buffer");
   if (nseq <= 0 || nseq > c->max_seqs) return fail(LLM_ERR_INVALID, "nseq %d out of range", nseq);
-  if (temperature > 1e-6f)
-    return fail(LLM_ERR_UNSUPPORTED, "temperature %g: sampling is not implemented on the CUDA path (greedy only)",
-                static_cast<double>(temperature));
+  // infer.go:144-146: negative temperature -> 0 (greedy); the call samples with `temperature`
+  // from the context's generator state (llm_set_sampling's seed and per-slot draw counts)
+  if (!(temperature > 0.f)) temperature = 0.f;
+  struct TempScope {
+    llm_ctx* c;
+    float saved;
+    ~TempScope() { c->sample_temp = saved; }
+  } scope{c, c->sample_temp};
+  c->sample_temp = temperature;
+  c->sample_inv_t = static_cast<double>(1.0f / temperature);
   const int max_seq = c->max_pos;  // Decoder.maxSeq
   if (max_new <= 0) max_new = 64;  // infer.go:147-149
   std::vector<std::vector<int>> toks(nseq);
@@ -1888,6 +1928,25 @@ extern "C" int llm_stories_decode(llm_ctx* c, int seq, const int32_t* prompt, in
 }
 
 // ============================================================================ options
+extern "C" double llm_sample_uniform(uint64_t seed, int32_t slot, uint64_t counter) {
+  return sample_uniform(seed, kSampleStreamBase + static_cast<uint64_t>(slot), counter);
+}
+
+extern "C" int llm_set_sampling(llm_ctx* c, float temperature, uint64_t seed, int reset_draws) {
+  if (!c) return fail(LLM_ERR_INVALID, "nil context");
+  if (std::isnan(temperature)) return fail(LLM_ERR_INVALID, "temperature is NaN");
+  RC(set_device(c));
+  CU(cudaStreamSynchronize(c->stream));
+  c->sample_temp = temperature > 0.f ? temperature : 0.f;
+  c->sample_inv_t = c->sample_temp > 0.f ? static_cast<double>(1.0f / c->sample_temp) : 0.0;
+  c->sample_seed = seed;
+  if (reset_draws && c->d_draws) CU(cudaMemset(c->d_draws, 0, static_cast<size_t>(c->max_seqs) * 8));
+  // the temperature and seed are kernel arguments baked into captured steps
+  for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
+  c->graphs.clear();
+  return LLM_OK;
+}
+
 extern "C" int llm_set_option(llm_ctx* c, int option, int value) {
   if (!c) return fail(LLM_ERR_INVALID, "nil context");
   bool* flag = nullptr;
@@ -2284,6 +2343,32 @@ int debug_gemm(int device, bool in8, int act, const void* hA, const void* hB, si
   return LLM_OK;
 }
 }  // namespace
+
+extern "C" int llm_debug_sample(int device, const float* logits, int rows, int vocab, float temperature,
+                                const double* u, int32_t* out) {
+  if (!logits || !u || !out || rows <= 0 || vocab <= 0) return fail(LLM_ERR_INVALID, "bad arguments");
+  if (!(temperature > 1e-6f)) return fail(LLM_ERR_INVALID, "temperature %g takes the greedy path", static_cast<double>(temperature));
+  if (cudaSetDevice(device) != cudaSuccess) return fail(LLM_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+  DevBuf dl, du, dout;
+  CU(cudaMalloc(&dl.p, static_cast<size_t>(rows) * vocab * 4));
+  CU(cudaMalloc(&du.p, static_cast<size_t>(rows) * 8));
+  CU(cudaMalloc(&dout.p, static_cast<size_t>(rows) * 4));
+  CU(cudaMemcpy(dl.p, logits, static_cast<size_t>(rows) * vocab * 4, cudaMemcpyHostToDevice));
+  CU(cudaMemcpy(du.p, u, static_cast<size_t>(rows) * 8, cudaMemcpyHostToDevice));
+  SampleParams sp{};
+  sp.logits = static_cast<const float*>(dl.p);
+  sp.rows = rows;
+  sp.V = vocab;
+  sp.ld = vocab;
+  sp.inv_t = static_cast<double>(1.0f / temperature);
+  sp.u = static_cast<const double*>(du.p);
+  sp.out = static_cast<int*>(dout.p);
+  sample_kernel<<<rows, kSampleThreads>>>(sp);
+  CU(cudaGetLastError());
+  CU(cudaDeviceSynchronize());
+  CU(cudaMemcpy(out, dout.p, static_cast<size_t>(rows) * 4, cudaMemcpyDeviceToHost));
+  return LLM_OK;
+}
 
 extern "C" int llm_debug_gemm_i8(int device, const int8_t* A, const int8_t* B, int M, int N, int K, int splits, int32_t* C) {
   if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0 || K % 128) return fail(LLM_ERR_INVALID, "bad arguments (K %% 128 == 0)");

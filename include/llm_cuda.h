@@ -162,7 +162,8 @@ int llm_generate(llm_ctx *ctx, const int32_t *seq_ids, const int32_t *tokens, co
 /* Greedy Decode of one sequence slot with the reference's host rules (ane/stories/infer.go:136-202):
  * empty prompt -> [BOS=1]; prompt longer than max_seq keeps its last max_seq tokens;
  * prompt tokens range-checked ("prompt token[%d]=%d out of range"); stop at max_new
- * (<= 0 -> 64), at max_seq, or after EOS=2.  temperature > 1e-6 returns LLM_ERR_UNSUPPORTED.
+ * (<= 0 -> 64), at max_seq, or after EOS=2.  temperature > 1e-6 samples (llm_set_sampling's
+ * generator state, this call's temperature); otherwise greedy.
  * out_tokens needs max_seq entries; it receives prompt + generated tokens. */
 int llm_stories_decode(llm_ctx *ctx, int seq, const int32_t *prompt, int n_prompt, int max_new,
                        float temperature, int32_t *out_tokens, int32_t *n_tokens, int32_t *prompt_len,
@@ -172,6 +173,24 @@ int llm_stories_decode(llm_ctx *ctx, int seq, const int32_t *prompt, int n_promp
 int llm_stories_decode_batch(llm_ctx *ctx, const int32_t *prompts, const int32_t *prompt_lens, int nseq,
                              int max_new, float temperature, int32_t *out_tokens, int32_t *n_tokens,
                              int32_t *prompt_len, int32_t *stopped_on_eos);
+
+/* ---------------------------------------------------------------- temperature sampling */
+/* Sample the next tokens with `temperature` (> 1e-6; <= 1e-6 or negative = greedy argmax) as
+ * sampleFromLogits does (ane/stories/infer.go:347-371: f32 max, invT = float64(1/T), f64
+ * exp-sum inverse CDF, first index whose running sum reaches u * total, else vocab - 1) for
+ * every following prefill / decode step / generate step, until changed.  u comes from a
+ * counter-based generator (llm_sample_uniform) of `seed`, the row's sequence slot and that
+ * slot's draw count, which each sample advances on the device; reset_draws != 0 zeroes every
+ * slot's count (infer.go:150-152 reseeding).  Go's math/rand stream of the reference is not
+ * reproduced (parity of the uniforms is unpinned; the sampler given the same u and logits is
+ * checked against the oracle).  llm_stories_decode[_batch] take their temperature per call. */
+int llm_set_sampling(llm_ctx *ctx, float temperature, uint64_t seed, int reset_draws);
+/* The generator: u in [0, 1) for (seed, slot, counter); SplitMix64 of a per-slot key plus the
+ * counter, top 53 bits. */
+double llm_sample_uniform(uint64_t seed, int32_t slot, uint64_t counter);
+/* Test hook: the device sampler on host logits [rows, vocab] with explicit uniforms u[rows]. */
+int llm_debug_sample(int device, const float *logits, int rows, int vocab, float temperature,
+                     const double *u, int32_t *out);
 
 /* ---------------------------------------------------------------- execution options */
 #define LLM_OPT_CUDA_GRAPHS 1  /* replay each decode step as a captured CUDA graph (default 1)   */

@@ -413,6 +413,34 @@ static uint64_t splitmix64(uint64_t x) {
   return x ^ (x >> 31);
 }
 
+/* The sampling uniform of the CUDA path's documented generator: a per-stream key from the
+ * seed, then SplitMix64 of key + counter, top 53 bits scaled to [0, 1). */
+double oracle_uniform(uint64_t seed, uint64_t stream, uint64_t counter) {
+  const uint64_t key = splitmix64(seed ^ splitmix64(stream * 0xD1B54A32D192ED03ull + 0x8CB92BA72F3D8DD7ull));
+  return (double)(splitmix64(key + counter) >> 11) * (1.0 / 9007199254740992.0);
+}
+
+/* ane/stories/infer.go:347-371 sampleFromLogits with the uniform u given: temperature <= 1e-6
+ * -> argmax; else f32 max, invT = float64(f32 1/temperature), total = sequential float64 sum
+ * of exp((f64(l) - f64(mx)) * invT), target = u * total, first i whose running sum >= target,
+ * else n - 1. */
+int oracle_sample_from_logits(const float *logits, int n, float temperature, double u) {
+  if (temperature <= 1e-6f) return oracle_argmax(logits, n);
+  float mx = logits[0];
+  for (int i = 1; i < n; i++)
+    if (logits[i] > mx) mx = logits[i];
+  const double inv_t = (double)(1.0f / temperature);
+  double total = 0.0;
+  for (int i = 0; i < n; i++) total += exp(((double)logits[i] - (double)mx) * inv_t);
+  const double target = u * total;
+  double acc = 0.0;
+  for (int i = 0; i < n; i++) {
+    acc += exp(((double)logits[i] - (double)mx) * inv_t);
+    if (acc >= target) return i;
+  }
+  return n - 1;
+}
+
 void oracle_seq_fill_kv_synthetic(const oracle_model *m, oracle_seq *s, int n_pos, uint64_t seed) {
   const oracle_config *c = &m->c;
   if (n_pos > c->max_seq) n_pos = c->max_seq;

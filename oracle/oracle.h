@@ -17,6 +17,7 @@
  *   ane/stories/infer.go:313-322  matVec: serial f32 sum per output row
  *   ane/stories/infer.go:324-326  silu via float64 exp
  *   ane/stories/infer.go:328-345  softmaxPrefix: f32 max, float64 exp/sum, f32 probs
+ *   ane/stories/infer.go:347-371  sampleFromLogits (uniform given; Go's math/rand is not restated)
  *   ane/stories/infer.go:373-383  argmax: strict '>' (first maximum wins)
  *   training/training_dynamic/io.h:434-455   GQA head map kv_head = q_head / (heads/kv_heads)
  *   bridge/ane_bridge.m:374-398   int8 quantiser: scale = maxabs/127 (0 -> 1), v = x/scale,
@@ -108,6 +109,10 @@ int oracle_teacher_forced(const oracle_model *m, oracle_seq *s, const int32_t *t
 
 /* ---- building blocks (known-answer and bit-exact checks) ---- */
 int oracle_argmax(const float *v, int n);
+/* ane/stories/infer.go:347-371 with the uniform given (Go draws it from math/rand). */
+int oracle_sample_from_logits(const float *logits, int n, float temperature, double u);
+/* The CUDA path's counter-based uniform in [0, 1) (stream = sampling stream base + slot). */
+double oracle_uniform(uint64_t seed, uint64_t stream, uint64_t counter);
 void oracle_rmsnorm(float *out, const float *x, const float *w, int n, double eps);
 void oracle_rope_tables(int max_pos, int head_dim, double theta, float *cos_out, float *sin_out);
 void oracle_softmax_prefix(float *dst, const float *src, int n);

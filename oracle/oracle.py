@@ -67,6 +67,8 @@ def lib() -> C.CDLL:
         "oracle_decode": (C.c_int, [C.c_void_p, C.c_void_p, i32p, C.c_int, C.c_int, i32p, i32p, i32p, i32p]),
         "oracle_teacher_forced": (C.c_int, [C.c_void_p, C.c_void_p, i32p, C.c_int, i32p, _FP]),
         "oracle_argmax": (C.c_int, [_FP, C.c_int]),
+        "oracle_sample_from_logits": (C.c_int, [_FP, C.c_int, C.c_float, C.c_double]),
+        "oracle_uniform": (C.c_double, [C.c_uint64, C.c_uint64, C.c_uint64]),
         "oracle_rmsnorm": (None, [_FP, _FP, _FP, C.c_int, C.c_double]),
         "oracle_rope_tables": (None, [C.c_int, C.c_int, C.c_double, _FP, _FP]),
         "oracle_softmax_prefix": (None, [_FP, _FP, C.c_int]),
@@ -235,6 +237,20 @@ def round_f16(x: float) -> float:
 
 def round_bf16(x: float) -> float:
     return lib().oracle_round_bf16(x)
+
+
+SAMPLE_STREAM_BASE = 0x5A4D000000000000
+
+
+def uniform(seed: int, slot: int, counter: int) -> float:
+    """The CUDA path's sampling uniform for sequence slot `slot`, draw number `counter`."""
+    return lib().oracle_uniform(seed, SAMPLE_STREAM_BASE + slot, counter)
+
+
+def sample_from_logits(logits, temperature: float, u: float) -> int:
+    """ane/stories/infer.go:347-371 with the uniform given."""
+    a = f32(logits)
+    return lib().oracle_sample_from_logits(_p(a), a.size, temperature, u)
 
 
 def set_attn_reverse(on: bool):

@@ -164,8 +164,6 @@ def test_stories_decoder_mirror_rules():
     assert r.PromptLength == 40 and r.Tokens == long[-40:]
     with pytest.raises(_abi.LLMError, match=r"prompt token\[1\]=5000 out of range"):
         dec.Decode(None, DecodeOptions(MaxNewTokens=5, PromptTokens=[4, 5000]))
-    with pytest.raises(_abi.LLMError, match="sampling is not implemented"):
-        dec.Decode(None, DecodeOptions(MaxNewTokens=5, Temperature=0.8, PromptTokens=[4]))
     # EvalNextLogits == the logits of a decode step
     lg = dec.EvalNextLogits(7, 0)
     ref = m.seq().forward(7, 0)

@@ -344,3 +344,66 @@ def test_bf16_qwen3_order_sensitivity():
     d = float(np.abs(a - b).max())
     print(f"qwen3 bf16: oracle vs oracle with reversed sums: max |dlogit| = {d:.4f}")
     assert 0.012 <= d < 0.03
+
+
+def _splitmix64(x):
+    m = (1 << 64) - 1
+    x = (x + 0x9E3779B97F4A7C15) & m
+    x = ((x ^ (x >> 30)) * 0xBF58476D1CE4E5B9) & m
+    x = ((x ^ (x >> 27)) * 0x94D049BB133111EB) & m
+    return x ^ (x >> 31)
+
+
+def _uniform_py(seed, stream, counter):
+    m = (1 << 64) - 1
+    key = _splitmix64(seed ^ _splitmix64((stream * 0xD1B54A32D192ED03 + 0x8CB92BA72F3D8DD7) & m))
+    return (_splitmix64((key + counter) & m) >> 11) * (1.0 / 9007199254740992.0)
+
+
+def _sample_py(logits, temperature, u):
+    """ane/stories/infer.go:347-371 restated in plain Python (float64 sums, f32 1/T)."""
+    import math
+    lg = [float(np.float32(v)) for v in logits]
+    if temperature <= 1e-6:
+        return int(np.argmax(np.asarray(logits, np.float32)))
+    mx = lg[0]
+    for v in lg[1:]:
+        if v > mx:
+            mx = v
+    inv_t = float(np.float32(1.0) / np.float32(temperature))
+    total = 0.0
+    for v in lg:
+        total += math.exp((v - mx) * inv_t)
+    target = u * total
+    acc = 0.0
+    for i, v in enumerate(lg):
+        acc += math.exp((v - mx) * inv_t)
+        if acc >= target:
+            return i
+    return len(lg) - 1
+
+
+def test_sampling_uniform_matches_restatement_and_library():
+    from ane import _abi
+    for seed, slot, ctr in [(0, 0, 0), (1234, 5, 17), (2**63 + 11, 255, 2**40), (7, 4095, 3)]:
+        want = _uniform_py(seed, O.SAMPLE_STREAM_BASE + slot, ctr)
+        assert O.uniform(seed, slot, ctr) == want
+        assert _abi.lib().llm_sample_uniform(seed, slot, ctr) == want
+        assert 0.0 <= want < 1.0
+
+
+def test_sample_from_logits_known_answers_and_restatement():
+    # two tokens with weights 1/3 and 1 at T=1 (total 4/3): u <= 1/4 -> 0, else 1
+    lg = np.array([0.0, np.log(3.0)], np.float32)
+    assert O.sample_from_logits(lg, 1.0, 0.2) == 0
+    assert O.sample_from_logits(lg, 1.0, 0.3) == 1
+    assert O.sample_from_logits(lg, 1e-7, 0.0) == 1          # greedy branch
+    assert O.sample_from_logits(np.zeros(5, np.float32), 0.5, 0.0) == 0
+    assert O.sample_from_logits(np.zeros(5, np.float32), 0.5, 0.999999) == 4
+    rng = np.random.default_rng(3)
+    for _ in range(50):
+        n = int(rng.integers(1, 300))
+        lg = (rng.standard_normal(n) * rng.uniform(0.1, 8)).astype(np.float32)
+        t = float(rng.choice([0.0, 0.3, 0.8, 1.0, 1.7]))
+        u = float(rng.random())
+        assert O.sample_from_logits(lg, t, u) == _sample_py(lg, t, u)
