@@ -33,6 +33,9 @@ LLM_DTYPE_W8A8_BF16 = 4
 LLM_WEIGHTS_LLAMA2C = 1
 LLM_WEIGHTS_CHECKPOINT = 2
 
+LLM_ARITH_STORIES = 0
+LLM_ARITH_STORIESANE = 1
+
 DTYPES = {
     "fp16": LLM_DTYPE_F16,
     "bf16": LLM_DTYPE_BF16,
@@ -49,6 +52,7 @@ EXPORTS = [
     "llm_stories_decode_batch", "llm_ctx_stream", "llm_synchronize", "llm_step_kernel_count",
     "llm_memory_bytes", "llm_time_attention", "llm_profile_step", "llm_trace_step", "llm_debug_norm_quant", "llm_debug_gemm_i8",
     "llm_debug_gemm_f16", "llm_debug_read_kv", "llm_gemm_i8_splitk_noalloc", "llm_set_option", "llm_set_sampling", "llm_sample_uniform", "llm_debug_sample",
+    "llm_eval_window",
 ]
 
 LLM_OPT_CUDA_GRAPHS = 1
@@ -129,6 +133,7 @@ def lib() -> C.CDLL:
         "llm_set_sampling": (C.c_int, [C.c_void_p, C.c_float, C.c_uint64, C.c_int]),
         "llm_sample_uniform": (C.c_double, [C.c_uint64, C.c_int32, C.c_uint64]),
         "llm_debug_sample": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_float, C.c_void_p, C.c_void_p]),
+        "llm_eval_window": (C.c_int, [C.c_void_p, C.c_int, i32p, C.c_int, C.c_int, i32p, _FP]),
         "llm_profile_step": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.c_size_t, C.POINTER(C.c_double)]),
         "llm_trace_step": (C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t, C.POINTER(C.c_double)]),
         "llm_debug_norm_quant": (C.c_int, [C.c_int, _FP, _FP, C.c_int, C.c_int, C.c_double, C.POINTER(C.c_int8), _FP]),

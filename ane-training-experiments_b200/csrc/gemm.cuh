@@ -18,7 +18,9 @@
 //   EPI_F32     store fp32 (logits / debug)
 //   EPI_S32     store the raw int32 accumulators (bit-exact int8 GEMM check)
 //   EPI_RESID   out = resid + y                       (:225-228, :236-239)
+//               or resid + a * y (ane/storiesane/residual.go:9, a = 1/sqrt(2 * layers))
 //   EPI_SWIGLU  g_j = silu(h1_j) * h3_j on interleaved W1/W3 rows   (:231-235)
+//               or (h1 * sigmoid(h1)) * h3 (ane/storiesane/accel_other.go:66-71)
 //   EPI_QKV     per-head QK-norm, RoPE (:222, :247-265), q store, paged K/V write (:223)
 //   EPI_ARGMAX  per-row (max, first index) partial per N tile for the greedy token (:373-383)
 #pragma once
@@ -66,7 +68,23 @@ struct GemmParams {
   // memory, which lets a GEMM CTA share an SM with an attention CTA
   int stages;
   TraceRec* trace;  // llm_trace_step (tcgen05 GEMM only)
+  // storiesane arithmetic (ane/storiesane/residual.go:9, accel_other.go:60-71):
+  // EPI_RESID out = resid + resid_scale * y when resid_scale != 0 (0 = out = y + resid);
+  // EPI_SWIGLU silu_form 1 = (h1 * f32(1 / (1 + exp(-h1)))) * h3 (0 = h1 / (1 + exp(-h1)) * h3)
+  float resid_scale;
+  int silu_form;
 };
+
+// SiLU gate of one (h1, h3) pair in the selected form (see GemmParams::silu_form).
+__device__ __forceinline__ float swiglu_pair(float h1, float up, int form) {
+  if (form == 0) return __fmul_rn(__fdiv_rn(h1, __fadd_rn(1.0f, expf(-h1))), up);
+  const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-h1)));
+  return __fmul_rn(__fmul_rn(h1, sig), up);
+}
+// Residual update of one element (see GemmParams::resid_scale).
+__device__ __forceinline__ float resid_add(float y, float r, float scale) {
+  return scale == 0.0f ? __fadd_rn(y, r) : __fadd_rn(r, __fmul_rn(scale, y));
+}
 
 template <typename InT> struct GemmAcc { using type = float; };
 template <> struct GemmAcc<int8_t> { using type = int; };
@@ -286,9 +304,10 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(GemmParams p) {
             const float* rs = p.resid + static_cast<size_t>(r) * p.ldo + cl;
             if (cl + 1 < p.N) {
               float2 rv = *reinterpret_cast<const float2*>(rs);
-              *reinterpret_cast<float2*>(o) = make_float2(__fadd_rn(v0, rv.x), __fadd_rn(v1, rv.y));
+              *reinterpret_cast<float2*>(o) =
+                  make_float2(resid_add(v0, rv.x, p.resid_scale), resid_add(v1, rv.y, p.resid_scale));
             } else if (cl < p.N) {
-              o[0] = __fadd_rn(v0, rs[0]);
+              o[0] = resid_add(v0, rs[0], p.resid_scale);
             }
           } else {
             if (cl < p.N) o[0] = v0;
@@ -306,8 +325,7 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(GemmParams p) {
           const int r = row_of(mt, 2 * h), cl = col_of(nt, 0);
           if (r >= p.M || cl >= p.N) continue;
           const float h1 = value(mt, nt, 2 * h), h3 = value(mt, nt, 2 * h + 1);
-          const float sg = __fdiv_rn(h1, __fadd_rn(1.0f, expf(-h1)));
-          const float gv = __fmul_rn(sg, h3);
+          const float gv = swiglu_pair(h1, h3, p.silu_form);
           const size_t idx = static_cast<size_t>(r) * F + (cl >> 1);
           if (p.swiglu_f32) reinterpret_cast<float*>(p.out)[idx] = gv;
           else reinterpret_cast<OutT*>(p.out)[idx] = ActTraits<OutT>::from_f(gv);

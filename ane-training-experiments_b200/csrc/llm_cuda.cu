@@ -501,6 +501,8 @@ struct llm_ctx {
   unsigned long long* argmax_part = nullptr;
   float* logits = nullptr;
   size_t logits_rows = 0;
+  float* logits_t = nullptr;  // llm_eval_window: channel-first logits [vocab][window]
+  size_t logits_t_rows = 0;
   int *d_seq = nullptr, *d_tok = nullptr, *d_pos = nullptr, *d_next = nullptr, *d_gen_start = nullptr;
   int *d_blk_row0 = nullptr, *d_blk_nq = nullptr, *d_final = nullptr;
   int* d_gen_out = nullptr;
@@ -532,6 +534,10 @@ struct llm_ctx {
   // how one micro-batch's attention launch waits for the other's: 0 = its completion,
   // 1 = all of its CTAs having started (launch-completion event)
   int attn_chain = 1;
+  // layer arithmetic of the forward pass (llm_eval_window selects storiesane's for one call):
+  // residual scale (0 = plain residual) and SiLU gate form, see GemmParams
+  float resid_scale = 0.f;
+  int silu_form = 0;
   // temperature sampling (llm_set_sampling): temperature <= 1e-6 = greedy
   float sample_temp = 0.f;
   double sample_inv_t = 0.0;
@@ -1397,6 +1403,7 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
       p.out = c->x + static_cast<size_t>(P.r0) * D;
       p.resid = c->x + static_cast<size_t>(P.r0) * D;
       p.ldo = D;
+      p.resid_scale = c->resid_scale;
       p.trace = tr("wo", l, P);
       t_prio = prio;
       t_use_pdl = chain_pdl;
@@ -1416,6 +1423,7 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
       p.b_scale = L.s13;
       p.out = bytes(c->gbuf, static_cast<size_t>(P.r0) * F * (i8 ? 4 : ab));
       p.swiglu_f32 = i8 ? 1 : 0;
+      p.silu_form = c->silu_form;
       p.trace = tr("w13", l, P);
       t_prio = prio;
       t_use_pdl = chain_pdl;
@@ -1448,6 +1456,7 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
       p.out = c->x + static_cast<size_t>(P.r0) * D;
       p.resid = c->x + static_cast<size_t>(P.r0) * D;
       p.ldo = D;
+      p.resid_scale = c->resid_scale;
       p.trace = tr("w2", l, P);
       t_prio = prio;
       t_use_pdl = chain_pdl;
@@ -1644,8 +1653,21 @@ extern "C" int llm_decode_step(llm_ctx* c, const int32_t* seq_ids, const int32_t
   return check_device_error(c);
 }
 
+namespace {
+// llm_prefill; with all_rows, every row's logits stay in c->logits ([rows][vocab], one chunk
+// only) and every row's greedy token in c->d_next, without sampling (llm_eval_window).
+int prefill_impl(llm_ctx* c, const int32_t* seq_ids, const int32_t* tokens, const int32_t* lens,
+                 const int32_t* start_pos, int nseq, int32_t* next_tokens, float* logits, bool all_rows);
+}  // namespace
+
 extern "C" int llm_prefill(llm_ctx* c, const int32_t* seq_ids, const int32_t* tokens, const int32_t* lens,
                            const int32_t* start_pos, int nseq, int32_t* next_tokens, float* logits) {
+  return prefill_impl(c, seq_ids, tokens, lens, start_pos, nseq, next_tokens, logits, false);
+}
+
+namespace {
+int prefill_impl(llm_ctx* c, const int32_t* seq_ids, const int32_t* tokens, const int32_t* lens,
+                 const int32_t* start_pos, int nseq, int32_t* next_tokens, float* logits, bool all_rows) {
   RC(check_ready(c));
   if (!seq_ids || !tokens || !lens || !next_tokens) return fail(LLM_ERR_INVALID, "nil buffer");
   if (nseq <= 0 || nseq > c->max_seqs) return fail(LLM_ERR_INVALID, "nseq %d out of range", nseq);
@@ -1669,7 +1691,10 @@ extern "C" int llm_prefill(llm_ctx* c, const int32_t* seq_ids, const int32_t* to
     off += lens[i];
   }
   RC(upload_dirty(c, dirty));
-  if (logits || sampling_on(c)) RC(ensure_logits(c, nseq));
+  if (all_rows && rows.size() > static_cast<size_t>(c->max_rows))
+    return fail(LLM_ERR_INVALID, "%zu rows exceed one chunk of %d", rows.size(), c->max_rows);
+  if (all_rows) RC(ensure_logits(c, static_cast<int>(rows.size())));
+  else if (logits || sampling_on(c)) RC(ensure_logits(c, nseq));
   const int Rmax = c->max_rows;
   size_t r = 0;
   while (r < rows.size()) {
@@ -1695,7 +1720,7 @@ extern "C" int llm_prefill(llm_ctx* c, const int32_t* seq_ids, const int32_t* to
     }
     for (int i = 0; i < R; ++i) {
       const Row& w = rows[r + i];
-      const bool last = (r + i + 1 == rows.size()) || rows[r + i + 1].owner != w.owner;
+      const bool last = all_rows || (r + i + 1 == rows.size()) || rows[r + i + 1].owner != w.owner;
       if (last) {
         h[5 * R + nf++] = i;
         final_owner.push_back(w.owner);
@@ -1717,9 +1742,12 @@ extern "C" int llm_prefill(llm_ctx* c, const int32_t* seq_ids, const int32_t* to
     rs.attn_splits = attn_splits_for(c, nb, max_ctx);
     rs.d_final = c->d_final;
     rs.n_final = nf;
-    rs.d_logits = logits ? c->logits : nullptr;
-    rs.sample = sampling_on(c) && nf > 0;
-    if (nf > 0) {
+    rs.d_logits = logits || all_rows ? c->logits : nullptr;
+    rs.sample = sampling_on(c) && nf > 0 && !all_rows;
+    if (all_rows) {
+      RC(enqueue_forward(c, rs));
+      CU(cudaStreamSynchronize(c->stream));
+    } else if (nf > 0) {
       RC(enqueue_forward(c, rs));
       std::vector<int> nxt(nf);
       CU(cudaMemcpyAsync(nxt.data(), c->d_next, nf * 4, cudaMemcpyDeviceToHost, c->stream));
@@ -1742,6 +1770,96 @@ extern "C" int llm_prefill(llm_ctx* c, const int32_t* seq_ids, const int32_t* to
     }
     r = r1;
   }
+  return check_device_error(c);
+}
+}  // namespace
+
+// Channel-first copy of row-major logits: out[v][r] = in[r][v] (32x32 tiles through shared memory).
+__global__ void __launch_bounds__(256) transpose_rows_kernel(const float* in, int rows, int V, float* out) {
+  __shared__ float tile[32][33];
+  const int v0 = blockIdx.x * 32, r0 = blockIdx.y * 32, tx = threadIdx.x, ty = threadIdx.y;
+  for (int j = ty; j < 32; j += 8)
+    if (r0 + j < rows && v0 + tx < V) tile[j][tx] = in[static_cast<size_t>(r0 + j) * V + v0 + tx];
+  __syncthreads();
+  for (int j = ty; j < 32; j += 8)
+    if (v0 + j < V && r0 + tx < rows) out[static_cast<size_t>(v0 + j) * rows + r0 + tx] = tile[tx][j];
+}
+
+extern "C" int llm_eval_window(llm_ctx* c, int slot, const int32_t* tokens, int seq, int arithmetic,
+                               int32_t* next_token, float* logits_cf) {
+  RC(check_ready(c));
+  if (!tokens || !next_token) return fail(LLM_ERR_INVALID, "nil buffer");
+  if (slot < 0 || slot >= c->max_seqs) return fail(LLM_ERR_INVALID, "sequence %d out of range", slot);
+  if (seq <= 0 || seq > c->max_pos || seq > c->max_rows)
+    return fail(LLM_ERR_INVALID, "window length %d out of range (1..%d)", seq, std::min(c->max_pos, c->max_rows));
+  if (arithmetic != LLM_ARITH_STORIES && arithmetic != LLM_ARITH_STORIESANE)
+    return fail(LLM_ERR_INVALID, "unknown arithmetic %d", arithmetic);
+  RC(set_device(c));
+  struct ArithScope {
+    llm_ctx* c;
+    float r;
+    int f;
+    ~ArithScope() {
+      c->resid_scale = r;
+      c->silu_form = f;
+    }
+  } scope{c, c->resid_scale, c->silu_form};
+  if (arithmetic == LLM_ARITH_STORIESANE) {
+    // ane/storiesane/residual.go:9: float32(1 / sqrt(2 * layers))
+    c->resid_scale = static_cast<float>(1.0 / std::sqrt(2.0 * static_cast<double>(c->cfg.n_layers)));
+    c->silu_form = 1;
+  }
+  RC(llm_seq_release(c, slot));
+  int32_t len = seq, nt = 0;
+  int rc = prefill_impl(c, &slot, tokens, &len, nullptr, 1, &nt, nullptr, true);
+  if (!rc) {
+    const int V = c->cfg.vocab;
+    int32_t* h = c->h_pin;
+    if (sampling_on(c)) {  // the last position's token, drawn from the slot's stream
+      SampleParams sp{};
+      sp.logits = c->logits + static_cast<size_t>(seq - 1) * V;
+      sp.rows = 1;
+      sp.V = V;
+      sp.ld = V;
+      sp.inv_t = c->sample_inv_t;
+      sp.row_index = c->d_final + (seq - 1);
+      sp.seq_ids = c->d_seq;
+      sp.seed = c->sample_seed;
+      sp.draws = c->d_draws;
+      sp.out = c->d_sampled;
+      sample_kernel<<<1, kSampleThreads, 0, c->stream>>>(sp);
+      if (cudaGetLastError() != cudaSuccess) rc = fail(LLM_ERR_CUDA, "sample launch failed");
+      else if (cudaMemcpyAsync(h, c->d_sampled, 4, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
+        rc = fail(LLM_ERR_CUDA, "copy failed");
+    } else if (cudaMemcpyAsync(h, c->d_next + (seq - 1), 4, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess) {
+      rc = fail(LLM_ERR_CUDA, "copy failed");
+    }
+    if (!rc && logits_cf) {
+      if (!c->logits_t || c->logits_t_rows < static_cast<size_t>(seq)) {
+        if (c->logits_t) {
+          cudaStreamSynchronize(c->stream);
+          cudaFree(c->logits_t);
+          c->allocs.erase(std::find(c->allocs.begin(), c->allocs.end(), static_cast<void*>(c->logits_t)));
+          c->logits_t = nullptr;
+        }
+        rc = dalloc_t(c, &c->logits_t, static_cast<size_t>(seq) * V * 4, &c->bytes_other);
+        c->logits_t_rows = rc ? 0 : seq;
+      }
+      if (!rc) {
+        transpose_rows_kernel<<<dim3((V + 31) / 32, (seq + 31) / 32), dim3(32, 8), 0, c->stream>>>(c->logits, seq, V,
+                                                                                                 c->logits_t);
+        if (cudaGetLastError() != cudaSuccess ||
+            cudaMemcpyAsync(logits_cf, c->logits_t, static_cast<size_t>(seq) * V * 4, cudaMemcpyDeviceToHost,
+                            c->stream) != cudaSuccess)
+          rc = fail(LLM_ERR_CUDA, "channel-first logits copy failed");
+      }
+    }
+    if (!rc && cudaStreamSynchronize(c->stream) != cudaSuccess) rc = fail(LLM_ERR_CUDA, "stream sync failed");
+    if (!rc) *next_token = h[0];
+  }
+  const int rc2 = llm_seq_release(c, slot);
+  if (rc) return rc;
+  RC(rc2);
   return check_device_error(c);
 }
 

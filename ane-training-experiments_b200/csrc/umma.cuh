@@ -337,7 +337,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         for (int j = 0; j < 32; ++j) {
           const int ch = ch0 + c * 32 + j;
           if (c * 32 + j < BN && tok_ok && ch < p.N)
-            reinterpret_cast<float*>(p.out)[static_cast<size_t>(tok) * p.ldo + ch] = __fadd_rn(v[j], rs[j]);
+            reinterpret_cast<float*>(p.out)[static_cast<size_t>(tok) * p.ldo + ch] = resid_add(v[j], rs[j], p.resid_scale);
         }
       }
     } else if constexpr (EPI == EPI_SWIGLU) {
@@ -349,8 +349,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         float g[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float h1 = v[2 * i], up = v[2 * i + 1];
-          g[i] = __fmul_rn(__fdiv_rn(h1, __fadd_rn(1.0f, expf(-h1))), up);
+          g[i] = swiglu_pair(v[2 * i], v[2 * i + 1], p.silu_form);
         }
         const int j0 = (ch0 + c * 32) / 2;  // first output channel of the chunk
         if (tok_ok) {

@@ -174,6 +174,23 @@ int llm_stories_decode_batch(llm_ctx *ctx, const int32_t *prompts, const int32_t
                              int max_new, float temperature, int32_t *out_tokens, int32_t *n_tokens,
                              int32_t *prompt_len, int32_t *stopped_on_eos);
 
+/* ---------------------------------------------------------------- full-window evaluation */
+/* Layer arithmetic of llm_eval_window. */
+#define LLM_ARITH_STORIES 0     /* stories.Decoder: x + branch, silu(h1) = h1 / (1 + exp(-h1))    */
+#define LLM_ARITH_STORIESANE 1  /* storiesane CPU forward (ane/storiesane/engine.go:804-842):
+                                   x + a * branch with a = float32(1/sqrt(2 * layers))
+                                   (residual.go:9), gate = (h1 * sigmoid(h1)) * h3
+                                   (accel_other.go:66-71)                                      */
+/* One full window of `seq` tokens at positions 0..seq-1 from an empty cache in sequence slot
+ * `slot` (released before and after): every position's logits, written channel-first as
+ * logits_cf[vocab][seq] when non-NULL (the layout of storiesane.Engine.EvalLogits,
+ * engine.go:363-376), and the next token after the last position in *next_token (greedy, or
+ * sampled per llm_set_sampling from the slot's stream).  seq <= the KV cache's max_pos.
+ * Replaces Engine.evalLogitsInto (engine.go:734-747) / evalLogitsCPUInto (:804-842); the
+ * windowed Engine.Decode (decode.go:18-94) calls it once per generated token. */
+int llm_eval_window(llm_ctx *ctx, int slot, const int32_t *tokens, int seq, int arithmetic,
+                    int32_t *next_token, float *logits_cf);
+
 /* ---------------------------------------------------------------- temperature sampling */
 /* Sample the next tokens with `temperature` (> 1e-6; <= 1e-6 or negative = greedy argmax) as
  * sampleFromLogits does (ane/stories/infer.go:347-371: f32 max, invT = float64(1/T), f64

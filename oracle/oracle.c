@@ -258,7 +258,15 @@ struct oracle_model {
   const float *rms_final;
   layer_t *layers;
   float *rope_cos, *rope_sin;
+  float resid_scale; /* 0: x + branch (stories); else x + resid_scale * branch (storiesane) */
+  int silu_form;     /* 0: h1 / (1 + exp(-h1)); 1: h1 * f32(1 / (1 + exp(-h1))) (storiesane) */
 };
+
+/* Select the storiesane CPU forward's arithmetic (ane/storiesane/engine.go:804-842). */
+void oracle_model_set_storiesane(oracle_model *m, int on) {
+  m->resid_scale = on ? (float)(1.0 / sqrt(2.0 * (double)m->c.n_layers)) : 0.0f;
+  m->silu_form = on ? 1 : 0;
+}
 
 struct oracle_seq {
   const oracle_model *m;
@@ -619,13 +627,25 @@ int oracle_forward(const oracle_model *m, oracle_seq *s, int token, int pos, flo
     memcpy(s->vcache + base, s->v, sizeof(float) * (size_t)m->kv_dim);
     attend(s, l, pos);
     linear(s, s->x2, &L->wo, s->att);
-    for (int i = 0; i < D; i++) s->x2[i] += s->x[i];
+    if (m->resid_scale != 0.0f) /* ane/storiesane/accel_other.go:60-64: base + scale*branch */
+      for (int i = 0; i < D; i++) s->x2[i] = s->x[i] + m->resid_scale * s->x2[i];
+    else
+      for (int i = 0; i < D; i++) s->x2[i] += s->x[i];
 
     oracle_rmsnorm(s->xn, s->x2, L->rms_ffn, D, c->norm_eps);
     linear2(s, s->h1, &L->w1, s->h3, &L->w3, s->xn);
-    for (int i = 0; i < F; i++) s->g[i] = oracle_silu(s->h1[i]) * s->h3[i];
+    if (m->silu_form) /* ane/storiesane/accel_other.go:66-71 */
+      for (int i = 0; i < F; i++) {
+        float sig = (float)(1.0 / (1.0 + exp(-(double)s->h1[i])));
+        s->g[i] = (s->h1[i] * sig) * s->h3[i];
+      }
+    else
+      for (int i = 0; i < F; i++) s->g[i] = oracle_silu(s->h1[i]) * s->h3[i];
     linear(s, s->y, &L->w2, s->g);
-    for (int i = 0; i < D; i++) s->x[i] = s->x2[i] + s->y[i];
+    if (m->resid_scale != 0.0f)
+      for (int i = 0; i < D; i++) s->x[i] = s->x2[i] + m->resid_scale * s->y[i];
+    else
+      for (int i = 0; i < D; i++) s->x[i] = s->x2[i] + s->y[i];
   }
   oracle_rmsnorm(s->xn, s->x, m->rms_final, D, c->norm_eps);
   round_vec(m->act, s->xn, D);

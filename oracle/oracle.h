@@ -19,6 +19,8 @@
  *   ane/stories/infer.go:328-345  softmaxPrefix: f32 max, float64 exp/sum, f32 probs
  *   ane/stories/infer.go:347-371  sampleFromLogits (uniform given; Go's math/rand is not restated)
  *   ane/stories/infer.go:373-383  argmax: strict '>' (first maximum wins)
+ *   ane/storiesane/engine.go:804-842, decode.go:83-94  storiesane full-window forward (residual
+ *                                 scale, gate form) and the BOS left-padded decode window
  *   training/training_dynamic/io.h:434-455   GQA head map kv_head = q_head / (heads/kv_heads)
  *   bridge/ane_bridge.m:374-398   int8 quantiser: scale = maxabs/127 (0 -> 1), v = x/scale,
  *                                 clamp [-128,127], (int8)(v + (v>=0 ? 0.5 : -0.5))
@@ -89,6 +91,10 @@ typedef struct oracle_seq oracle_seq;
 #define ORACLE_ERANGE_POS -3
 
 oracle_model *oracle_model_new(const oracle_config *cfg, const oracle_weights_f32 *w);
+/* 1: the storiesane CPU forward's arithmetic (ane/storiesane/engine.go:804-842): residual
+ * x + a*branch with a = float32(1/sqrt(2*layers)) (residual.go:9, accel_other.go:60-64) and
+ * the gate (h1 * f32(1/(1+exp(-h1)))) * h3 (accel_other.go:66-71); 0: stories.Decoder's. */
+void oracle_model_set_storiesane(oracle_model *m, int on);
 void oracle_model_free(oracle_model *m);
 oracle_seq *oracle_seq_new(const oracle_model *m);
 void oracle_seq_free(oracle_seq *s);

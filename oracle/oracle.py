@@ -59,6 +59,7 @@ def lib() -> C.CDLL:
     sig = {
         "oracle_model_new": (C.c_void_p, [C.POINTER(oracle_config), C.POINTER(oracle_weights_f32)]),
         "oracle_model_free": (None, [C.c_void_p]),
+        "oracle_model_set_storiesane": (None, [C.c_void_p, C.c_int]),
         "oracle_seq_new": (C.c_void_p, [C.c_void_p]),
         "oracle_seq_free": (None, [C.c_void_p]),
         "oracle_seq_reset": (None, [C.c_void_p]),
@@ -103,7 +104,7 @@ def f32(a):
 class Model:
     """oracle_model over fp32 weights given as a dict or as ane.stories.ModelWeights."""
 
-    def __init__(self, cfg: dict, weights, mode: str = "fp32"):
+    def __init__(self, cfg: dict, weights, mode: str = "fp32", storiesane: bool = False):
         self.cfg = dict(cfg)
         self.vocab = cfg["vocab"]
         self.max_seq = cfg["max_seq"]
@@ -128,6 +129,14 @@ class Model:
         self.h = lib().oracle_model_new(C.byref(oc), C.byref(w))
         if not self.h:
             raise ValueError("oracle_model_new rejected the configuration")
+        if storiesane:
+            lib().oracle_model_set_storiesane(self.h, 1)
+
+    def eval_window(self, tokens) -> np.ndarray:
+        """ane/storiesane/engine.go:804-842: logits of every window position, channel-first
+        [vocab, len(tokens)] (positions 0..len-1 from an empty cache)."""
+        _, lg = self.seq().teacher_forced(list(tokens), want_logits=True)
+        return np.ascontiguousarray(lg.T)
 
     def seq(self) -> "Seq":
         return Seq(self)
