@@ -50,7 +50,7 @@ EXPORTS = [
     "llm_seq_release", "llm_prefill", "llm_decode_step", "llm_generate_begin",
     "llm_generate_steps", "llm_generate_end", "llm_generate", "llm_stories_decode",
     "llm_stories_decode_batch", "llm_ctx_stream", "llm_synchronize", "llm_step_kernel_count",
-    "llm_memory_bytes", "llm_time_attention", "llm_profile_step", "llm_trace_step", "llm_debug_norm_quant", "llm_debug_gemm_i8",
+    "llm_memory_bytes", "llm_time_attention", "llm_profile_step", "llm_trace_step", "llm_trace_begin", "llm_trace_end", "llm_debug_norm_quant", "llm_debug_gemm_i8",
     "llm_debug_gemm_f16", "llm_debug_read_kv", "llm_gemm_i8_splitk_noalloc", "llm_set_option", "llm_set_sampling", "llm_sample_uniform", "llm_debug_sample",
     "llm_eval_window",
 ]
@@ -65,6 +65,7 @@ LLM_OPT_ATTN_CHAIN = 7
 LLM_OPT_MICRO_BATCHES = 8
 LLM_OPT_OVERLAP_GRAPHS = 9
 LLM_OPT_CHAIN_PDL = 10
+LLM_OPT_PREFILL_TILES = 11
 
 
 class LLMError(RuntimeError):
@@ -134,6 +135,8 @@ def lib() -> C.CDLL:
         "llm_sample_uniform": (C.c_double, [C.c_uint64, C.c_int32, C.c_uint64]),
         "llm_debug_sample": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_float, C.c_void_p, C.c_void_p]),
         "llm_eval_window": (C.c_int, [C.c_void_p, C.c_int, i32p, C.c_int, C.c_int, i32p, _FP]),
+        "llm_trace_begin": (C.c_int, [C.c_void_p]),
+        "llm_trace_end": (C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t, C.POINTER(C.c_double)]),
         "llm_profile_step": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.c_size_t, C.POINTER(C.c_double)]),
         "llm_trace_step": (C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t, C.POINTER(C.c_double)]),
         "llm_debug_norm_quant": (C.c_int, [C.c_int, _FP, _FP, C.c_int, C.c_int, C.c_double, C.POINTER(C.c_int8), _FP]),

@@ -461,6 +461,16 @@ class Engine:
         _abi.check(_abi.lib().llm_profile_step(self.h, iters, buf, len(buf), C.byref(us)))
         return buf.value.decode(), us.value
 
+    def trace_begin(self) -> None:
+        """Record the launch timeline of the following forward passes (see llm_trace_begin)."""
+        _abi.check(_abi.lib().llm_trace_begin(self.h))
+
+    def trace_end(self):
+        buf = C.create_string_buffer(1 << 17)
+        us = C.c_double()
+        _abi.check(_abi.lib().llm_trace_end(self.h, buf, len(buf), C.byref(us)))
+        return buf.value.decode(), us.value
+
     def trace_step(self):
         """Launch timeline (device globaltimer) of the next decode step of the generate batch."""
         buf = C.create_string_buffer(1 << 17)

@@ -62,10 +62,6 @@ struct AttnCfg {
   static_assert(WARP_BYTES >= 8 * HD * 4 + 64 * 4, "merge area must fit in a warp's ring");
 };
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-}
-
 // Fused per-token quantisation: called by every CTA after it stored its rows' fp32 outputs.
 // The CTA that completes a row (the last of its n_kv_heads producers) reads the whole row back
 // from L2 and applies the bridge quantiser exactly as the row kernel in norm.cuh does.

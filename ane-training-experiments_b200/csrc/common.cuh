@@ -128,6 +128,11 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity)
     if (mbar_try_wait(bar, parity)) return true;
   return false;
 }
+// Order this thread's generic-proxy shared-memory accesses before later async-proxy ones
+// (a bulk copy refilling a buffer that was just read or written).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
 // Bulk (TMA engine) copy of `bytes` contiguous bytes from global to this CTA's shared
 // memory, completing `bytes` of transaction count on mbarrier `bar`.  Both addresses
 // 16-byte aligned, bytes a multiple of 16.

@@ -20,6 +20,7 @@
 
 #include "../../include/llm_cuda.h"
 #include "attention.cuh"
+#include "attn_prefill.cuh"
 #include "common.cuh"
 #include "gemm.cuh"
 #include "norm.cuh"
@@ -263,6 +264,21 @@ cudaError_t attn_launch_t(const AttnParams& p, cudaStream_t s, bool prepare) {
   dim3 grid(p.n_blocks, p.n_kv_heads, p.splits);
   (void)cudaGetLastError();
   return launch_pdl(k, grid, dim3(kAttnWarps * 32), smem, s, p);
+}
+
+template <typename T, int HD>
+cudaError_t attn_prefill_launch_t(const PrefillAttnParams& p, cudaStream_t s, bool prepare) {
+  auto k = attn_prefill_kernel<T, HD>;
+  constexpr int smem = PrefillCfg<T, HD>::SMEM;
+  if (prepare) return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  (void)cudaGetLastError();
+  return launch_pdl(k, dim3(p.n_tiles, p.n_kv_heads), dim3(kPrefillWarps * 32), smem, s, p);
+}
+
+cudaError_t attn_prefill_any(int act, int hd, const PrefillAttnParams& p, cudaStream_t s, bool prepare) {
+  if (act == 1) return hd == 64 ? attn_prefill_launch_t<__half, 64>(p, s, prepare) : attn_prefill_launch_t<__half, 128>(p, s, prepare);
+  return hd == 64 ? attn_prefill_launch_t<__nv_bfloat16, 64>(p, s, prepare)
+                  : attn_prefill_launch_t<__nv_bfloat16, 128>(p, s, prepare);
 }
 
 cudaError_t attn_any(int act, int hd, const AttnParams& p, cudaStream_t s, bool prepare) {
@@ -534,6 +550,7 @@ struct llm_ctx {
   // how one micro-batch's attention launch waits for the other's: 0 = its completion,
   // 1 = all of its CTAs having started (launch-completion event)
   int attn_chain = 1;
+  bool prefill_tiles = true;  // prefill attention by query tiles (attn_prefill_kernel)
   // layer arithmetic of the forward pass (llm_eval_window selects storiesane's for one call):
   // residual scale (0 = plain residual) and SiLU gate form, see GemmParams
   float resid_scale = 0.f;
@@ -608,6 +625,8 @@ int prepare_kernels(llm_ctx* c) {
     }
   AttnParams ap{};
   CU(attn_any(c->act, c->cfg.head_dim, ap, c->stream, true));
+  PrefillAttnParams pp{};
+  CU(attn_prefill_any(c->act, c->cfg.head_dim, pp, c->stream, true));
   CUtensorMap dummy{};
   for (int e : epis)
     for (int bn : {16, 32, 64, 128, 256}) {
@@ -1167,6 +1186,7 @@ struct RowsSpec {
   int* gen_out = nullptr;
   int gen_cap = 0;
   bool sample = false;  // draw the next token with sample_kernel (temperature sampling)
+  bool prefill_tiles = false;  // blocks are query tiles of attn_prefill_kernel (<= 128/group rows)
 };
 
 const CUtensorMap* tmap(llm_ctx* c, const void* ptr, int esz, int k, int rows, int box) {
@@ -1350,6 +1370,41 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
   };
 
   auto attention = [&](const Part& P, int l) -> int {
+    if (rs.prefill_tiles) {  // prefill: query tiles over the paged cache, then the int8 quantiser
+      PrefillAttnParams pp{};
+      pp.q = c->qbuf;
+      pp.kv_pool = c->kv_pool;
+      pp.block_table = c->d_block_table;
+      pp.max_pages_per_seq = c->max_pages_per_seq;
+      pp.seq_ids = c->d_seq;
+      pp.positions = c->d_pos;
+      pp.tile_row0 = rs.d_blk_row0;
+      pp.tile_nq = rs.d_blk_nq;
+      pp.n_tiles = rs.n_blocks;
+      pp.n_heads = k.n_heads;
+      pp.n_kv_heads = k.n_kv_heads;
+      pp.layer = l;
+      pp.n_pages = c->n_pages;
+      pp.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(k.head_dim)));
+      pp.out = c->attn;
+      pp.out_f32 = i8 ? 1 : 0;
+      pp.err = c->d_err;
+      pp.trace = tr("attention", l, P);
+      t_prio = 0;
+      CU(attn_prefill_any(c->act, k.head_dim, pp, P.s, false));
+      if (i8) {
+        NormParams np_{};
+        np_.x = static_cast<const float*>(c->attn);
+        np_.w = nullptr;
+        np_.D = Q;
+        np_.rows = R;
+        np_.q = c->aq;
+        np_.scale = c->as;
+        np_.trace = tr("quant(attn)", l, P);
+        CU(norm_any(c->act, true, np_, P.s));
+      }
+      return LLM_OK;
+    }
     AttnParams ap{};
     ap.q = bytes(c->qbuf, static_cast<size_t>(P.r0) * Q * ab);
     ap.kv_pool = c->kv_pool;
@@ -1589,7 +1644,8 @@ int run_step(llm_ctx* c, int n, int splits, int mode) {
   }
   // overlapped micro-batch steps launch eagerly unless LLM_OPT_OVERLAP_GRAPHS: their
   // cross-stream schedule measured faster from eager launches than from a replayed graph
-  if (!c->use_graphs || (overlap_applies(c, n, true) && !c->overlap_graphs)) return enqueue_forward(c, rs);
+  if (!c->use_graphs || c->tracing || (overlap_applies(c, n, true) && !c->overlap_graphs))
+    return enqueue_forward(c, rs);
   GraphKey key{n, splits, mode | (rs.sample ? 8 : 0)};
   auto it = c->graphs.find(key);
   if (it == c->graphs.end()) {
@@ -1672,7 +1728,10 @@ int prefill_impl(llm_ctx* c, const int32_t* seq_ids, const int32_t* tokens, cons
   if (!seq_ids || !tokens || !lens || !next_tokens) return fail(LLM_ERR_INVALID, "nil buffer");
   if (nseq <= 0 || nseq > c->max_seqs) return fail(LLM_ERR_INVALID, "nseq %d out of range", nseq);
   RC(set_device(c));
-  const int qpos = std::max(1, 8 / c->group);
+  // attention blocks: query tiles of 128/group rows for attn_prefill_kernel (groups dividing
+  // 8), else blocks of 8/group rows for the decode kernel's block-causal mode
+  const bool tiles = c->prefill_tiles && 8 % c->group == 0;
+  const int qpos = tiles ? kPrefillRows / c->group : std::max(1, 8 / c->group);
   // rows (seq, tok, pos, owner)
   struct Row { int seq, tok, pos, owner; };
   std::vector<Row> rows;
@@ -1739,7 +1798,8 @@ int prefill_impl(llm_ctx* c, const int32_t* seq_ids, const int32_t* tokens, cons
     rs.d_blk_row0 = c->d_blk_row0;
     rs.d_blk_nq = c->d_blk_nq;
     rs.n_blocks = nb;
-    rs.attn_splits = attn_splits_for(c, nb, max_ctx);
+    rs.prefill_tiles = tiles;
+    rs.attn_splits = tiles ? 1 : attn_splits_for(c, nb, max_ctx);
     rs.d_final = c->d_final;
     rs.n_final = nf;
     rs.d_logits = logits || all_rows ? c->logits : nullptr;
@@ -2075,6 +2135,7 @@ extern "C" int llm_set_option(llm_ctx* c, int option, int value) {
     case LLM_OPT_OVERLAP: flag = &c->overlap; break;
     case LLM_OPT_OVERLAP_GRAPHS: flag = &c->overlap_graphs; break;
     case LLM_OPT_CHAIN_PDL: flag = &c->chain_pdl; break;
+    case LLM_OPT_PREFILL_TILES: flag = &c->prefill_tiles; break;
     case LLM_OPT_ATTN_CHAIN:
       if (value < 0 || value > 1) return fail(LLM_ERR_INVALID, "attention chain mode %d out of range [0, 1]", value);
       if (c->attn_chain != value) {
@@ -2287,29 +2348,27 @@ extern "C" int llm_profile_step(llm_ctx* c, int iters, char* report, size_t repo
   return check_device_error(c);
 }
 
-extern "C" int llm_trace_step(llm_ctx* c, char* report, size_t report_len, double* step_us) {
-  RC(check_ready(c));
-  if (c->gen_n <= 0) return fail(LLM_ERR_STATE, "llm_generate_begin not called");
-  if (c->gen_steps_done >= c->gen_max_steps)
-    return fail(LLM_ERR_STATE, "no reserved generate step left to trace (reserve one more in llm_generate_begin)");
+namespace {
+// Start recording launch timelines: every following enqueue_forward appends its launches
+// (up to kTraceCap) until trace_finish.
+int trace_begin(llm_ctx* c) {
   RC(set_device(c));
   if (!c->d_trace) RC(dalloc_t(c, &c->d_trace, kTraceCap * sizeof(TraceRec), &c->bytes_other));
-  std::vector<TraceRec> h(kTraceCap);
-  for (auto& r : h) r = TraceRec{~0ull, 0ull, 0ull, 0ull};
+  std::vector<TraceRec> h(kTraceCap, TraceRec{~0ull, 0ull, 0ull, 0ull});
   CU(cudaStreamSynchronize(c->stream));
   CU(cudaMemcpy(c->d_trace, h.data(), kTraceCap * sizeof(TraceRec), cudaMemcpyHostToDevice));
-  // The next step of the generate batch (its position is reserved), launched eagerly in the
-  // current schedule; tokens and positions are not advanced.
-  RowsSpec rs;
-  rs.R = c->gen_n;
-  rs.n_blocks = c->gen_n;
-  rs.attn_splits = c->gen_splits;
   c->trace_labels.clear();
   c->tracing = true;
-  int rc = enqueue_forward(c, rs);
+  return LLM_OK;
+}
+
+// Stop recording and format one line per recorded launch.
+int trace_finish(llm_ctx* c, char* report, size_t report_len, double* span_us) {
   c->tracing = false;
-  if (rc) return rc;
+  RC(set_device(c));
   CU(cudaStreamSynchronize(c->stream));
+  if (!c->d_trace) return fail(LLM_ERR_STATE, "no trace recorded");
+  std::vector<TraceRec> h(kTraceCap);
   CU(cudaMemcpy(h.data(), c->d_trace, kTraceCap * sizeof(TraceRec), cudaMemcpyDeviceToHost));
   unsigned long long t0 = ~0ull, t1 = 0;
   for (size_t i = 0; i < c->trace_labels.size(); ++i)
@@ -2334,8 +2393,39 @@ extern "C" int llm_trace_step(llm_ctx* c, char* report, size_t report_len, doubl
     memcpy(report, out.data(), n);
     report[n] = 0;
   }
-  if (step_us) *step_us = t1 > t0 ? (t1 - t0) * 1e-3 : 0.0;
+  if (span_us) *span_us = t1 > t0 ? (t1 - t0) * 1e-3 : 0.0;
   return check_device_error(c);
+}
+}  // namespace
+
+extern "C" int llm_trace_step(llm_ctx* c, char* report, size_t report_len, double* step_us) {
+  RC(check_ready(c));
+  if (c->gen_n <= 0) return fail(LLM_ERR_STATE, "llm_generate_begin not called");
+  if (c->gen_steps_done >= c->gen_max_steps)
+    return fail(LLM_ERR_STATE, "no reserved generate step left to trace (reserve one more in llm_generate_begin)");
+  RC(trace_begin(c));
+  // The next step of the generate batch (its position is reserved), launched eagerly in the
+  // current schedule; tokens and positions are not advanced.
+  RowsSpec rs;
+  rs.R = c->gen_n;
+  rs.n_blocks = c->gen_n;
+  rs.attn_splits = c->gen_splits;
+  const int rc = enqueue_forward(c, rs);
+  if (rc) {
+    c->tracing = false;
+    return rc;
+  }
+  return trace_finish(c, report, report_len, step_us);
+}
+
+extern "C" int llm_trace_begin(llm_ctx* c) {
+  RC(check_ready(c));
+  return trace_begin(c);
+}
+
+extern "C" int llm_trace_end(llm_ctx* c, char* report, size_t report_len, double* span_us) {
+  if (!c) return fail(LLM_ERR_INVALID, "nil context");
+  return trace_finish(c, report, report_len, span_us);
 }
 
 extern "C" int llm_debug_read_kv(llm_ctx* c, int layer, int seq, int pos, float* kout, float* vout) {

@@ -225,6 +225,8 @@ int llm_debug_sample(int device, const float *logits, int rows, int vocab, float
                                     measured faster for this schedule)                          */
 #define LLM_OPT_CHAIN_PDL 10    /* overlap mode: programmatic dependent launch between the kernels of a
                                     micro-batch's projection chain (attention excluded)        */
+#define LLM_OPT_PREFILL_TILES 11 /* prefill attention by query tiles of 128/group positions (default 1);
+                                     0 = the decode kernel's blocks of 8/group positions       */
 #define LLM_OPT_ATTN_CHAIN 7   /* overlap mode: a micro-batch's attention launch starts once every CTA of
                                   the other's has started (1, default) or once it completed (0)  */
 /* Set an execution option (value 0/1).  Results do not depend on the options beyond fp32
@@ -260,6 +262,12 @@ int llm_profile_step(llm_ctx *ctx, int iters, char *report, size_t report_len, d
  * start, the spread of CTA start times, the last CTA end (microseconds from the step's first
  * CTA, device globaltimer) and its CTA count.  step_us receives first start to last end. */
 int llm_trace_step(llm_ctx *ctx, char *report, size_t report_len, double *step_us);
+/* Record the launch timeline of every forward pass enqueued between llm_trace_begin and
+ * llm_trace_end (prefill chunks, decode steps, window evaluations; at most 1024 launches),
+ * then report it as llm_trace_step does.  While recording, decode steps launch eagerly (no
+ * CUDA graph replay), so every launch carries its record. */
+int llm_trace_begin(llm_ctx *ctx);
+int llm_trace_end(llm_ctx *ctx, char *report, size_t report_len, double *span_us);
 
 /* ---------------------------------------------------------------- allocation-free entry point */
 /* No counterpart in the reference.  Split-K int8 GEMM C[M,N] = A[M,K] . B[N,K]^T with int32

@@ -234,3 +234,33 @@ def test_overlapped_microbatches_equal_single_stream(cfg, dtype, batch, parts, g
     pick = [0, batch // 2 - 1, batch // 2 + 7, batch - 1]
     worst, agree, _ = oracle_check(m, [prompts[i] for i in pick], [t1[i] for i in pick], [l1[i] for i in pick])
     assert worst <= LOGIT_TOL[dtype] and agree >= TOP1_MIN[dtype], (worst, agree)
+
+
+@pytest.mark.parametrize("cfg,dtype", [(TINY_GQA, "bf16"), (TINY_GQA, "w8a8_bf16"), (TINY_MHA, "fp16")],
+                         ids=["gqa-bf16", "gqa-w8a8", "mha-fp16"])
+def test_prefill_query_tiles_long_prompts(cfg, dtype):
+    """Prompts spanning several 64-position KV tiles and several query tiles (128/group
+    positions), ragged at every boundary, one continued from a cached prefix: the tiled prefill
+    attention must meet the oracle, and agree with the decode kernel's block mode."""
+    w = weights(cfg)
+    rng = np.random.default_rng(17)
+    lens = [1, 63, 64, 65, 129, 200, 300]
+    prompts = [rng.integers(3, cfg.vocab, L).tolist() for L in lens]
+    m = O.Model(cfg.oracle_dict(), w, dtype)
+    results = {}
+    for tiles in (1, 0):
+        eng = engine(cfg, dtype, w, max_batch=len(lens) + 1, max_pos=320)
+        eng.set_option(_abi.LLM_OPT_PREFILL_TILES, tiles)
+        toks, logits = gpu_run(eng, prompts, steps=4)
+        # a prompt continued from its cached first 100 positions
+        p = prompts[-1]
+        eng.prefill([len(lens)], [p[:100]])
+        nxt, lg = eng.prefill([len(lens)], [p[100:]], start_pos=[100], want_logits=True)
+        eng.close()
+        worst, agree, n = oracle_check(m, prompts, toks, logits)
+        print(f"{cfg.name} {dtype} tiles={tiles}: max|dlogit|={worst:.3e} top1={agree:.4f}")
+        assert worst <= LOGIT_TOL[dtype] and agree >= TOP1_MIN[dtype], (tiles, worst, agree)
+        assert np.abs(lg[0] - logits[-1][0]).max() <= LOGIT_TOL[dtype]
+        results[tiles] = logits
+    for a, b in zip(results[0], results[1]):
+        assert np.abs(a - b).max() <= LOGIT_TOL[dtype]
