@@ -49,7 +49,7 @@ EXPORTS = [
     "llm_load_weights_synthetic", "llm_synth_normal", "llm_synth_stream", "llm_kv_alloc",
     "llm_seq_release", "llm_prefill", "llm_decode_step", "llm_generate_begin",
     "llm_generate_steps", "llm_generate_end", "llm_generate", "llm_stories_decode",
-    "llm_stories_decode_batch", "llm_ctx_stream", "llm_synchronize", "llm_step_kernel_count",
+    "llm_stories_decode_batch", "llm_ctx_stream", "llm_synchronize", "llm_step_kernel_count", "llm_step_parts",
     "llm_memory_bytes", "llm_time_attention", "llm_profile_step", "llm_trace_step", "llm_trace_begin", "llm_trace_end", "llm_debug_norm_quant", "llm_debug_gemm_i8",
     "llm_debug_gemm_f16", "llm_debug_read_kv", "llm_gemm_i8_splitk_noalloc", "llm_set_option", "llm_set_sampling", "llm_sample_uniform", "llm_debug_sample",
     "llm_eval_window",
@@ -128,6 +128,7 @@ def lib() -> C.CDLL:
         "llm_ctx_stream": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
         "llm_synchronize": (C.c_int, [C.c_void_p]),
         "llm_step_kernel_count": (C.c_int, [C.c_void_p, C.c_int, i32p]),
+        "llm_step_parts": (C.c_int, [C.c_void_p, C.c_int, i32p]),
         "llm_memory_bytes": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
         "llm_time_attention": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
         "llm_load_weights_file": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int]),

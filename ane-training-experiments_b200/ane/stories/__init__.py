@@ -436,6 +436,12 @@ class Engine:
     def synchronize(self) -> None:
         _abi.check(_abi.lib().llm_synchronize(self.h))
 
+    def step_parts(self, n: int) -> int:
+        """Micro-batches a decode step of n sequences runs as (1 = single stream)."""
+        k = C.c_int32()
+        _abi.check(_abi.lib().llm_step_parts(self.h, n, C.byref(k)))
+        return k.value
+
     def kernel_count(self, n: int) -> int:
         v = C.c_int32()
         _abi.check(_abi.lib().llm_step_kernel_count(self.h, n, C.byref(v)))

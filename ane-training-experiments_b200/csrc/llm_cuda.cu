@@ -538,13 +538,16 @@ struct llm_ctx {
   std::map<GraphKey, cudaGraphExec_t> graphs;
   bool use_graphs = true;
   bool use_umma = true;  // tcgen05 GEMMs (false: the warp-level mma.sync GEMMs)
-  // programmatic dependent launch between the step's kernels: off by default, it measured
-  // 2% slower on the Qwen3 W8A8 decode step (9.47 vs 9.28 ms at 256 sequences)
-  bool use_pdl = false;
-  // Overlapped decode: the batch runs as two micro-batches on two streams whose attention
-  // launches alternate, so one micro-batch's projections and row kernels (latency-bound)
-  // run while the other's attention (HBM-bound) streams the KV cache.
-  bool overlap = true;
+  // programmatic dependent launch between the kernels of single-stream steps and prefill:
+  // measured 2-8% faster on latency-bound steps (Stories110M fp16 x 64: 0.749 -> 0.692 ms;
+  // Qwen3 bf16 x 128 at context 768: 3.79 -> 3.65 ms).  Overlapped steps do not use it (a
+  // waiting dependent CTA holds SM resources the other micro-batches' attention needs), unless
+  // chain_pdl.
+  bool use_pdl = true;
+  // Overlapped decode: the batch runs as micro-batches on their own streams whose attention
+  // launches form a chain, so one micro-batch's projections and row kernels (latency-bound)
+  // run while the others' attention (HBM-bound) streams the KV cache.
+  int overlap = 1;  // 0 off, 1 when the step's K/V time covers the host launches, 2 always
   int overlap_ring_kb = 100;  // tcgen05 stage ring in overlap mode: fits beside an attention CTA
   int attn_splits = 0;        // decode attention splits per sequence (0 = chosen per batch)
   // how one micro-batch's attention launch waits for the other's: 0 = its completion,
@@ -566,6 +569,7 @@ struct llm_ctx {
   TraceRec* d_trace = nullptr;
   std::vector<std::string> trace_labels;
   int micro_batches = 4;      // micro-batches of the overlapped schedule (2..kMaxParts)
+  double step_kv_positions = 0;  // sum over the step's rows of their context lengths
   bool overlap_graphs = false;  // capture overlapped steps in CUDA graphs (eager launches measured faster)
   bool chain_pdl = false;       // overlap mode: programmatic dependent launch within projection chains
   cudaStream_t xstream[3] = {nullptr, nullptr, nullptr};  // micro-batches 1.. (0 runs on `stream`)
@@ -1235,11 +1239,23 @@ struct Part {
 
 
 // Micro-batches a decode step over R rows runs as (1 = the single-stream schedule): up to
-// LLM_OPT_MICRO_BATCHES, each at least kOverlapMinPartRows rows.
+// LLM_OPT_MICRO_BATCHES, each at least kOverlapMinPartRows rows, and only as many as the step
+// can afford.  Overlapped steps launch eagerly, so the host must enqueue a step's launches
+// faster than the device streams its K/V cache: with ~kEagerLaunchUs of host time per launch,
+// a k-part step needs k * (launches per part) * kEagerLaunchUs <= (K/V bytes of the step at
+// kHbmBytesPerUs) / kOverlapHostMargin.  Shorter contexts keep the single-stream graph.
+constexpr double kEagerLaunchUs = 4.0;
+constexpr double kHbmBytesPerUs = 6.5e6;
+constexpr double kOverlapHostMargin = 1.2;
 int overlap_parts(const llm_ctx* c, int R, bool decode_rows) {
   if (!c->overlap || !c->use_umma || !decode_rows) return 1;
-  const int k = std::min(std::min(c->micro_batches, kMaxParts), R / kOverlapMinPartRows);
-  return k >= 2 ? k : 1;
+  const int kmax = std::min(std::min(c->micro_batches, kMaxParts), R / kOverlapMinPartRows);
+  const int L = c->cfg.n_layers;
+  const int per_part = 1 + L * (6 + (c->in8 ? 1 : 0)) + (L - 1);
+  const double kv_us = c->step_kv_positions * 2.0 * c->kv_dim * act_bytes(c) * L / kHbmBytesPerUs;
+  for (int k = kmax; k >= 2; --k)
+    if (c->overlap == 2 || (k * per_part + 3) * kEagerLaunchUs * kOverlapHostMargin <= kv_us) return k;
+  return 1;
 }
 bool overlap_applies(const llm_ctx* c, int R, bool decode_rows) { return overlap_parts(c, R, decode_rows) > 1; }
 // Temperature sampling replaces the greedy argmax (sampleFromLogits, infer.go:347-349).
@@ -1296,7 +1312,8 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
   const int ring_kb = overlap ? c->overlap_ring_kb : 0;
   const int prio = overlap ? c->prio_hi : 0;
   // programmatic dependent launch inside a micro-batch's projection chain (not for attention)
-  const bool chain_pdl = c->use_pdl || (overlap && c->chain_pdl);
+  const bool chain_pdl = overlap ? c->chain_pdl : c->use_pdl;
+  t_use_pdl = overlap ? false : c->use_pdl;
   auto bytes = [](const void* base, size_t off) -> void* {
     return const_cast<uint8_t*>(static_cast<const uint8_t*>(base)) + off;
   };
@@ -1433,7 +1450,7 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
       ap.row_counters = c->row_counters + P.r0;
     }
     t_prio = 0;
-    t_use_pdl = c->use_pdl;
+    t_use_pdl = overlap ? false : c->use_pdl;
     // overlapped schedule: this launch's "all CTAs started" event gates the other micro-batch's
     // next attention launch, which then fills the tail wave of this one
     t_lc_event = overlap && c->attn_chain == 1 ? c->ev_att[P.idx] : nullptr;
@@ -1545,7 +1562,7 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
     }
   }
   t_prio = 0;
-  t_use_pdl = c->use_pdl;
+  t_use_pdl = overlap ? false : c->use_pdl;
   for (int h = 1; h < np; ++h) {
     CU(cudaEventRecord(c->ev_join, parts[h].s));
     CU(cudaStreamWaitEvent(c->stream, c->ev_join, 0));
@@ -1679,14 +1696,17 @@ extern "C" int llm_decode_step(llm_ctx* c, const int32_t* seq_ids, const int32_t
   RC(set_device(c));
   std::vector<int> dirty;
   int max_ctx = 0;
+  double kv_positions = 0;
   for (int i = 0; i < n; ++i) {
     RC(validate_row(c, seq_ids[i], tokens[i], positions[i]));
     for (int j = 0; j < i; ++j)
       if (seq_ids[j] == seq_ids[i]) return fail(LLM_ERR_INVALID, "sequence %d appears twice in one step", seq_ids[i]);
     RC(ensure_pages(c, seq_ids[i], positions[i], &dirty));
     max_ctx = std::max(max_ctx, positions[i] + 1);
+    kv_positions += positions[i] + 1.0;
   }
   RC(upload_dirty(c, dirty));
+  c->step_kv_positions = kv_positions;
   int32_t* h = c->h_pin;
   memcpy(h, seq_ids, n * 4);
   memcpy(h + n, tokens, n * 4);
@@ -1932,6 +1952,7 @@ extern "C" int llm_generate_begin(llm_ctx* c, const int32_t* seq_ids, const int3
   RC(set_device(c));
   std::vector<int> dirty;
   int max_ctx = 0;
+  double kv_positions = 0;
   for (int i = 0; i < n; ++i) {
     RC(validate_row(c, seq_ids[i], tokens[i], positions[i]));
     if (positions[i] + max_steps - 1 >= c->max_pos)
@@ -1940,6 +1961,7 @@ extern "C" int llm_generate_begin(llm_ctx* c, const int32_t* seq_ids, const int3
       if (seq_ids[j] == seq_ids[i]) return fail(LLM_ERR_INVALID, "sequence %d appears twice", seq_ids[i]);
     RC(ensure_pages(c, seq_ids[i], positions[i] + max_steps - 1, &dirty));
     max_ctx = std::max(max_ctx, positions[i] + max_steps);
+    kv_positions += positions[i] + 0.5 * max_steps + 0.5;
   }
   RC(upload_dirty(c, dirty));
   if (sampling_on(c)) RC(ensure_logits(c, n));
@@ -1981,6 +2003,7 @@ extern "C" int llm_generate_begin(llm_ctx* c, const int32_t* seq_ids, const int3
   c->gen_steps_done = 0;
   c->gen_max_steps = max_steps;
   c->gen_splits = attn_splits_for(c, n, max_ctx);
+  c->step_kv_positions = kv_positions;
   c->gen_seq.assign(seq_ids, seq_ids + n);
   c->gen_pos0.assign(positions, positions + n);
   return LLM_OK;
@@ -2132,7 +2155,16 @@ extern "C" int llm_set_option(llm_ctx* c, int option, int value) {
     case LLM_OPT_CUDA_GRAPHS: flag = &c->use_graphs; break;
     case LLM_OPT_TCGEN05_GEMM: flag = &c->use_umma; break;
     case LLM_OPT_PDL: flag = &c->use_pdl; break;
-    case LLM_OPT_OVERLAP: flag = &c->overlap; break;
+    case LLM_OPT_OVERLAP:
+      if (value < 0 || value > 2) return fail(LLM_ERR_INVALID, "overlap mode %d out of range [0, 2]", value);
+      if (c->overlap != value) {
+        RC(set_device(c));
+        CU(cudaStreamSynchronize(c->stream));
+        for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
+        c->graphs.clear();
+        c->overlap = value;
+      }
+      return LLM_OK;
     case LLM_OPT_OVERLAP_GRAPHS: flag = &c->overlap_graphs; break;
     case LLM_OPT_CHAIN_PDL: flag = &c->chain_pdl; break;
     case LLM_OPT_PREFILL_TILES: flag = &c->prefill_tiles; break;
@@ -2194,6 +2226,12 @@ extern "C" int llm_synchronize(llm_ctx* c) {
   RC(set_device(c));
   CU(cudaStreamSynchronize(c->stream));
   return check_device_error(c);
+}
+
+extern "C" int llm_step_parts(llm_ctx* c, int n, int* parts) {
+  if (!c || !parts) return fail(LLM_ERR_INVALID, "nil argument");
+  *parts = overlap_parts(c, n, true);
+  return LLM_OK;
 }
 
 extern "C" int llm_step_kernel_count(llm_ctx* c, int n, int* count) {

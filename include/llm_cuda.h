@@ -212,11 +212,14 @@ int llm_debug_sample(int device, const float *logits, int rows, int vocab, float
 /* ---------------------------------------------------------------- execution options */
 #define LLM_OPT_CUDA_GRAPHS 1  /* replay each decode step as a captured CUDA graph (default 1)   */
 #define LLM_OPT_TCGEN05_GEMM 2 /* tcgen05 projections (default 1); 0 = warp-level mma.sync ones   */
-#define LLM_OPT_PDL 3          /* programmatic dependent launch between step kernels (default 0) */
+#define LLM_OPT_PDL 3          /* programmatic dependent launch between the kernels of single-stream
+                                  steps and prefill chunks (default 1)                           */
 #define LLM_OPT_OVERLAP 4      /* decode batches of >= 64 sequences run as micro-batches (of >= 32
                                   sequences, at most LLM_OPT_MICRO_BATCHES) on their own streams
                                   whose attention launches form a chain, overlapping one
-                                  micro-batch's projections with the others' attention (default 1) */
+                                  micro-batch's projections with the others' attention:
+                                  0 never, 1 when the step's K/V streaming time covers the host's
+                                  eager launches (default; see llm_step_parts), 2 always         */
 #define LLM_OPT_OVERLAP_RING_KB 5 /* shared memory (KB) of a projection's stage ring in overlap
                                      mode, so it fits beside an attention CTA (default 100)     */
 #define LLM_OPT_ATTN_SPLITS 6  /* decode attention splits per sequence; 0 = chosen per batch (default) */
@@ -238,8 +241,13 @@ int llm_set_option(llm_ctx *ctx, int option, int value);
 /* The context's CUDA stream (cudaStream_t) so callers can record events on it. */
 int llm_ctx_stream(llm_ctx *ctx, void **stream);
 int llm_synchronize(llm_ctx *ctx);
-/* Number of kernel launches one decode step of n sequences makes. */
+/* Number of kernel launches one decode step of n sequences makes (for the contexts of the
+ * last llm_decode_step / llm_generate_begin). */
 int llm_step_kernel_count(llm_ctx *ctx, int n, int *count);
+/* Micro-batches such a step runs as (1 = the single-stream, graph-replayed schedule).  The
+ * overlapped schedule is chosen when the step's K/V bytes take the device longer to stream
+ * than the host needs to enqueue the extra launches (it launches eagerly). */
+int llm_step_parts(llm_ctx *ctx, int n, int *parts);
 /* Device bytes held by the context (weights, KV pool, buffers, workspace). */
 int llm_memory_bytes(llm_ctx *ctx, uint64_t *weights, uint64_t *kv_pool, uint64_t *other);
 /* Time `iters` back-to-back launches of the attention kernel of every layer for the

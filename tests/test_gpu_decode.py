@@ -215,8 +215,9 @@ def test_overlapped_microbatches_equal_single_stream(cfg, dtype, batch, parts, g
     runs = []
     for overlap in (0, 1):
         eng = engine(cfg, dtype, w, max_batch=batch, max_pos=96)
-        eng.set_option(_abi.LLM_OPT_OVERLAP, overlap)
+        eng.set_option(_abi.LLM_OPT_OVERLAP, 2 * overlap)  # 2: overlap regardless of the cost rule
         eng.set_option(_abi.LLM_OPT_MICRO_BATCHES, parts)
+        assert eng.step_parts(batch) == (parts if overlap else 1)
         eng.set_option(_abi.LLM_OPT_OVERLAP_GRAPHS, graphs)
         toks, logits = gpu_run(eng, prompts, steps=6)
         seqs = list(range(batch))
