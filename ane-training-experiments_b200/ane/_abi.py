@@ -51,7 +51,7 @@ EXPORTS = [
     "llm_generate_steps", "llm_generate_end", "llm_generate", "llm_stories_decode",
     "llm_stories_decode_batch", "llm_ctx_stream", "llm_synchronize", "llm_step_kernel_count", "llm_step_parts",
     "llm_memory_bytes", "llm_time_attention", "llm_profile_step", "llm_trace_step", "llm_trace_begin", "llm_trace_end", "llm_debug_norm_quant", "llm_debug_gemm_i8",
-    "llm_debug_gemm_f16", "llm_debug_read_kv", "llm_gemm_i8_splitk_noalloc", "llm_set_option", "llm_set_sampling", "llm_sample_uniform", "llm_debug_sample",
+    "llm_debug_gemm_f16", "llm_debug_read_kv", "llm_gemm_i8_splitk_noalloc", "llm_set_option", "llm_set_sampling", "llm_sample_uniform", "llm_debug_sample", "llm_debug_wait_timeout",
     "llm_eval_window",
 ]
 

@@ -2590,6 +2590,36 @@ int debug_gemm(int device, bool in8, int act, const void* hA, const void* hB, si
 }
 }  // namespace
 
+// A wait that nothing completes: one mbarrier expecting an arrival that never comes, polled at
+// most `polls` times, then the kernel records kDevWaitTimeout and returns (the failure path of
+// every bounded wait in the token loop's kernels).
+__global__ void wait_probe_kernel(uint32_t polls, int* err) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  bool done = false;
+  for (uint32_t i = 0; i < polls && !done; ++i) done = mbar_try_wait(smem_u32(&bar), 0);
+  if (!done && threadIdx.x == 0) atomicExch(err, kDevWaitTimeout);
+}
+
+extern "C" int llm_debug_wait_timeout(int device, uint32_t polls) {
+  if (cudaSetDevice(device) != cudaSuccess) return fail(LLM_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+  DevBuf derr;
+  CU(cudaMalloc(&derr.p, 4));
+  CU(cudaMemset(derr.p, 0, 4));
+  wait_probe_kernel<<<1, 32>>>(polls, static_cast<int*>(derr.p));
+  CU(cudaGetLastError());
+  CU(cudaDeviceSynchronize());
+  int h = 0;
+  CU(cudaMemcpy(&h, derr.p, 4, cudaMemcpyDeviceToHost));
+  if (h) return fail(LLM_ERR_DEVICE, "kernel reported device error %d (%s)", h,
+                     h == kDevWaitTimeout ? "bounded wait expired" : "unknown");
+  return LLM_OK;
+}
+
 extern "C" int llm_debug_sample(int device, const float* logits, int rows, int vocab, float temperature,
                                 const double* u, int32_t* out) {
   if (!logits || !u || !out || rows <= 0 || vocab <= 0) return fail(LLM_ERR_INVALID, "bad arguments");

@@ -205,6 +205,10 @@ int llm_set_sampling(llm_ctx *ctx, float temperature, uint64_t seed, int reset_d
 /* The generator: u in [0, 1) for (seed, slot, counter); SplitMix64 of a per-slot key plus the
  * counter, top 53 bits. */
 double llm_sample_uniform(uint64_t seed, int32_t slot, uint64_t counter);
+/* Failure-path test hook: a kernel waits on an mbarrier that nothing completes, gives up after
+ * `polls` polls and records the timeout like every bounded wait of the token loop; the call
+ * returns LLM_ERR_DEVICE ("bounded wait expired") and the device stays usable. */
+int llm_debug_wait_timeout(int device, uint32_t polls);
 /* Test hook: the device sampler on host logits [rows, vocab] with explicit uniforms u[rows]. */
 int llm_debug_sample(int device, const float *logits, int rows, int vocab, float temperature,
                      const double *u, int32_t *out);

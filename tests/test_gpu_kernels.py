@@ -121,3 +121,4 @@ def test_gemm_16bit_matches_fp32_reference(dtype, M, N, K, splits):
     ref = round_to(A, dtype).astype(np.float64) @ round_to(B, dtype).astype(np.float64).T
     scale = np.abs(round_to(A, dtype)).astype(np.float64) @ np.abs(round_to(B, dtype)).astype(np.float64).T
     assert np.all(np.abs(Cm - ref) <= 1e-4 * scale + 1e-6)
+
