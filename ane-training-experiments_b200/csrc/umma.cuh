@@ -298,7 +298,91 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
       }
     };
 
-    if constexpr (EPI == EPI_S32) {
+    // Coalesced output: the stage ring is idle once the accumulator is complete (every MMA has
+    // read its stages and no copy is outstanding), so a tile of per-token rows is written there
+    // and then stored row by row with 16-byte vectors, consecutive threads on consecutive
+    // columns, instead of each thread storing its own row (32 rows per warp instruction).
+    float* const stg = reinterpret_cast<float*>(smem_raw + (sbase - smem_u32(smem_raw)));
+    constexpr int OUT_COLS = EPI == EPI_SWIGLU ? BN / 2 : BN;  // values per token row of the tile
+    constexpr int SP = OUT_COLS + 4;                             // staging pitch (floats)
+    const bool staged = STAGES * STAGE_BYTES >= kUmmaTokens * SP * 4 &&
+                        (EPI == EPI_RESID || EPI == EPI_F32 || EPI == EPI_S32 || EPI == EPI_SWIGLU);
+    auto stage4 = [&](int col, float a, float b, float c_, float d) {
+      *reinterpret_cast<float4*>(stg + tl * SP + col) = make_float4(a, b, c_, d);
+    };
+
+    if (staged && (EPI == EPI_RESID || EPI == EPI_F32 || EPI == EPI_S32)) {
+      for (int c = 0; c < NCH; ++c) {
+        float v[32];
+        if constexpr (EPI == EPI_S32) {
+          uint32_t r[32];
+          tmem_ld32(trow + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(ok ? r[j] : 0u);
+        } else {
+          load_chunk(c, v);
+        }
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+          if (c * 32 + j < BN) stage4(c * 32 + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
+      }
+      epi_bar();
+      // out may alias resid (in-place residual): each element is read and written by one thread
+      constexpr int C4 = BN / 4;
+      for (int idx = et; idx < kUmmaTokens * C4; idx += 128) {
+        const int row = idx / C4, col = 4 * (idx % C4);
+        const int t = tok0 + row, ch = ch0 + col;
+        if (t >= p.M || ch >= p.N) continue;
+        const float4 y = *reinterpret_cast<const float4*>(stg + row * SP + col);
+        float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + static_cast<size_t>(t) * p.ldo + ch);
+        if constexpr (EPI == EPI_RESID) {
+          const float4 r = *reinterpret_cast<const float4*>(p.resid + static_cast<size_t>(t) * p.ldo + ch);
+          *dst = make_float4(resid_add(y.x, r.x, p.resid_scale), resid_add(y.y, r.y, p.resid_scale),
+                             resid_add(y.z, r.z, p.resid_scale), resid_add(y.w, r.w, p.resid_scale));
+        } else {
+          *dst = y;  // fp32 values, or the int32 accumulators' bit patterns
+        }
+      }
+    } else if (staged && EPI == EPI_SWIGLU) {
+      for (int c = 0; c < NCH; ++c) {
+        float v[32];
+        load_chunk(c, v);
+        float g[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) g[i] = swiglu_pair(v[2 * i], v[2 * i + 1], p.silu_form);
+#pragma unroll
+        for (int i = 0; i < 16; i += 4)
+          if (c * 16 + i < OUT_COLS) stage4(c * 16 + i, g[i], g[i + 1], g[i + 2], g[i + 3]);
+      }
+      epi_bar();
+      const int F = p.N / 2, j0 = ch0 / 2;
+      if (p.swiglu_f32) {
+        constexpr int C4 = OUT_COLS / 4;
+        for (int idx = et; idx < kUmmaTokens * C4; idx += 128) {
+          const int row = idx / C4, col = 4 * (idx % C4);
+          const int t = tok0 + row;
+          if (t >= p.M || j0 + col >= F) continue;
+          *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + static_cast<size_t>(t) * F + j0 + col) =
+              *reinterpret_cast<const float4*>(stg + row * SP + col);
+        }
+      } else {
+        constexpr int C8 = OUT_COLS / 8;
+        for (int idx = et; idx < kUmmaTokens * C8; idx += 128) {
+          const int row = idx / C8, col = 8 * (idx % C8);
+          const int t = tok0 + row;
+          if (t >= p.M || j0 + col >= F) continue;
+          const float4 a = *reinterpret_cast<const float4*>(stg + row * SP + col);
+          const float4 b = *reinterpret_cast<const float4*>(stg + row * SP + col + 4);
+          uint4 pk;
+          pk.x = ActTraits<OutT>::pack2(a.x, a.y);
+          pk.y = ActTraits<OutT>::pack2(a.z, a.w);
+          pk.z = ActTraits<OutT>::pack2(b.x, b.y);
+          pk.w = ActTraits<OutT>::pack2(b.z, b.w);
+          *reinterpret_cast<uint4*>(reinterpret_cast<OutT*>(p.out) + static_cast<size_t>(t) * F + j0 + col) = pk;
+        }
+      }
+    } else if constexpr (EPI == EPI_S32) {
       for (int c = 0; c < NCH; ++c) {
         uint32_t r[32];
         tmem_ld32(trow + c * 32, r);
