@@ -548,7 +548,7 @@ struct llm_ctx {
   // launches form a chain, so one micro-batch's projections and row kernels (latency-bound)
   // run while the others' attention (HBM-bound) streams the KV cache.
   int overlap = 1;  // 0 off, 1 when the step's K/V time covers the host launches, 2 always
-  int overlap_ring_kb = 100;  // tcgen05 stage ring in overlap mode: fits beside an attention CTA
+  int overlap_ring_kb = 64;   // tcgen05 stage ring in overlap mode: fits beside two attention CTAs
   int attn_splits = 0;        // decode attention splits per sequence (0 = chosen per batch)
   // how one micro-batch's attention launch waits for the other's: 0 = its completion,
   // 1 = all of its CTAs having started (launch-completion event)

@@ -225,7 +225,7 @@ int llm_debug_sample(int device, const float *logits, int rows, int vocab, float
                                   0 never, 1 when the step's K/V streaming time covers the host's
                                   eager launches (default; see llm_step_parts), 2 always         */
 #define LLM_OPT_OVERLAP_RING_KB 5 /* shared memory (KB) of a projection's stage ring in overlap
-                                     mode, so it fits beside an attention CTA (default 100)     */
+                                     mode, so it fits beside two attention CTAs (default 64)   */
 #define LLM_OPT_ATTN_SPLITS 6  /* decode attention splits per sequence; 0 = chosen per batch (default) */
 #define LLM_OPT_MICRO_BATCHES 8 /* most micro-batches of the overlapped schedule, 2..4 (default 4)  */
 #define LLM_OPT_OVERLAP_GRAPHS 9 /* capture overlapped steps in CUDA graphs (default 0: eager launches,
