@@ -53,17 +53,22 @@ struct AttnParams {
 
 constexpr int kAttnWarps = 4;
 
-// Page-ring depth per warp for head_dim 128 (the ring of head_dim 64 holds twice as many pages).
+// Page-ring depth per warp (pages of 16 positions in flight per warp).
 // Two pages (64 KB per CTA, three CTAs per SM) measured faster than three (96 KB, two per SM):
 // 235.7 vs 240.6 us per Qwen3 layer at 256 sequences x 1536 positions (6.92 vs 6.78 TB/s).
 #ifndef LLM_ATTN_STAGES_HD128
 #define LLM_ATTN_STAGES_HD128 2
 #endif
+// head_dim 64: two pages as well (32 KB per CTA): 28.4 vs 36.3 us per Stories110M layer at 256
+// sequences x ~160 positions against four pages (short contexts want more CTAs per SM).
+#ifndef LLM_ATTN_STAGES_HD64
+#define LLM_ATTN_STAGES_HD64 2
+#endif
 
 template <typename T, int HD>
 struct AttnCfg {
   static constexpr int PAGE_BYTES = 2 * 16 * HD * (int)sizeof(T);
-  static constexpr int STAGES = HD >= 128 ? LLM_ATTN_STAGES_HD128 : 2 * LLM_ATTN_STAGES_HD128;
+  static constexpr int STAGES = HD >= 128 ? LLM_ATTN_STAGES_HD128 : LLM_ATTN_STAGES_HD64;
   static constexpr int WARP_BYTES = STAGES * PAGE_BYTES;
   static constexpr int SMEM = kAttnWarps * WARP_BYTES;
   static_assert(WARP_BYTES >= 8 * HD * 4 + 64 * 4, "merge area must fit in a warp's ring");
