@@ -66,6 +66,8 @@ LLM_OPT_MICRO_BATCHES = 8
 LLM_OPT_OVERLAP_GRAPHS = 9
 LLM_OPT_CHAIN_PDL = 10
 LLM_OPT_PREFILL_TILES = 11
+LLM_OPT_PREFILL_RING_KB = 13
+LLM_OPT_PREFILL_BN = 14
 
 
 class LLMError(RuntimeError):

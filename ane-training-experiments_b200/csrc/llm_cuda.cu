@@ -554,6 +554,11 @@ struct llm_ctx {
   // 1 = all of its CTAs having started (launch-completion event)
   int attn_chain = 1;
   bool prefill_tiles = true;  // prefill attention by query tiles (attn_prefill_kernel)
+  // tcgen05 stage ring of prefill-sized GEMMs (0 = the full ring) and their channel tile
+  // (0 = the widest supported): two 64 KB CTAs per SM measured fastest (Qwen3 W8A8 prefill of
+  // 256 x 1516 tokens 1441 -> 1270 ms; Qwen3 bf16 306 -> 266 ms; Stories W8A8 33.2 -> 28.9 ms)
+  int prefill_ring_kb = 64;
+  int prefill_bn = 128;
   // layer arithmetic of the forward pass (llm_eval_window selects storiesane's for one call):
   // residual scale (0 = plain residual) and SiLU gate form, see GemmParams
   float resid_scale = 0.f;
@@ -1208,7 +1213,16 @@ int gemm(llm_ctx* c, bool in8, int epi, GemmParams p, cudaStream_t stream = null
   const int esz = in8 ? 1 : 2;
   p.argmax_parts = (p.N + argmax_tile_width(c->use_umma) - 1) / argmax_tile_width(c->use_umma);
   if (c->use_umma) {
-    const int bn = umma_bn_for(p.M, p.N, epi, c->cfg.head_dim, c->n_sm);
+    int bn = umma_bn_for(p.M, p.N, epi, c->cfg.head_dim, c->n_sm);
+    // Prefill-sized GEMMs (more tiles than SMs): a smaller stage ring lets two CTAs share an SM,
+    // so one CTA's epilogue overlaps the other's mainloop; 128-wide channel tiles keep the
+    // staged (coalesced) epilogue within that ring.
+    const long long tm = (p.M + kUmmaTokens - 1) / kUmmaTokens;
+    if (c->prefill_ring_kb > 0 && tm * ((p.N + 255) / 256) > c->n_sm) {
+      if (c->prefill_bn > 0 && umma_bn_supported(epi, c->prefill_bn) && epi != EPI_QKV && epi != EPI_ARGMAX)
+        bn = c->prefill_bn;
+      if (ring_kb <= 0) ring_kb = c->prefill_ring_kb;
+    }
     if (ring_kb > 0) p.stages = std::max(2, (ring_kb * 1024 - 1024) / ((kUmmaTokens + bn) * 128));
     const CUtensorMap* tx = tmap(c, p.A, esz, p.K, p.M, kUmmaTokens);
     const CUtensorMap* tw = tmap(c, p.B, esz, p.K, p.N, bn);
@@ -2187,6 +2201,13 @@ extern "C" int llm_set_option(llm_ctx* c, int option, int value) {
         c->graphs.clear();
         c->micro_batches = value;
       }
+      return LLM_OK;
+    case LLM_OPT_PREFILL_RING_KB:
+    case LLM_OPT_PREFILL_BN:
+      if (value < 0 || (option == LLM_OPT_PREFILL_RING_KB && value > 200) ||
+          (option == LLM_OPT_PREFILL_BN && value != 0 && value != 64 && value != 128 && value != 256))
+        return fail(LLM_ERR_INVALID, "option %d value %d out of range", option, value);
+      (option == LLM_OPT_PREFILL_RING_KB ? c->prefill_ring_kb : c->prefill_bn) = value;
       return LLM_OK;
     case LLM_OPT_ATTN_SPLITS:
       if (value < 0 || value > 64) return fail(LLM_ERR_INVALID, "attention splits %d out of range [0, 64]", value);

@@ -137,7 +137,7 @@ __device__ __forceinline__ uint32_t float_key_fast(float f) {
 }
 
 template <typename InT, typename OutT, int BN, int EPI>
-__global__ void __launch_bounds__(kUmmaThreads, 1)
+__global__ void __launch_bounds__(kUmmaThreads, 2)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, GemmParams p) {
   constexpr bool I8 = sizeof(InT) == 1;
   constexpr int MAX_STAGES = umma_stages<BN>();
