@@ -5,9 +5,11 @@
 // training/training_dynamic/io.h:434-455.
 //
 // KV layout in HBM: pages of 16 positions; for (layer, page, kv_head) one contiguous block
-// [K: 16 x hd][V: 16 x hd] of the activation type, each 16-byte chunk c of row s stored at
-// chunk c ^ (s & 7) so ldmatrix reads of 8 rows are bank-conflict free.  A block table
-// maps (sequence, logical page) -> physical page.
+// [K: 16 x hd][V: 16 x hd] of the activation type, each of them laid out by kv_off
+// (common.cuh): 64-element row halves as 128-byte rows of 16 x 128 B sub-blocks, 16-byte chunk
+// c of row s at c ^ (s & 7), so ldmatrix reads of 8 rows are bank-conflict free and a
+// sub-block is a 128B-swizzled K-major tcgen05 operand.  A block table maps (sequence, logical
+// page) -> physical page.
 //
 // One CTA = (query block, kv_head, split).  A query block is up to 8/group consecutive
 // query positions of one sequence (1 for decode); its columns c = qi*group + h cover every
@@ -231,10 +233,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(AttnParams p) {
     const int tok_base = lp * 16;
     if (tok_base + 16 > ctx) {
       // zero V rows past the context so 0-weight x stale data can never produce NaN
-      T* vrow = reinterpret_cast<T*>(wbuf + s * PB + 16 * ROWB);
+      uint8_t* vblk = wbuf + s * PB + 16 * ROWB;
       for (int i = lane; i < 16 * HD / 8; i += 32) {
-        const int rr = i / (HD / 8);
-        if (tok_base + rr >= ctx) reinterpret_cast<uint4*>(vrow)[i] = make_uint4(0, 0, 0, 0);
+        const int rr = i / (HD / 8), c = i % (HD / 8);
+        if (tok_base + rr >= ctx) *reinterpret_cast<uint4*>(vblk + kv_off(rr, c)) = make_uint4(0, 0, 0, 0);
       }
       __syncwarp();
     }
@@ -243,7 +245,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(AttnParams p) {
     for (int ks = 0; ks < KS; ++ks) {
       uint32_t a[4];
       const int row = (lane & 7) + 8 * ((lane >> 3) & 1);
-      ldmatrix_x4(a, kb + swz(row, 2 * ks + (lane >> 4), ROWB));
+      ldmatrix_x4(a, kb + kv_off(row, 2 * ks + (lane >> 4)));
       mma_16816(sacc, a, qb[ks][0], qb[ks][1], T());
     }
     const int tk0 = tok_base + g, tk1 = tk0 + 8;
@@ -294,7 +296,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(AttnParams p) {
     for (int mt = 0; mt < KS; ++mt) {
       uint32_t a[4];
       const int row = (lane & 7) + 8 * (lane >> 4);
-      ldmatrix_x4_trans(a, vb + swz(row, 2 * mt + ((lane >> 3) & 1), ROWB));
+      ldmatrix_x4_trans(a, vb + kv_off(row, 2 * mt + ((lane >> 3) & 1)));
       mma_16816(o[mt], a, bh0, bh1, T());
       mma_16816(o[mt], a, bl0, bl1, T());
     }

@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(kPrefillWarps * 32, 1) attn_prefill_kernel(Pre
       for (int i = threadIdx.x; i < (64 - valid) * (HD / 8); i += kPrefillWarps * 32) {
         const int pr = valid + i / (HD / 8);  // tile-relative position
         const int c = i % (HD / 8);
-        uint4* dst = reinterpret_cast<uint4*>(smem + s * Cfg::STAGE_BYTES + (pr >> 4) * PB + 16 * ROWB + (pr & 15) * ROWB) + c;
+        uint4* dst = reinterpret_cast<uint4*>(smem + s * Cfg::STAGE_BYTES + (pr >> 4) * PB + 16 * ROWB + kv_off(pr & 15, c));
         *dst = make_uint4(0, 0, 0, 0);
       }
       __syncthreads();
@@ -174,7 +174,7 @@ __global__ void __launch_bounds__(kPrefillWarps * 32, 1) attn_prefill_kernel(Pre
           uint32_t b[4];
           const int mi = lane >> 3;
           const int row = ((mi >> 1) << 3) + (lane & 7);
-          ldmatrix_x4(b, st + pg * PB + swz(row, 2 * ks + (mi & 1), ROWB));
+          ldmatrix_x4(b, st + pg * PB + kv_off(row, 2 * ks + (mi & 1)));
           mma_16816(sc[2 * pg], qf[ks], b[0], b[1], T());
           mma_16816(sc[2 * pg + 1], qf[ks], b[2], b[3], T());
         }
@@ -239,7 +239,7 @@ __global__ void __launch_bounds__(kPrefillWarps * 32, 1) attn_prefill_kernel(Pre
         for (int nt = 0; nt < NO; nt += 2) {
           uint32_t b[4];
           const int row = (lane & 7) + 8 * ((lane >> 3) & 1);
-          ldmatrix_x4_trans(b, vb + swz(row, nt + (lane >> 4), ROWB));
+          ldmatrix_x4_trans(b, vb + kv_off(row, nt + (lane >> 4)));
           mma_16816(o[nt], ah, b[0], b[1], T());
           mma_16816(o[nt], al, b[0], b[1], T());
           mma_16816(o[nt + 1], ah, b[2], b[3], T());

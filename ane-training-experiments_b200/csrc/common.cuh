@@ -236,6 +236,14 @@ __device__ __forceinline__ int8_t quant_bridge_fast(float x, float scale, float 
 // Byte offset of 16-byte chunk `chunk` of row `row` in a tile whose rows are `row_bytes`
 // long, XOR-swizzled within each 128-byte group so that 8 consecutive rows reading the
 // same logical chunk hit 8 different bank groups.
+// Byte offset of 16-byte chunk `chunk` (8 elements) of row `row` (0..15) inside the K or the V
+// block of a KV-cache page (16 rows x head_dim 2-byte elements).  Each 64-element half of a row
+// is a 128-byte row of its own 16 x 128 B sub-block (sub-blocks 2 KB apart), with chunk c of
+// row r at position c ^ (r & 7): the 128-byte-swizzle layout of a K-major tcgen05 operand, and
+// bank-conflict free for ldmatrix.  For head_dim 64 this is one sub-block.
+__host__ __device__ __forceinline__ uint32_t kv_off(int row, int chunk) {
+  return static_cast<uint32_t>((chunk >> 3) * 2048 + row * 128 + (((chunk & 7) ^ (row & 7)) << 4));
+}
 __device__ __forceinline__ uint32_t swz(int row, int chunk, int row_bytes) {
   return static_cast<uint32_t>(row * row_bytes + ((chunk ^ (row & 7)) << 4));
 }

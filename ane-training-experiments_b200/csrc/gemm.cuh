@@ -452,9 +452,8 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(GemmParams p) {
         const int slot = pos & 15;
         const size_t blk = ((static_cast<size_t>(p.layer) * p.n_pages + page) * p.n_kv_heads + head) * 2 + (region - 1);
         OutT* base = reinterpret_cast<OutT*>(p.kv_pool) + blk * 16 * hd;
-        // element d of row `slot` lives at chunk (d/8) ^ (slot&7) within the row
-        const int chunk = (d0 >> 3) ^ (slot & 7);
-        OutT* dst = base + slot * hd + chunk * 8 + (d0 & 7);
+        // element d of row `slot` lives in chunk d/8 placed by kv_off (common.cuh)
+        OutT* dst = reinterpret_cast<OutT*>(reinterpret_cast<uint8_t*>(base) + kv_off(slot, d0 >> 3)) + (d0 & 7);
 #pragma unroll
         for (int e = 0; e < 4; ++e)
           if (e < E) dst[e] = ActTraits<OutT>::from_f(v[e]);

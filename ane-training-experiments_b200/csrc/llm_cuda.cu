@@ -167,8 +167,8 @@ __global__ void read_kv_kernel(const T* pool, int layer, int n_pages, int n_kv_h
   const int which = i / kv_dim, j = i % kv_dim, head = j / hd, d = j % hd;
   const size_t blk = ((static_cast<size_t>(layer) * n_pages + page) * n_kv_heads + head) * 2 + which;
   const T* base = pool + blk * 16 * hd;
-  const int chunk = (d >> 3) ^ (slot & 7);
-  const float val = ActTraits<T>::to_f(base[slot * hd + chunk * 8 + (d & 7)]);
+  const float val =
+      ActTraits<T>::to_f(*(reinterpret_cast<const T*>(reinterpret_cast<const uint8_t*>(base) + kv_off(slot, d >> 3)) + (d & 7)));
   (which ? v : k)[j] = val;
 }
 

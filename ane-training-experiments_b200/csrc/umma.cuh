@@ -513,7 +513,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
         } else {
           const size_t blk =
               ((static_cast<size_t>(p.layer) * p.n_pages + page) * p.n_kv_heads + head) * 2 + (region - 1);
-          kv_base = reinterpret_cast<OutT*>(p.kv_pool) + blk * 16 * hd + slot * hd;
+          kv_base = reinterpret_cast<OutT*>(p.kv_pool) + blk * 16 * hd;  // the page's K or V block
         }
       }
       for (int c = 0; c < NCH; ++c) {
@@ -556,10 +556,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
           for (int h = 0; h < 4; ++h) dst[h] = pk[h];
         } else if (kv_base) {
 #pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            const int chunk = ((d0 >> 3) + h) ^ (slot & 7);
-            *reinterpret_cast<uint4*>(kv_base + chunk * 8) = pk[h];
-          }
+          for (int h = 0; h < 4; ++h)
+            *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(kv_base) + kv_off(slot, (d0 >> 3) + h)) = pk[h];
         }
       }
     }
