@@ -68,6 +68,7 @@ LLM_OPT_CHAIN_PDL = 10
 LLM_OPT_PREFILL_TILES = 11
 LLM_OPT_PREFILL_RING_KB = 13
 LLM_OPT_PREFILL_BN = 14
+LLM_OPT_PREFILL_TC = 15
 
 
 class LLMError(RuntimeError):

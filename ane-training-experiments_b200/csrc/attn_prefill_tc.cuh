@@ -1,0 +1,348 @@
+// attn_prefill_tc.cuh -- causal prefill attention on the 5th-generation tensor cores.
+//
+// Reference: ane/stories/infer.go:267-299 (attend: scores q.k/sqrt(hd) over t <= pos,
+// softmaxPrefix, PV) for many query positions of one sequence at once, with the GQA head map
+// kv_head = q_head / group of training/training_dynamic/io.h:434-455.
+//
+// One CTA = (query tile, kv head): 128 score rows, row = h * (128/group) + i for head h of the
+// kv head's group and query position i of the tile; TMEM lane = row.  The sequence's cached
+// K/V pages are streamed 64 positions at a time through a STAGES-deep ring (bulk copies of the
+// pages' 16 x 128 B sub-blocks, see kv_off in common.cuh, placed so that a 64-position tile of
+// every 64-element half of K and V is one 128B-swizzled operand).  Per tile t:
+//   MMA warp:      S_t[128 x 64]  = Q . K_t^T      (tcgen05.mma kind::f16, K-major Q and K,
+//                                                   f32 accumulator in TMEM, double-buffered)
+//   softmax warps: one thread per row reads its 64 scores from TMEM, applies scale and the
+//                  causal mask, updates the running max / sum, rescales its O row in TMEM
+//                  when the max moved, and writes P as two activation-type terms hi + lo
+//                  (the decode kernel's ~16-bit softmax weights) into shared memory
+//   MMA warp:      O[128 x hd] += P_hi . V_t + P_lo . V_t  (P K-major, V MN-major)
+// S_{t+1} is issued before the softmax of t finishes, so the tensor core and the softmax
+// overlap.  Warp 0 = bulk-copy producer, warp 1 = TMEM allocator + MMA issuer (one thread),
+// warps 2..5 = softmax / epilogue.  Every wait is bounded; on expiry the CTA records
+// kDevWaitTimeout, drains its copies and still frees its TMEM.
+#pragma once
+#include "attn_prefill.cuh"
+#include "common.cuh"
+#include "umma.cuh"
+
+namespace llm {
+
+template <typename T, int HD>
+struct PrefillTcCfg {
+  static constexpr int HALVES = HD / 64;              // 64-element halves of a K / V row
+  static constexpr int SUB = 16 * 128;                // one page's half sub-block (bytes)
+  static constexpr int REGION = 4 * SUB;              // 64 positions of one half (bytes)
+  static constexpr int STAGE_BYTES = 2 * HALVES * REGION;  // K halves then V halves
+  static constexpr int STAGES = 3;
+  static constexpr int Q_BYTES = HALVES * 128 * 128;  // 128 rows x HD, K-major halves
+  static constexpr int P_BYTES = 128 * 128;           // 128 rows x 64 positions
+  static constexpr int SMEM = Q_BYTES + 2 * P_BYTES + STAGES * STAGE_BYTES + 1024;
+  static constexpr uint32_t TMEM_COLS = 256;          // S: 2 x 64 columns, O: HD columns at 128
+};
+
+template <typename T, int HD>
+__global__ void __launch_bounds__(192, 1) attn_prefill_tc_kernel(PrefillAttnParams p) {
+  using Cfg = PrefillTcCfg<T, HD>;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr int HALVES = Cfg::HALVES;
+  constexpr int SUB = Cfg::SUB;
+  constexpr int REGION = Cfg::REGION;
+  constexpr int ROWB = HD * (int)sizeof(T);  // bytes of one K or V row in the page block
+  // MN-major V: the second 64-element chunk of hd is the next half's region; with one half
+  // the offset is never applied and stays inside the stage
+  constexpr uint32_t V_LBO = HALVES > 1 ? REGION : 1024;
+
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t kv_full[STAGES], kv_empty[STAGES], s_full[2], p_ready, pv_done, q_ready, drain;
+  __shared__ uint32_t s_tmem;
+
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t q_s = sbase;
+  const uint32_t ph_s = q_s + Cfg::Q_BYTES;
+  const uint32_t pl_s = ph_s + Cfg::P_BYTES;
+  const uint32_t ring = pl_s + Cfg::P_BYTES;
+  uint8_t* const gbase = smem_raw + (sbase - smem_u32(smem_raw));  // generic pointer of sbase
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = p.n_tiles - 1 - static_cast<int>(blockIdx.x);  // longest first
+  const int kvh = blockIdx.y;
+  const int group = p.n_heads / p.n_kv_heads;
+  const int QT = 128 / group;
+
+  griddep_launch_dependents();
+  trace_start(p.trace);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&kv_full[s]), 1);
+      mbar_init(smem_u32(&kv_empty[s]), 1);
+    }
+    mbar_init(smem_u32(&s_full[0]), 1);
+    mbar_init(smem_u32(&s_full[1]), 1);
+    mbar_init(smem_u32(&p_ready), 128);
+    mbar_init(smem_u32(&pv_done), 1);
+    mbar_init(smem_u32(&q_ready), 128);
+    mbar_init(smem_u32(&drain), 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&s_tmem), Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  griddep_wait();
+
+  const int r0 = p.tile_row0[tile];
+  const int nq = p.tile_nq[tile];
+  const int seq = p.seq_ids[r0];
+  const int pos0 = p.positions[r0];
+  const int ctx = pos0 + nq;
+  const int nkv = (ctx + 63) >> 6;            // 64-position K/V tiles the CTA needs
+  const int n_pages_ctx = (ctx + 15) >> 4;
+  bool failed = false;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ bulk-copy producer
+    if (lane == 0) {
+      const T* pool = reinterpret_cast<const T*>(p.kv_pool);
+      const int* bt = p.block_table + static_cast<size_t>(seq) * p.max_pages_per_seq;
+      int issued = 0;
+      for (int t = 0; t < nkv; ++t) {
+        const int s = t % STAGES;
+        if (t >= STAGES && !mbar_wait_bounded(smem_u32(&kv_empty[s]), ((t / STAGES) + 1) & 1)) {
+          failed = true;
+          break;
+        }
+        const int first = 4 * t, np = min(4, n_pages_ctx - first);
+        const uint32_t bar = smem_u32(&kv_full[s]);
+        mbar_arrive_expect_tx(bar, np * 2 * HALVES * SUB);
+        const uint32_t st = ring + s * Cfg::STAGE_BYTES;
+        for (int j = 0; j < np; ++j) {
+          int phys = bt[first + j];
+          if (phys < 0 || phys >= p.n_pages) {
+            if (p.err) atomicExch(p.err, kDevBadPage);
+            phys = 0;
+          }
+          const uint8_t* kblk = reinterpret_cast<const uint8_t*>(
+              pool + ((static_cast<size_t>(p.layer) * p.n_pages + phys) * p.n_kv_heads + kvh) * (2 * 16 * HD));
+          for (int hh = 0; hh < HALVES; ++hh) {
+            bulk_g2s(st + hh * REGION + j * SUB, kblk + hh * SUB, SUB, bar);                          // K half
+            bulk_g2s(st + (HALVES + hh) * REGION + j * SUB, kblk + 16 * ROWB + hh * SUB, SUB, bar);  // V half
+          }
+        }
+        issued = t + 1;
+      }
+      // copies still in flight must land before the CTA's shared memory goes away
+      for (int t = max(0, issued - STAGES); t < issued; ++t)
+        mbar_wait_bounded(smem_u32(&kv_full[t % STAGES]), (t / STAGES) & 1);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = umma_idesc<T>(128, 64);
+      constexpr uint32_t idesc_pv = umma_idesc<T>(128, HD) | (1u << 16);  // B (V) MN-major
+      const uint32_t o_tmem = tmem + 128;
+      auto issue_s = [&](int t) -> bool {
+        const int s = t % STAGES;
+        if (!mbar_wait_bounded(smem_u32(&kv_full[s]), (t / STAGES) & 1)) return false;
+        tc_fence_after();
+        const uint32_t st = ring + s * Cfg::STAGE_BYTES;
+        const uint32_t d = tmem + (t & 1) * 64;
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k) {
+          const int hh = k >> 2, kk = k & 3;
+          umma<false>(d, sw128_desc(q_s + hh * 128 * 128 + 32 * kk), sw128_desc(st + hh * REGION + 32 * kk), idesc_s,
+                      k > 0 ? 1u : 0u);
+        }
+        tc_commit(smem_u32(&s_full[t & 1]));
+        return true;
+      };
+      bool ok = mbar_wait_bounded(smem_u32(&q_ready), 0);
+      if (ok) ok = issue_s(0);
+      if (ok && nkv > 1) ok = issue_s(1);
+      for (int t = 0; ok && t < nkv; ++t) {
+        if (!mbar_wait_bounded(smem_u32(&p_ready), t & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t vst = ring + (t % STAGES) * Cfg::STAGE_BYTES + HALVES * REGION;
+#pragma unroll
+        for (int term = 0; term < 2; ++term) {
+          const uint32_t pa = term == 0 ? ph_s : pl_s;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)  // 16 positions per MMA
+            umma<false>(o_tmem, sw128_desc(pa + 32 * kk), sw128_desc_mn(vst + kk * 2048, V_LBO, 1024), idesc_pv,
+                        (t > 0 || term > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(smem_u32(&kv_empty[t % STAGES]));
+        tc_commit(smem_u32(&pv_done));
+        if (t + 2 < nkv) ok = issue_s(t + 2);
+      }
+      if (!ok) failed = true;
+      // every MMA this thread issued has completed before TMEM is freed (matters on the
+      // timeout path; on the normal path the softmax warps already waited for the last one)
+      tc_commit(smem_u32(&drain));
+      mbar_wait_bounded(smem_u32(&drain), 0);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax / epilogue warps
+    const int q = warp & 3;
+    const int tl = q * 32 + lane;              // score row = TMEM lane
+    const int h = tl / QT, i = tl % QT;
+    const bool row_ok = i < nq;
+    const int lim = row_ok ? pos0 + i : -1;    // last visible position of this row
+    const int head = kvh * group + h;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(q * 32) << 16);
+
+    // Q row -> shared memory, K-major 128B-swizzled halves
+    {
+      const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.q) +
+                                                        (static_cast<size_t>(r0 + (row_ok ? i : 0)) * p.n_heads + head) * HD);
+#pragma unroll
+      for (int c = 0; c < HD / 8; ++c) {
+        const uint4 v = row_ok ? src[c] : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(gbase + (c >> 3) * 128 * 128 + tl * 128 + (((c & 7) ^ (tl & 7)) << 4)) = v;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(smem_u32(&q_ready));
+    }
+
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int t = 0; t < nkv; ++t) {
+      // wait results are made warp-uniform: the TMEM loads below are warp-collective
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&s_full[t & 1]), (t >> 1) & 1))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float sv[64];
+      {
+        uint32_t r[32];
+        tmem_ld32(trow + (t & 1) * 64, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sv[j] = __uint_as_float(r[j]);
+        tmem_ld32(trow + (t & 1) * 64 + 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sv[32 + j] = __uint_as_float(r[j]);
+      }
+      const int kbase = t * 64;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 64; ++j) {
+        sv[j] = kbase + j <= lim ? sv[j] * p.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, sv[j]);
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const float mu = m_new == -INFINITY ? 0.f : m_new;
+      const float alpha = exp2f(m_run - mu);
+      float rs = 0.f;
+#pragma unroll
+      for (int j = 0; j < 64; ++j) {
+        sv[j] = exp2f(sv[j] - mu);
+        rs += sv[j];
+      }
+      l_run = l_run * alpha + rs;
+      m_run = m_new;
+
+      // PV of the previous tile must be complete before O is rescaled and P overwritten
+      if (t > 0) {
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&pv_done), (t - 1) & 1))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll
+          for (int c = 0; c < HD / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(trow + 128 + c * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * alpha);
+            tmem_st32(trow + 128 + c * 32, r);
+          }
+          tmem_wait_st();
+        }
+      }
+      // the tile's V rows past the context were not loaded (or are stale): zero them so a
+      // zero weight times stale shared memory cannot make NaN
+      const int valid = ctx - kbase;
+      if (valid < 64) {
+        uint8_t* vreg = gbase + (ring - sbase) + (t % STAGES) * Cfg::STAGE_BYTES + HALVES * REGION;
+        for (int idx = tl; idx < (64 - valid) * HALVES * 8; idx += 128) {
+          const int rr = valid + idx / (HALVES * 8), rem = idx % (HALVES * 8);
+          *reinterpret_cast<uint4*>(vreg + (rem >> 3) * REGION + rr * 128 + ((rem & 7) << 4)) = make_uint4(0, 0, 0, 0);
+        }
+      }
+      // P row (64 positions) as hi + lo activation-type terms, K-major 128B-swizzled
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint4 hi, lo;
+        uint32_t* hp = reinterpret_cast<uint32_t*>(&hi);
+        uint32_t* lp = reinterpret_cast<uint32_t*>(&lo);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float a = sv[8 * c + 2 * e], b = sv[8 * c + 2 * e + 1];
+          hp[e] = ActTraits<T>::pack2(a, b);
+          const float2 hv = ActTraits<T>::unpack2(hp[e]);
+          lp[e] = ActTraits<T>::pack2(a - hv.x, b - hv.y);
+        }
+        const uint32_t off = tl * 128 + ((c ^ (tl & 7)) << 4);
+        *reinterpret_cast<uint4*>(gbase + (ph_s - sbase) + off) = hi;
+        *reinterpret_cast<uint4*>(gbase + (pl_s - sbase) + off) = lo;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(smem_u32(&p_ready));
+    }
+    if (ok && nkv > 0) {
+      ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&pv_done), (nkv - 1) & 1));
+      tc_fence_after();
+    }
+    if (!ok) failed = true;
+    // O row / l -> output row (fp32, or the activation type)
+    const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
+#pragma unroll
+    for (int c = 0; c < HD / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(trow + 128 + c * 32, r);
+      tmem_wait_ld();
+      if (!row_ok || !ok) continue;
+      const size_t oi = (static_cast<size_t>(r0 + i) * p.n_heads + head) * HD + c * 32;
+      if (p.out_f32) {
+        float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + oi);
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+          dst[j / 4] = make_float4(__uint_as_float(r[j]) * inv, __uint_as_float(r[j + 1]) * inv,
+                                   __uint_as_float(r[j + 2]) * inv, __uint_as_float(r[j + 3]) * inv);
+      } else {
+        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.out) + oi);
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          uint4 v;
+          v.x = ActTraits<T>::pack2(__uint_as_float(r[j]) * inv, __uint_as_float(r[j + 1]) * inv);
+          v.y = ActTraits<T>::pack2(__uint_as_float(r[j + 2]) * inv, __uint_as_float(r[j + 3]) * inv);
+          v.z = ActTraits<T>::pack2(__uint_as_float(r[j + 4]) * inv, __uint_as_float(r[j + 5]) * inv);
+          v.w = ActTraits<T>::pack2(__uint_as_float(r[j + 6]) * inv, __uint_as_float(r[j + 7]) * inv);
+          dst[j / 8] = v;
+        }
+      }
+    }
+  }
+  if (failed && p.err) atomicExch(p.err, kDevWaitTimeout);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  }
+  trace_end(p.trace);
+}
+
+}  // namespace llm

@@ -109,6 +109,9 @@ __device__ __forceinline__ void fence_mbar_init() {
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
 }
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
+}
 // Returns true once the phase with parity `parity` has completed.  The suspend-time hint
 // (nanoseconds) bounds how long a waiting thread sleeps before re-checking: without it the
 // system default applies, and a wait that spans a whole GEMM main loop was observed to round

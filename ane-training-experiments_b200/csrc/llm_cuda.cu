@@ -21,6 +21,7 @@
 #include "../../include/llm_cuda.h"
 #include "attention.cuh"
 #include "attn_prefill.cuh"
+#include "attn_prefill_tc.cuh"
 #include "common.cuh"
 #include "gemm.cuh"
 #include "norm.cuh"
@@ -279,6 +280,22 @@ cudaError_t attn_prefill_any(int act, int hd, const PrefillAttnParams& p, cudaSt
   if (act == 1) return hd == 64 ? attn_prefill_launch_t<__half, 64>(p, s, prepare) : attn_prefill_launch_t<__half, 128>(p, s, prepare);
   return hd == 64 ? attn_prefill_launch_t<__nv_bfloat16, 64>(p, s, prepare)
                   : attn_prefill_launch_t<__nv_bfloat16, 128>(p, s, prepare);
+}
+
+template <typename T, int HD>
+cudaError_t attn_prefill_tc_launch_t(const PrefillAttnParams& p, cudaStream_t s, bool prepare) {
+  auto k = attn_prefill_tc_kernel<T, HD>;
+  constexpr int smem = PrefillTcCfg<T, HD>::SMEM;
+  if (prepare) return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  (void)cudaGetLastError();
+  return launch_pdl(k, dim3(p.n_tiles, p.n_kv_heads), dim3(192), smem, s, p);
+}
+
+cudaError_t attn_prefill_tc_any(int act, int hd, const PrefillAttnParams& p, cudaStream_t s, bool prepare) {
+  if (act == 1)
+    return hd == 64 ? attn_prefill_tc_launch_t<__half, 64>(p, s, prepare) : attn_prefill_tc_launch_t<__half, 128>(p, s, prepare);
+  return hd == 64 ? attn_prefill_tc_launch_t<__nv_bfloat16, 64>(p, s, prepare)
+                  : attn_prefill_tc_launch_t<__nv_bfloat16, 128>(p, s, prepare);
 }
 
 cudaError_t attn_any(int act, int hd, const AttnParams& p, cudaStream_t s, bool prepare) {
@@ -554,6 +571,7 @@ struct llm_ctx {
   // 1 = all of its CTAs having started (launch-completion event)
   int attn_chain = 1;
   bool prefill_tiles = true;  // prefill attention by query tiles (attn_prefill_kernel)
+  bool prefill_tc = true;     // ... on the tcgen05 tensor cores (attn_prefill_tc_kernel)
   // tcgen05 stage ring of prefill-sized GEMMs (0 = the full ring) and their channel tile
   // (0 = the widest supported): two 64 KB CTAs per SM measured fastest (Qwen3 W8A8 prefill of
   // 256 x 1516 tokens 1441 -> 1270 ms; Qwen3 bf16 306 -> 266 ms; Stories W8A8 33.2 -> 28.9 ms)
@@ -636,6 +654,7 @@ int prepare_kernels(llm_ctx* c) {
   CU(attn_any(c->act, c->cfg.head_dim, ap, c->stream, true));
   PrefillAttnParams pp{};
   CU(attn_prefill_any(c->act, c->cfg.head_dim, pp, c->stream, true));
+  CU(attn_prefill_tc_any(c->act, c->cfg.head_dim, pp, c->stream, true));
   CUtensorMap dummy{};
   for (int e : epis)
     for (int bn : {16, 32, 64, 128, 256}) {
@@ -1422,7 +1441,8 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
       pp.err = c->d_err;
       pp.trace = tr("attention", l, P);
       t_prio = 0;
-      CU(attn_prefill_any(c->act, k.head_dim, pp, P.s, false));
+      if (c->prefill_tc) CU(attn_prefill_tc_any(c->act, k.head_dim, pp, P.s, false));
+      else CU(attn_prefill_any(c->act, k.head_dim, pp, P.s, false));
       if (i8) {
         NormParams np_{};
         np_.x = static_cast<const float*>(c->attn);
@@ -2182,6 +2202,7 @@ extern "C" int llm_set_option(llm_ctx* c, int option, int value) {
     case LLM_OPT_OVERLAP_GRAPHS: flag = &c->overlap_graphs; break;
     case LLM_OPT_CHAIN_PDL: flag = &c->chain_pdl; break;
     case LLM_OPT_PREFILL_TILES: flag = &c->prefill_tiles; break;
+    case LLM_OPT_PREFILL_TC: flag = &c->prefill_tc; break;
     case LLM_OPT_ATTN_CHAIN:
       if (value < 0 || value > 1) return fail(LLM_ERR_INVALID, "attention chain mode %d out of range [0, 1]", value);
       if (c->attn_chain != value) {

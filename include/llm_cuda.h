@@ -238,6 +238,8 @@ int llm_debug_sample(int device, const float *logits, int rows, int vocab, float
                                       share an SM (default 64; 0 = the full ring)                */
 #define LLM_OPT_PREFILL_BN 14   /* channel tile of prefill-sized tcgen05 GEMMs (64, 128, 256;
                                    default 128; 0 = the widest)                               */
+#define LLM_OPT_PREFILL_TC 15   /* prefill query tiles on tcgen05 tensor cores (TMEM accumulators);
+                                   0 = the mma.sync tile kernel (default 1)                   */
 #define LLM_OPT_ATTN_CHAIN 7   /* overlap mode: a micro-batch's attention launch starts once every CTA of
                                   the other's has started (1, default) or once it completed (0)  */
 /* Set an execution option (value 0/1).  Results do not depend on the options beyond fp32

@@ -242,16 +242,18 @@ def test_overlapped_microbatches_equal_single_stream(cfg, dtype, batch, parts, g
 def test_prefill_query_tiles_long_prompts(cfg, dtype):
     """Prompts spanning several 64-position KV tiles and several query tiles (128/group
     positions), ragged at every boundary, one continued from a cached prefix: the tiled prefill
-    attention must meet the oracle, and agree with the decode kernel's block mode."""
+    attention, on the tcgen05 tensor cores and on the mma.sync kernel, must meet the oracle and
+    agree with the decode kernel's block mode."""
     w = weights(cfg)
     rng = np.random.default_rng(17)
     lens = [1, 63, 64, 65, 129, 200, 300]
     prompts = [rng.integers(3, cfg.vocab, L).tolist() for L in lens]
     m = O.Model(cfg.oracle_dict(), w, dtype)
     results = {}
-    for tiles in (1, 0):
+    for tiles, tc in ((1, 1), (1, 0), (0, 0)):
         eng = engine(cfg, dtype, w, max_batch=len(lens) + 1, max_pos=320)
         eng.set_option(_abi.LLM_OPT_PREFILL_TILES, tiles)
+        eng.set_option(_abi.LLM_OPT_PREFILL_TC, tc)
         toks, logits = gpu_run(eng, prompts, steps=4)
         # a prompt continued from its cached first 100 positions
         p = prompts[-1]
@@ -259,9 +261,10 @@ def test_prefill_query_tiles_long_prompts(cfg, dtype):
         nxt, lg = eng.prefill([len(lens)], [p[100:]], start_pos=[100], want_logits=True)
         eng.close()
         worst, agree, n = oracle_check(m, prompts, toks, logits)
-        print(f"{cfg.name} {dtype} tiles={tiles}: max|dlogit|={worst:.3e} top1={agree:.4f}")
-        assert worst <= LOGIT_TOL[dtype] and agree >= TOP1_MIN[dtype], (tiles, worst, agree)
+        print(f"{cfg.name} {dtype} tiles={tiles} tc={tc}: max|dlogit|={worst:.3e} top1={agree:.4f}")
+        assert worst <= LOGIT_TOL[dtype] and agree >= TOP1_MIN[dtype], (tiles, tc, worst, agree)
         assert np.abs(lg[0] - logits[-1][0]).max() <= LOGIT_TOL[dtype]
-        results[tiles] = logits
-    for a, b in zip(results[0], results[1]):
-        assert np.abs(a - b).max() <= LOGIT_TOL[dtype]
+        results[(tiles, tc)] = logits
+    for key in ((1, 1), (1, 0)):
+        for a, b in zip(results[(0, 0)], results[key]):
+            assert np.abs(a - b).max() <= LOGIT_TOL[dtype], key
