@@ -68,8 +68,10 @@ __global__ void __launch_bounds__(kPrefillWarps * 32, 1) attn_prefill_kernel(Pre
   griddep_launch_dependents();
   trace_start(p.trace);
   griddep_wait();
-  const int tile = p.n_tiles - 1 - static_cast<int>(blockIdx.x);  // longest first
-  const int kvh = blockIdx.y;
+  // 1-D grid, kv head fastest: the host lists tiles longest context first, so every kv
+  // head's longest tiles start in the first wave
+  const int tile = static_cast<int>(blockIdx.x) / p.n_kv_heads;
+  const int kvh = static_cast<int>(blockIdx.x) % p.n_kv_heads;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int group = p.n_heads / p.n_kv_heads;

@@ -6,20 +6,23 @@
 //
 // One CTA = (query tile, kv head): 128 score rows, row = h * (128/group) + i for head h of the
 // kv head's group and query position i of the tile; TMEM lane = row.  The sequence's cached
-// K/V pages are streamed 64 positions at a time through a STAGES-deep ring (bulk copies of the
-// pages' 16 x 128 B sub-blocks, see kv_off in common.cuh, placed so that a 64-position tile of
-// every 64-element half of K and V is one 128B-swizzled operand).  Per tile t:
-//   MMA warp:      S_t[128 x 64]  = Q . K_t^T      (tcgen05.mma kind::f16, K-major Q and K,
-//                                                   f32 accumulator in TMEM, double-buffered)
+// K/V pages are streamed 64 positions at a time through separate K and V rings (bulk copies of
+// the pages' 16 x 128 B sub-blocks, see kv_off in common.cuh, placed so that a 64-position tile
+// of every 64-element half of K and V is one 128B-swizzled operand).  Per tile t:
+//   MMA warp:      S_t[128 x 64] = Q . K_t^T   (tcgen05.mma kind::f16, Q and K K-major in shared
+//                                               memory, f32 accumulator in TMEM, two buffers)
 //   softmax warps: one thread per row reads its 64 scores from TMEM, applies scale and the
-//                  causal mask, updates the running max / sum, rescales its O row in TMEM
-//                  when the max moved, and writes P as two activation-type terms hi + lo
-//                  (the decode kernel's ~16-bit softmax weights) into shared memory
-//   MMA warp:      O[128 x hd] += P_hi . V_t + P_lo . V_t  (P K-major, V MN-major)
-// S_{t+1} is issued before the softmax of t finishes, so the tensor core and the softmax
-// overlap.  Warp 0 = bulk-copy producer, warp 1 = TMEM allocator + MMA issuer (one thread),
-// warps 2..5 = softmax / epilogue.  Every wait is bounded; on expiry the CTA records
-// kDevWaitTimeout, drains its copies and still frees its TMEM.
+//                  causal mask, accumulates the row sum against a reference max, and writes P
+//                  as two activation-type terms hi + lo (the decode kernel's ~16-bit softmax
+//                  weights) back into the same TMEM columns
+//   MMA warp:      O[128 x hd] += P_hi . V_t + P_lo . V_t   (A = P from TMEM, V MN-major)
+// The reference max of a row moves only when a tile's max exceeds it by more than 2^8 (log2
+// domain 8): P <= 256 stays exact in the hi + lo split, and the O rescale -- the one step that
+// has to wait for the previous PV -- becomes rare.  S_{t+1} runs on the tensor core while the
+// softmax of t runs, and two CTAs share an SM (~97 KB shared memory, 256 TMEM columns each), so
+// one CTA's softmax overlaps the other's MMAs.  Warp 0 = bulk-copy producer, warp 1 = TMEM
+// allocator + MMA issuer (one thread), warps 2..5 = softmax / epilogue.  Every wait is bounded;
+// on expiry the CTA records kDevWaitTimeout, drains its copies and MMAs and still frees its TMEM.
 #pragma once
 #include "attn_prefill.cuh"
 #include "common.cuh"
@@ -32,53 +35,60 @@ struct PrefillTcCfg {
   static constexpr int HALVES = HD / 64;              // 64-element halves of a K / V row
   static constexpr int SUB = 16 * 128;                // one page's half sub-block (bytes)
   static constexpr int REGION = 4 * SUB;              // 64 positions of one half (bytes)
-  static constexpr int STAGE_BYTES = 2 * HALVES * REGION;  // K halves then V halves
-  static constexpr int STAGES = 3;
+  static constexpr int TILE_BYTES = HALVES * REGION;  // K (or V) of one 64-position tile
+  static constexpr int K_STAGES = HD == 64 ? 3 : 2;
+  static constexpr int V_STAGES = HD == 64 ? 3 : 2;
   static constexpr int Q_BYTES = HALVES * 128 * 128;  // 128 rows x HD, K-major halves
-  static constexpr int P_BYTES = 128 * 128;           // 128 rows x 64 positions
-  static constexpr int SMEM = Q_BYTES + 2 * P_BYTES + STAGES * STAGE_BYTES + 1024;
-  static constexpr uint32_t TMEM_COLS = 256;          // S: 2 x 64 columns, O: HD columns at 128
+  static constexpr int SMEM = Q_BYTES + (K_STAGES + V_STAGES) * TILE_BYTES + 1024;
+  static constexpr uint32_t TMEM_COLS = 256;          // S/P: 2 x 64 columns, O: HD columns at 128
+  static constexpr float RESCALE_LOG2 = 8.0f;         // reference max moves beyond this gap
 };
 
 template <typename T, int HD>
-__global__ void __launch_bounds__(192, 1) attn_prefill_tc_kernel(PrefillAttnParams p) {
+__global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(PrefillAttnParams p) {
   using Cfg = PrefillTcCfg<T, HD>;
-  constexpr int STAGES = Cfg::STAGES;
+  constexpr int KS = Cfg::K_STAGES, VS = Cfg::V_STAGES;
   constexpr int HALVES = Cfg::HALVES;
   constexpr int SUB = Cfg::SUB;
   constexpr int REGION = Cfg::REGION;
   constexpr int ROWB = HD * (int)sizeof(T);  // bytes of one K or V row in the page block
   // MN-major V: the second 64-element chunk of hd is the next half's region; with one half
-  // the offset is never applied and stays inside the stage
+  // the offset is never applied and stays inside the tile
   constexpr uint32_t V_LBO = HALVES > 1 ? REGION : 1024;
 
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t kv_full[STAGES], kv_empty[STAGES], s_full[2], p_ready, pv_done, q_ready, drain;
+  __shared__ __align__(8) uint64_t k_full[KS], k_empty[KS], v_full[VS], v_empty[VS], s_full[2], p_ready[2],
+      pv_done, q_ready, drain;
   __shared__ uint32_t s_tmem;
 
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const uint32_t q_s = sbase;
-  const uint32_t ph_s = q_s + Cfg::Q_BYTES;
-  const uint32_t pl_s = ph_s + Cfg::P_BYTES;
-  const uint32_t ring = pl_s + Cfg::P_BYTES;
+  const uint32_t k_ring = q_s + Cfg::Q_BYTES;
+  const uint32_t v_ring = k_ring + KS * Cfg::TILE_BYTES;
   uint8_t* const gbase = smem_raw + (sbase - smem_u32(smem_raw));  // generic pointer of sbase
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = p.n_tiles - 1 - static_cast<int>(blockIdx.x);  // longest first
-  const int kvh = blockIdx.y;
+  // 1-D grid, kv head fastest: the host lists tiles longest context first, so every kv
+  // head's longest tiles start in the first wave
+  const int tile = static_cast<int>(blockIdx.x) / p.n_kv_heads;
+  const int kvh = static_cast<int>(blockIdx.x) % p.n_kv_heads;
   const int group = p.n_heads / p.n_kv_heads;
   const int QT = 128 / group;
 
-  griddep_launch_dependents();
   trace_start(p.trace);
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(smem_u32(&kv_full[s]), 1);
-      mbar_init(smem_u32(&kv_empty[s]), 1);
+    for (int s = 0; s < KS; ++s) {
+      mbar_init(smem_u32(&k_full[s]), 1);
+      mbar_init(smem_u32(&k_empty[s]), 1);
+    }
+    for (int s = 0; s < VS; ++s) {
+      mbar_init(smem_u32(&v_full[s]), 1);
+      mbar_init(smem_u32(&v_empty[s]), 1);
     }
     mbar_init(smem_u32(&s_full[0]), 1);
     mbar_init(smem_u32(&s_full[1]), 1);
-    mbar_init(smem_u32(&p_ready), 128);
+    mbar_init(smem_u32(&p_ready[0]), 128);
+    mbar_init(smem_u32(&p_ready[1]), 128);
     mbar_init(smem_u32(&pv_done), 1);
     mbar_init(smem_u32(&q_ready), 128);
     mbar_init(smem_u32(&drain), 1);
@@ -92,6 +102,8 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_tc_kernel(PrefillAttnPara
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s_tmem;
+  // dependents launch only after every CTA of this grid holds its TMEM columns
+  griddep_launch_dependents();
   griddep_wait();
 
   const int r0 = p.tile_row0[tile];
@@ -108,35 +120,41 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_tc_kernel(PrefillAttnPara
     if (lane == 0) {
       const T* pool = reinterpret_cast<const T*>(p.kv_pool);
       const int* bt = p.block_table + static_cast<size_t>(seq) * p.max_pages_per_seq;
-      int issued = 0;
-      for (int t = 0; t < nkv; ++t) {
-        const int s = t % STAGES;
-        if (t >= STAGES && !mbar_wait_bounded(smem_u32(&kv_empty[s]), ((t / STAGES) + 1) & 1)) {
-          failed = true;
-          break;
-        }
+      // one tile of K (v = 0) or V (v = 1): its pages' half sub-blocks into one ring stage
+      auto load = [&](int t, int v, uint32_t dst, uint32_t bar) {
         const int first = 4 * t, np = min(4, n_pages_ctx - first);
-        const uint32_t bar = smem_u32(&kv_full[s]);
-        mbar_arrive_expect_tx(bar, np * 2 * HALVES * SUB);
-        const uint32_t st = ring + s * Cfg::STAGE_BYTES;
+        mbar_arrive_expect_tx(bar, np * HALVES * SUB);
         for (int j = 0; j < np; ++j) {
           int phys = bt[first + j];
           if (phys < 0 || phys >= p.n_pages) {
             if (p.err) atomicExch(p.err, kDevBadPage);
             phys = 0;
           }
-          const uint8_t* kblk = reinterpret_cast<const uint8_t*>(
-              pool + ((static_cast<size_t>(p.layer) * p.n_pages + phys) * p.n_kv_heads + kvh) * (2 * 16 * HD));
-          for (int hh = 0; hh < HALVES; ++hh) {
-            bulk_g2s(st + hh * REGION + j * SUB, kblk + hh * SUB, SUB, bar);                          // K half
-            bulk_g2s(st + (HALVES + hh) * REGION + j * SUB, kblk + 16 * ROWB + hh * SUB, SUB, bar);  // V half
-          }
+          const uint8_t* blk = reinterpret_cast<const uint8_t*>(
+                                   pool + ((static_cast<size_t>(p.layer) * p.n_pages + phys) * p.n_kv_heads + kvh) *
+                                              (2 * 16 * HD)) +
+                               v * 16 * ROWB;
+          for (int hh = 0; hh < HALVES; ++hh) bulk_g2s(dst + hh * REGION + j * SUB, blk + hh * SUB, SUB, bar);
         }
-        issued = t + 1;
+      };
+      int k_issued = 0, v_issued = 0;
+      for (int t = 0; t < nkv; ++t) {
+        if (t >= KS && !mbar_wait_bounded(smem_u32(&k_empty[t % KS]), ((t / KS) + 1) & 1)) {
+          failed = true;
+          break;
+        }
+        load(t, 0, k_ring + (t % KS) * Cfg::TILE_BYTES, smem_u32(&k_full[t % KS]));
+        k_issued = t + 1;
+        if (t >= VS && !mbar_wait_bounded(smem_u32(&v_empty[t % VS]), ((t / VS) + 1) & 1)) {
+          failed = true;
+          break;
+        }
+        load(t, 1, v_ring + (t % VS) * Cfg::TILE_BYTES, smem_u32(&v_full[t % VS]));
+        v_issued = t + 1;
       }
       // copies still in flight must land before the CTA's shared memory goes away
-      for (int t = max(0, issued - STAGES); t < issued; ++t)
-        mbar_wait_bounded(smem_u32(&kv_full[t % STAGES]), (t / STAGES) & 1);
+      for (int t = max(0, k_issued - KS); t < k_issued; ++t) mbar_wait_bounded(smem_u32(&k_full[t % KS]), (t / KS) & 1);
+      for (int t = max(0, v_issued - VS); t < v_issued; ++t) mbar_wait_bounded(smem_u32(&v_full[t % VS]), (t / VS) & 1);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -144,18 +162,20 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_tc_kernel(PrefillAttnPara
       constexpr uint32_t idesc_s = umma_idesc<T>(128, 64);
       constexpr uint32_t idesc_pv = umma_idesc<T>(128, HD) | (1u << 16);  // B (V) MN-major
       const uint32_t o_tmem = tmem + 128;
+      // S_t into TMEM columns (t & 1) * 64; frees the K stage when the MMAs complete
       auto issue_s = [&](int t) -> bool {
-        const int s = t % STAGES;
-        if (!mbar_wait_bounded(smem_u32(&kv_full[s]), (t / STAGES) & 1)) return false;
+        const int s = t % KS;
+        if (!mbar_wait_bounded(smem_u32(&k_full[s]), (t / KS) & 1)) return false;
         tc_fence_after();
-        const uint32_t st = ring + s * Cfg::STAGE_BYTES;
+        const uint32_t kst = k_ring + s * Cfg::TILE_BYTES;
         const uint32_t d = tmem + (t & 1) * 64;
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k) {
           const int hh = k >> 2, kk = k & 3;
-          umma<false>(d, sw128_desc(q_s + hh * 128 * 128 + 32 * kk), sw128_desc(st + hh * REGION + 32 * kk), idesc_s,
+          umma<false>(d, sw128_desc(q_s + hh * 128 * 128 + 32 * kk), sw128_desc(kst + hh * REGION + 32 * kk), idesc_s,
                       k > 0 ? 1u : 0u);
         }
+        tc_commit(smem_u32(&k_empty[s]));
         tc_commit(smem_u32(&s_full[t & 1]));
         return true;
       };
@@ -163,27 +183,35 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_tc_kernel(PrefillAttnPara
       if (ok) ok = issue_s(0);
       if (ok && nkv > 1) ok = issue_s(1);
       for (int t = 0; ok && t < nkv; ++t) {
-        if (!mbar_wait_bounded(smem_u32(&p_ready), t & 1)) {
+        if (!mbar_wait_bounded(smem_u32(&p_ready[t & 1]), (t >> 1) & 1) ||
+            !mbar_wait_bounded(smem_u32(&v_full[t % VS]), (t / VS) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t vst = ring + (t % STAGES) * Cfg::STAGE_BYTES + HALVES * REGION;
+        const uint32_t vst = v_ring + (t % VS) * Cfg::TILE_BYTES;
+        const uint32_t pa = tmem + (t & 1) * 64;  // P_hi at +0, P_lo at +32 (16-bit pairs)
 #pragma unroll
         for (int term = 0; term < 2; ++term) {
-          const uint32_t pa = term == 0 ? ph_s : pl_s;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)  // 16 positions per MMA
-            umma<false>(o_tmem, sw128_desc(pa + 32 * kk), sw128_desc_mn(vst + kk * 2048, V_LBO, 1024), idesc_pv,
-                        (t > 0 || term > 0 || kk > 0) ? 1u : 0u);
+            umma_ts(o_tmem, pa + term * 32 + kk * 8, sw128_desc_mn(vst + kk * 2048, V_LBO, 1024), idesc_pv,
+                    (t > 0 || term > 0 || kk > 0) ? 1u : 0u);
         }
-        tc_commit(smem_u32(&kv_empty[t % STAGES]));
+        tc_commit(smem_u32(&v_empty[t % VS]));
         tc_commit(smem_u32(&pv_done));
-        if (t + 2 < nkv) ok = issue_s(t + 2);
+        if (t + 2 < nkv) {
+          // S_{t+2} overwrites the columns P_t is read from: PV_t must be complete
+          if (!mbar_wait_bounded(smem_u32(&pv_done), t & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          ok = issue_s(t + 2);
+        }
       }
       if (!ok) failed = true;
-      // every MMA this thread issued has completed before TMEM is freed (matters on the
-      // timeout path; on the normal path the softmax warps already waited for the last one)
+      // every MMA this thread issued has completed before O is read and TMEM is freed
       tc_commit(smem_u32(&drain));
       mbar_wait_bounded(smem_u32(&drain), 0);
     }
@@ -210,99 +238,113 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_tc_kernel(PrefillAttnPara
       mbar_arrive(smem_u32(&q_ready));
     }
 
-    float m_run = -INFINITY, l_run = 0.f;
+    const float sl2 = p.scale_log2;
+    float m_ref = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int t = 0; t < nkv; ++t) {
-      // wait results are made warp-uniform: the TMEM loads below are warp-collective
+      // wait results are made warp-uniform: the TMEM accesses below are warp-collective
       if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&s_full[t & 1]), (t >> 1) & 1))) {
         ok = false;
         break;
       }
       tc_fence_after();
+      const uint32_t scol = trow + (t & 1) * 64;
       float sv[64];
       {
-        uint32_t r[32];
-        tmem_ld32(trow + (t & 1) * 64, r);
+        uint32_t ra[32], rb[32];
+        tmem_ld32(scol, ra);
+        tmem_ld32(scol + 32, rb);
         tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) sv[j] = __uint_as_float(r[j]);
-        tmem_ld32(trow + (t & 1) * 64 + 32, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) sv[32 + j] = __uint_as_float(r[j]);
+        for (int j = 0; j < 32; ++j) {
+          sv[j] = __uint_as_float(ra[j]);
+          sv[32 + j] = __uint_as_float(rb[j]);
+        }
       }
       const int kbase = t * 64;
-      float mx = -INFINITY;
+      // causal / ragged mask: only tiles reaching past some row's last visible position
+      if (__any_sync(0xffffffffu, kbase + 63 > lim)) {
 #pragma unroll
-      for (int j = 0; j < 64; ++j) {
-        sv[j] = kbase + j <= lim ? sv[j] * p.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, sv[j]);
+        for (int j = 0; j < 64; ++j)
+          if (kbase + j > lim) sv[j] = -INFINITY;
       }
-      const float m_new = fmaxf(m_run, mx);
+      float m8[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) m8[j] = sv[j];
+#pragma unroll
+      for (int j = 8; j < 64; ++j) m8[j & 7] = fmaxf(m8[j & 7], sv[j]);
+      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * sl2;  // scale > 0
+      // move the reference max only past the gap; the first visible tile always sets it
+      const bool move = mx > m_ref + Cfg::RESCALE_LOG2;
+      const float m_new = move ? mx : m_ref;
       const float mu = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = exp2f(m_run - mu);
-      float rs = 0.f;
+      const float alpha = move ? ex2_approx(m_ref - mu) : 1.0f;
+      float r8[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) r8[j] = 0.f;
 #pragma unroll
       for (int j = 0; j < 64; ++j) {
-        sv[j] = exp2f(sv[j] - mu);
-        rs += sv[j];
+        sv[j] = ex2_approx(fmaf(sv[j], sl2, -mu));
+        r8[j & 7] += sv[j];
       }
+      const float rs = ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
       l_run = l_run * alpha + rs;
-      m_run = m_new;
+      m_ref = m_new;
 
-      // PV of the previous tile must be complete before O is rescaled and P overwritten
-      if (t > 0) {
+      // O holds PV of tiles < t: rescale rows whose reference moved, after PV_{t-1} completed
+      // (tile 0's PV overwrites O, so nothing to rescale before it)
+      if (t > 0 && __any_sync(0xffffffffu, move)) {
         if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&pv_done), (t - 1) & 1))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll
-          for (int c = 0; c < HD / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld32(trow + 128 + c * 32, r);
-            tmem_wait_ld();
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(trow + 128 + c * 32, r);
+          tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * alpha);
-            tmem_st32(trow + 128 + c * 32, r);
-          }
-          tmem_wait_st();
+          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * alpha);
+          tmem_st32(trow + 128 + c * 32, r);
         }
       }
       // the tile's V rows past the context were not loaded (or are stale): zero them so a
-      // zero weight times stale shared memory cannot make NaN
+      // zero weight times stale shared memory cannot make NaN (only the last tile is ragged;
+      // its V copies land first)
       const int valid = ctx - kbase;
       if (valid < 64) {
-        uint8_t* vreg = gbase + (ring - sbase) + (t % STAGES) * Cfg::STAGE_BYTES + HALVES * REGION;
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&v_full[t % VS]), (t / VS) & 1))) {
+          ok = false;
+          break;
+        }
+        uint8_t* vreg = gbase + (v_ring - sbase) + (t % VS) * Cfg::TILE_BYTES;
         for (int idx = tl; idx < (64 - valid) * HALVES * 8; idx += 128) {
           const int rr = valid + idx / (HALVES * 8), rem = idx % (HALVES * 8);
           *reinterpret_cast<uint4*>(vreg + (rem >> 3) * REGION + rr * 128 + ((rem & 7) << 4)) = make_uint4(0, 0, 0, 0);
         }
+        fence_proxy_async_smem();
       }
-      // P row (64 positions) as hi + lo activation-type terms, K-major 128B-swizzled
+      // P row (64 positions) as hi + lo activation-type terms over the S columns just read
+      {
+        uint32_t hi[32], lo[32];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint4 hi, lo;
-        uint32_t* hp = reinterpret_cast<uint32_t*>(&hi);
-        uint32_t* lp = reinterpret_cast<uint32_t*>(&lo);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float a = sv[8 * c + 2 * e], b = sv[8 * c + 2 * e + 1];
-          hp[e] = ActTraits<T>::pack2(a, b);
-          const float2 hv = ActTraits<T>::unpack2(hp[e]);
-          lp[e] = ActTraits<T>::pack2(a - hv.x, b - hv.y);
+        for (int e = 0; e < 32; ++e) {
+          const float a = sv[2 * e], b = sv[2 * e + 1];
+          hi[e] = ActTraits<T>::pack2(a, b);
+          const float2 hv = ActTraits<T>::unpack2(hi[e]);
+          lo[e] = ActTraits<T>::pack2(a - hv.x, b - hv.y);
         }
-        const uint32_t off = tl * 128 + ((c ^ (tl & 7)) << 4);
-        *reinterpret_cast<uint4*>(gbase + (ph_s - sbase) + off) = hi;
-        *reinterpret_cast<uint4*>(gbase + (pl_s - sbase) + off) = lo;
+        tmem_st32(scol, hi);
+        tmem_st32(scol + 32, lo);
       }
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(smem_u32(&p_ready));
+      mbar_arrive(smem_u32(&p_ready[t & 1]));
     }
-    if (ok && nkv > 0) {
-      ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&pv_done), (nkv - 1) & 1));
+    if (ok) {
+      ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&drain), 0));
       tc_fence_after();
     }
     if (!ok) failed = true;

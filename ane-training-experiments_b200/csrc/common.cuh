@@ -125,6 +125,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// 2^x by the MUFU unit (PTX ex2.approx.ftz.f32: relative error ~2^-22, 2^-inf = +0)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
 // Bounded wait: false when the bound ran out (the caller reports kDevWaitTimeout).
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
   for (uint32_t i = 0; i < kMaxWaitPolls; ++i)

@@ -273,7 +273,7 @@ cudaError_t attn_prefill_launch_t(const PrefillAttnParams& p, cudaStream_t s, bo
   constexpr int smem = PrefillCfg<T, HD>::SMEM;
   if (prepare) return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   (void)cudaGetLastError();
-  return launch_pdl(k, dim3(p.n_tiles, p.n_kv_heads), dim3(kPrefillWarps * 32), smem, s, p);
+  return launch_pdl(k, dim3(p.n_tiles * p.n_kv_heads), dim3(kPrefillWarps * 32), smem, s, p);
 }
 
 cudaError_t attn_prefill_any(int act, int hd, const PrefillAttnParams& p, cudaStream_t s, bool prepare) {
@@ -288,7 +288,7 @@ cudaError_t attn_prefill_tc_launch_t(const PrefillAttnParams& p, cudaStream_t s,
   constexpr int smem = PrefillTcCfg<T, HD>::SMEM;
   if (prepare) return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   (void)cudaGetLastError();
-  return launch_pdl(k, dim3(p.n_tiles, p.n_kv_heads), dim3(192), smem, s, p);
+  return launch_pdl(k, dim3(p.n_tiles * p.n_kv_heads), dim3(192), smem, s, p);
 }
 
 cudaError_t attn_prefill_tc_any(int act, int hd, const PrefillAttnParams& p, cudaStream_t s, bool prepare) {
@@ -1830,6 +1830,18 @@ int prefill_impl(llm_ctx* c, const int32_t* seq_ids, const int32_t* tokens, cons
       h[4 * R + nb] = j - i;
       ++nb;
       i = j;
+    }
+    if (tiles) {
+      // query tiles longest context first (the prefill kernels start them in list order)
+      std::vector<std::pair<int, int>> blk(nb);
+      for (int b = 0; b < nb; ++b) blk[b] = {h[3 * R + b], h[4 * R + b]};
+      std::stable_sort(blk.begin(), blk.end(), [&](const std::pair<int, int>& a, const std::pair<int, int>& b) {
+        return rows[r + a.first].pos + a.second > rows[r + b.first].pos + b.second;
+      });
+      for (int b = 0; b < nb; ++b) {
+        h[3 * R + b] = blk[b].first;
+        h[4 * R + b] = blk[b].second;
+      }
     }
     for (int i = 0; i < R; ++i) {
       const Row& w = rows[r + i];

@@ -67,6 +67,15 @@ __device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t adesc, uint64_t b
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
   }
 }
+// kind::f16 MMA whose A operand (M lanes x K 16-bit elements, two per 32-bit column, row m in
+// lane m) is read from tensor memory at tmem_a; B from shared memory as in umma().
+__device__ __forceinline__ void umma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(acc));
+}
 // 32 lanes x 32 columns of 32-bit: thread t receives columns col..col+31 of lane (base lane + t)
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
