@@ -117,42 +117,59 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(PrefillAttnPara
 
   if (warp == 0) {
     // ------------------------------------------------------------ bulk-copy producer
-    if (lane == 0) {
-      const T* pool = reinterpret_cast<const T*>(p.kv_pool);
-      const int* bt = p.block_table + static_cast<size_t>(seq) * p.max_pages_per_seq;
-      // one tile of K (v = 0) or V (v = 1): its pages' half sub-blocks into one ring stage
-      auto load = [&](int t, int v, uint32_t dst, uint32_t bar) {
-        const int first = 4 * t, np = min(4, n_pages_ctx - first);
+    // The whole warp reads the block table, 32 pages (8 tiles) per coalesced load, one batch
+    // ahead of use; lane 0 issues the copies.  Waits run on every lane and are made uniform.
+    const T* pool = reinterpret_cast<const T*>(p.kv_pool);
+    const int* bt = p.block_table + static_cast<size_t>(seq) * p.max_pages_per_seq;
+    auto entries = [&](int first_page) -> int {
+      const int pg = first_page + lane;
+      if (pg >= n_pages_ctx) return 0;
+      int e = bt[pg];
+      if (e < 0 || e >= p.n_pages) {
+        if (p.err) atomicExch(p.err, kDevBadPage);
+        e = 0;
+      }
+      return e;
+    };
+    int ent = entries(0), ent_next = entries(32);
+    // one tile of K (v = 0) or V (v = 1): its pages' half sub-blocks into one ring stage
+    auto load = [&](int t, int v, uint32_t dst, uint32_t bar) {
+      const int np = min(4, n_pages_ctx - 4 * t);
+      int phys[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) phys[j] = __shfl_sync(0xffffffffu, ent, ((t & 7) << 2) + j);
+      if (lane == 0) {
         mbar_arrive_expect_tx(bar, np * HALVES * SUB);
         for (int j = 0; j < np; ++j) {
-          int phys = bt[first + j];
-          if (phys < 0 || phys >= p.n_pages) {
-            if (p.err) atomicExch(p.err, kDevBadPage);
-            phys = 0;
-          }
           const uint8_t* blk = reinterpret_cast<const uint8_t*>(
-                                   pool + ((static_cast<size_t>(p.layer) * p.n_pages + phys) * p.n_kv_heads + kvh) *
+                                   pool + ((static_cast<size_t>(p.layer) * p.n_pages + phys[j]) * p.n_kv_heads + kvh) *
                                               (2 * 16 * HD)) +
                                v * 16 * ROWB;
           for (int hh = 0; hh < HALVES; ++hh) bulk_g2s(dst + hh * REGION + j * SUB, blk + hh * SUB, SUB, bar);
         }
-      };
-      int k_issued = 0, v_issued = 0;
-      for (int t = 0; t < nkv; ++t) {
-        if (t >= KS && !mbar_wait_bounded(smem_u32(&k_empty[t % KS]), ((t / KS) + 1) & 1)) {
-          failed = true;
-          break;
-        }
-        load(t, 0, k_ring + (t % KS) * Cfg::TILE_BYTES, smem_u32(&k_full[t % KS]));
-        k_issued = t + 1;
-        if (t >= VS && !mbar_wait_bounded(smem_u32(&v_empty[t % VS]), ((t / VS) + 1) & 1)) {
-          failed = true;
-          break;
-        }
-        load(t, 1, v_ring + (t % VS) * Cfg::TILE_BYTES, smem_u32(&v_full[t % VS]));
-        v_issued = t + 1;
       }
-      // copies still in flight must land before the CTA's shared memory goes away
+    };
+    int k_issued = 0, v_issued = 0;
+    for (int t = 0; t < nkv; ++t) {
+      if (t > 0 && (t & 7) == 0) {
+        ent = ent_next;
+        ent_next = entries(4 * t + 32);
+      }
+      if (t >= KS && !__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&k_empty[t % KS]), ((t / KS) + 1) & 1))) {
+        failed = true;
+        break;
+      }
+      load(t, 0, k_ring + (t % KS) * Cfg::TILE_BYTES, smem_u32(&k_full[t % KS]));
+      k_issued = t + 1;
+      if (t >= VS && !__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&v_empty[t % VS]), ((t / VS) + 1) & 1))) {
+        failed = true;
+        break;
+      }
+      load(t, 1, v_ring + (t % VS) * Cfg::TILE_BYTES, smem_u32(&v_full[t % VS]));
+      v_issued = t + 1;
+    }
+    // copies still in flight must land before the CTA's shared memory goes away
+    if (lane == 0) {
       for (int t = max(0, k_issued - KS); t < k_issued; ++t) mbar_wait_bounded(smem_u32(&k_full[t % KS]), (t / KS) & 1);
       for (int t = max(0, v_issued - VS); t < v_issued; ++t) mbar_wait_bounded(smem_u32(&v_full[t % VS]), (t / VS) & 1);
     }
