@@ -362,20 +362,37 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
           if (c * 32 + j < BN) stage4(c * 32 + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
       }
       epi_bar();
-      // out may alias resid (in-place residual): each element is read and written by one thread
+      // out may alias resid (in-place residual): each element is read and written by one thread.
+      // The residual is read UNR vectors at a time so their L2 round trips overlap.
       constexpr int C4 = BN / 4;
-      for (int idx = et; idx < kUmmaTokens * C4; idx += 128) {
-        const int row = idx / C4, col = 4 * (idx % C4);
-        const int t = tok0 + row, ch = ch0 + col;
-        if (t >= p.M || ch >= p.N) continue;
-        const float4 y = *reinterpret_cast<const float4*>(stg + row * SP + col);
-        float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + static_cast<size_t>(t) * p.ldo + ch);
+      constexpr int PER_THREAD = kUmmaTokens * C4 / 128;
+      constexpr int UNR = PER_THREAD >= 8 ? 8 : PER_THREAD;
+      for (int it0 = 0; it0 < PER_THREAD; it0 += UNR) {
+        float4 r[UNR];
         if constexpr (EPI == EPI_RESID) {
-          const float4 r = *reinterpret_cast<const float4*>(p.resid + static_cast<size_t>(t) * p.ldo + ch);
-          *dst = make_float4(resid_add(y.x, r.x, p.resid_scale), resid_add(y.y, r.y, p.resid_scale),
-                             resid_add(y.z, r.z, p.resid_scale), resid_add(y.w, r.w, p.resid_scale));
-        } else {
-          *dst = y;  // fp32 values, or the int32 accumulators' bit patterns
+#pragma unroll
+          for (int u = 0; u < UNR; ++u) {
+            const int idx = et + (it0 + u) * 128;
+            const int row = idx / C4, col = 4 * (idx % C4);
+            const int t = tok0 + row, ch = ch0 + col;
+            r[u] = (t < p.M && ch < p.N) ? *reinterpret_cast<const float4*>(p.resid + static_cast<size_t>(t) * p.ldo + ch)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < UNR; ++u) {
+          const int idx = et + (it0 + u) * 128;
+          const int row = idx / C4, col = 4 * (idx % C4);
+          const int t = tok0 + row, ch = ch0 + col;
+          if (t >= p.M || ch >= p.N) continue;
+          const float4 y = *reinterpret_cast<const float4*>(stg + row * SP + col);
+          float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + static_cast<size_t>(t) * p.ldo + ch);
+          if constexpr (EPI == EPI_RESID) {
+            *dst = make_float4(resid_add(y.x, r[u].x, p.resid_scale), resid_add(y.y, r[u].y, p.resid_scale),
+                               resid_add(y.z, r[u].z, p.resid_scale), resid_add(y.w, r[u].w, p.resid_scale));
+          } else {
+            *dst = y;  // fp32 values, or the int32 accumulators' bit patterns
+          }
         }
       }
     } else if (staged && EPI == EPI_SWIGLU) {
