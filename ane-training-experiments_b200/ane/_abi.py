@@ -69,6 +69,7 @@ LLM_OPT_PREFILL_TILES = 11
 LLM_OPT_PREFILL_RING_KB = 13
 LLM_OPT_PREFILL_BN = 14
 LLM_OPT_PREFILL_TC = 15
+LLM_OPT_PREFILL_PERSIST = 16
 
 
 class LLMError(RuntimeError):

@@ -22,6 +22,7 @@
 #include "attention.cuh"
 #include "attn_prefill.cuh"
 #include "attn_prefill_tc.cuh"
+#include "umma_persist.cuh"
 #include "common.cuh"
 #include "gemm.cuh"
 #include "norm.cuh"
@@ -376,6 +377,39 @@ bool umma_bn_supported(int epi, int bn) {
   }
 }
 
+template <typename InT, typename OutT, int BN, int EPI>
+cudaError_t umma_persist_launch_t(const CUtensorMap& tx, const CUtensorMap& tw, const GemmParams& p, dim3 grid,
+                                  cudaStream_t s, bool prepare) {
+  constexpr int smem = PersistCfg<BN, EPI>::SMEM;
+  auto k = umma_persist_kernel<InT, OutT, BN, EPI>;
+  if (prepare) return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  (void)cudaGetLastError();
+  return launch_pdl(k, grid, dim3(PersistCfg<BN, EPI>::THREADS), smem, s, tx, tw, p);
+}
+
+// Persistent prefill projections: QKV (one head per tile), residual and SwiGLU at 128 columns.
+bool umma_persist_supported(int epi, int bn) {
+  return (epi == EPI_QKV && (bn == 64 || bn == 128)) || ((epi == EPI_RESID || epi == EPI_SWIGLU) && bn == 128);
+}
+
+template <typename InT, typename OutT>
+cudaError_t umma_persist_dispatch(const CUtensorMap& tx, const CUtensorMap& tw, const GemmParams& p, int epi, int bn,
+                                  dim3 grid, cudaStream_t s, bool prepare) {
+  if (epi == EPI_QKV && bn == 64) return umma_persist_launch_t<InT, OutT, 64, EPI_QKV>(tx, tw, p, grid, s, prepare);
+  if (epi == EPI_QKV && bn == 128) return umma_persist_launch_t<InT, OutT, 128, EPI_QKV>(tx, tw, p, grid, s, prepare);
+  if (epi == EPI_RESID && bn == 128) return umma_persist_launch_t<InT, OutT, 128, EPI_RESID>(tx, tw, p, grid, s, prepare);
+  if (epi == EPI_SWIGLU && bn == 128) return umma_persist_launch_t<InT, OutT, 128, EPI_SWIGLU>(tx, tw, p, grid, s, prepare);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t umma_persist_any(int act, bool in8, const CUtensorMap& tx, const CUtensorMap& tw, const GemmParams& p,
+                             int epi, int bn, dim3 grid, cudaStream_t s, bool prepare) {
+  if (in8) return act == 1 ? umma_persist_dispatch<int8_t, __half>(tx, tw, p, epi, bn, grid, s, prepare)
+                           : umma_persist_dispatch<int8_t, __nv_bfloat16>(tx, tw, p, epi, bn, grid, s, prepare);
+  return act == 1 ? umma_persist_dispatch<__half, __half>(tx, tw, p, epi, bn, grid, s, prepare)
+                  : umma_persist_dispatch<__nv_bfloat16, __nv_bfloat16>(tx, tw, p, epi, bn, grid, s, prepare);
+}
+
 template <typename InT, typename OutT, int EPI>
 cudaError_t umma_dispatch_bn(const CUtensorMap& tx, const CUtensorMap& tw, const GemmParams& p, int bn, dim3 grid,
                              cudaStream_t s, bool prepare) {
@@ -572,6 +606,7 @@ struct llm_ctx {
   int attn_chain = 1;
   bool prefill_tiles = true;  // prefill attention by query tiles (attn_prefill_kernel)
   bool prefill_tc = true;     // ... on the tcgen05 tensor cores (attn_prefill_tc_kernel)
+  bool prefill_persist = true;  // prefill projections on umma_persist_kernel
   // tcgen05 stage ring of prefill-sized GEMMs (0 = the full ring) and their channel tile
   // (0 = the widest supported): two 64 KB CTAs per SM measured fastest (Qwen3 W8A8 prefill of
   // 256 x 1516 tokens 1441 -> 1270 ms; Qwen3 bf16 306 -> 266 ms; Stories W8A8 33.2 -> 28.9 ms)
@@ -661,6 +696,12 @@ int prepare_kernels(llm_ctx* c) {
       if (!umma_bn_supported(e, bn)) continue;
       CU(umma_any(c->act, false, dummy, dummy, gp, e, bn, dim3(1), c->stream, true));
       if (c->in8) CU(umma_any(c->act, true, dummy, dummy, gp, e, bn, dim3(1), c->stream, true));
+    }
+  for (int e : epis)
+    for (int bn : {64, 128}) {
+      if (!umma_persist_supported(e, bn)) continue;
+      CU(umma_persist_any(c->act, false, dummy, dummy, gp, e, bn, dim3(1), c->stream, true));
+      if (c->in8) CU(umma_persist_any(c->act, true, dummy, dummy, gp, e, bn, dim3(1), c->stream, true));
     }
   return LLM_OK;
 }
@@ -1226,12 +1267,29 @@ const CUtensorMap* tmap(llm_ctx* c, const void* ptr, int esz, int k, int rows, i
   return &c->tmaps.emplace(key, m).first->second;
 }
 
+// Rows from which a projection runs on the persistent kernel (prefill chunks).
+constexpr int kPersistMinRows = 1024;
+
 // ring_kb > 0: cap the tcgen05 stage ring at that many KB of shared memory.
 int gemm(llm_ctx* c, bool in8, int epi, GemmParams p, cudaStream_t stream = nullptr, int ring_kb = 0) {
   if (!stream) stream = c->stream;
   const int esz = in8 ? 1 : 2;
   p.argmax_parts = (p.N + argmax_tile_width(c->use_umma) - 1) / argmax_tile_width(c->use_umma);
   if (c->use_umma) {
+    // Prefill chunks: the persistent kernel (tiles streamed through one ring per SM, epilogue
+    // of one tile overlapping the next tile's mainloop)
+    const int pbn = epi == EPI_QKV ? c->cfg.head_dim : 128;
+    if (c->prefill_persist && p.M >= kPersistMinRows && umma_persist_supported(epi, pbn)) {
+      const CUtensorMap* tx = tmap(c, p.A, esz, p.K, p.M, kUmmaTokens);
+      const CUtensorMap* tw = tmap(c, p.B, esz, p.K, p.N, pbn);
+      if (!tw || !tx) return LLM_ERR_CUDA;
+      p.k_splits = 1;
+      p.k_tiles_per_split = p.K * esz / 128;
+      p.err = c->d_err;
+      const int tiles = ((p.M + kUmmaTokens - 1) / kUmmaTokens) * ((p.N + pbn - 1) / pbn);
+      CU(umma_persist_any(c->act, in8, *tx, *tw, p, epi, pbn, dim3(std::min(tiles, c->n_sm)), stream, false));
+      return LLM_OK;
+    }
     int bn = umma_bn_for(p.M, p.N, epi, c->cfg.head_dim, c->n_sm);
     // Prefill-sized GEMMs (more tiles than SMs): a smaller stage ring lets two CTAs share an SM,
     // so one CTA's epilogue overlaps the other's mainloop; 128-wide channel tiles keep the
@@ -2215,6 +2273,7 @@ extern "C" int llm_set_option(llm_ctx* c, int option, int value) {
     case LLM_OPT_CHAIN_PDL: flag = &c->chain_pdl; break;
     case LLM_OPT_PREFILL_TILES: flag = &c->prefill_tiles; break;
     case LLM_OPT_PREFILL_TC: flag = &c->prefill_tc; break;
+    case LLM_OPT_PREFILL_PERSIST: flag = &c->prefill_persist; break;
     case LLM_OPT_ATTN_CHAIN:
       if (value < 0 || value > 1) return fail(LLM_ERR_INVALID, "attention chain mode %d out of range [0, 1]", value);
       if (c->attn_chain != value) {

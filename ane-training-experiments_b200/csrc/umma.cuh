@@ -547,12 +547,15 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
       const int hd = BN;
       float rr = 1.0f;
       if (region < 2 && p.qk_norm) {
+        // sum of squares in f64: per 32-column chunk in order, then the chunks in order
         double ss = 0.0;
         for (int c = 0; c < NCH; ++c) {
           float v[32];
           load_chunk(c, v);
+          double sc = 0.0;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) ss = __dadd_rn(ss, __dmul_rn((double)v[j], (double)v[j]));
+          for (int j = 0; j < 32; ++j) sc = __dadd_rn(sc, __dmul_rn((double)v[j], (double)v[j]));
+          ss = c == 0 ? sc : __dadd_rn(ss, sc);
         }
         rr = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)hd), p.eps))));
       }

@@ -240,6 +240,8 @@ int llm_debug_sample(int device, const float *logits, int rows, int vocab, float
                                    default 128; 0 = the widest)                               */
 #define LLM_OPT_PREFILL_TC 15   /* prefill query tiles on tcgen05 tensor cores (TMEM accumulators);
                                    0 = the mma.sync tile kernel (default 1)                   */
+#define LLM_OPT_PREFILL_PERSIST 16  /* projections of >= 1024-row chunks on the persistent tcgen05
+                                       kernel (double-buffered TMEM accumulators; default 1) */
 #define LLM_OPT_ATTN_CHAIN 7   /* overlap mode: a micro-batch's attention launch starts once every CTA of
                                   the other's has started (1, default) or once it completed (0)  */
 /* Set an execution option (value 0/1).  Results do not depend on the options beyond fp32

@@ -268,3 +268,32 @@ def test_prefill_query_tiles_long_prompts(cfg, dtype):
     for key in ((1, 1), (1, 0)):
         for a, b in zip(results[(0, 0)], results[key]):
             assert np.abs(a - b).max() <= LOGIT_TOL[dtype], key
+
+
+@pytest.mark.parametrize("cfg,dtype", [(TINY_GQA, "bf16"), (TINY_GQA, "w8a8_bf16"), (TINY_MHA, "fp16"),
+                                       (TINY_MHA, "w8a8_fp16")],
+                         ids=["gqa-bf16", "gqa-w8a8", "mha-fp16", "mha-w8a8"])
+def test_prefill_persistent_projections_bit_identical(cfg, dtype):
+    """Chunks of >= 1024 rows run their projections on the persistent tcgen05 kernel (two TMEM
+    accumulators, one ring per SM): logits, next tokens, the K/V cache and the following decode
+    steps must equal the per-tile kernel's bit for bit (same per-element arithmetic), with a
+    ragged last token tile."""
+    w = weights(cfg)
+    rng = np.random.default_rng(23)
+    lens = [300, 257, 211, 190, 133, 61]  # 1152 rows: 9 token tiles, the last one partial
+    prompts = [rng.integers(3, cfg.vocab, L).tolist() for L in lens]
+    out = {}
+    for persist in (1, 0):
+        eng = engine(cfg, dtype, w, max_batch=len(lens), max_pos=320)
+        eng.set_option(_abi.LLM_OPT_PREFILL_PERSIST, persist)
+        toks, logits = gpu_run(eng, prompts, steps=3)
+        kv = [eng.read_kv(l, s, p) for l in range(cfg.n_layers) for s in (0, 3, 5) for p in (0, lens[s] - 1)]
+        eng.close()
+        out[persist] = (toks, logits, kv)
+    a, b = out[1], out[0]
+    assert a[0] == b[0]
+    for x, y in zip(a[1], b[1]):
+        assert np.array_equal(x, y), np.abs(x - y).max()
+    for x, y in zip(a[2], b[2]):
+        for u, v in zip(x, y):
+            assert np.array_equal(u, v)
