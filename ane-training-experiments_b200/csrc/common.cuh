@@ -131,6 +131,12 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
   return y;
 }
+// 1/x by the MUFU unit (PTX rcp.approx.ftz.f32: within ~1 ulp; 1/inf = +0)
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
 // Bounded wait: false when the bound ran out (the caller reports kDevWaitTimeout).
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
   for (uint32_t i = 0; i < kMaxWaitPolls; ++i)

@@ -47,8 +47,10 @@ struct PersistCfg {
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr int SMEM = STAGES * STAGE_BYTES + STG_BYTES + 1024;
   static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulator buffers
-  // one epilogue warp per (TMEM lane quadrant, 32-column chunk)
-  static constexpr int EPI_WARPS = 4 * (BN / 32);
+  // one epilogue warp per (TMEM lane quadrant, 32-column chunk), at most 16 (a warp then
+  // takes every 4th chunk)
+  static constexpr int EPI_WARPS = 4 * (BN / 32) > 16 ? 16 : 4 * (BN / 32);
+  static constexpr int CPW = 4 * (BN / 32) / EPI_WARPS;  // chunks per epilogue warp
   static constexpr int EPI_THREADS = 32 * EPI_WARPS;
   static constexpr int THREADS = 64 + EPI_THREADS;
   static_assert(STAGES >= 2, "ring too shallow");
@@ -60,6 +62,7 @@ __global__ void __launch_bounds__(PersistCfg<BN, EPI>::THREADS, 1)
     umma_persist_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, GemmParams p) {
   using Cfg = PersistCfg<BN, EPI>;
   static_assert(EPI == EPI_QKV || EPI == EPI_RESID || EPI == EPI_SWIGLU, "prefill epilogues");
+  static_assert(EPI != EPI_QKV || Cfg::CPW == 1, "QKV: one chunk per epilogue warp");
   constexpr bool I8 = sizeof(InT) == 1;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int A_BYTES = Cfg::A_BYTES;
@@ -175,8 +178,9 @@ __global__ void __launch_bounds__(PersistCfg<BN, EPI>::THREADS, 1)
   } else {
     // ---------------------------------------------------------------- epilogue
     // warp w >= 2 reads TMEM lanes 32 * (w % 4) .. + 31 (its quadrant) and chunk (w - 2) / 4
+    constexpr int CPW = Cfg::CPW;
     const int q = warp & 3;
-    const int c = (warp - 2) >> 2;       // 32-column chunk of the accumulator
+    const int c = (warp - 2) >> 2;       // first 32-column chunk of the accumulator
     const int et = threadIdx.x - 64;     // 0 .. ET-1 among epilogue threads
     const int tl = q * 32 + lane;        // token within the tile (= TMEM lane)
     griddep_wait();  // positions, scales and the residual come from earlier kernels
@@ -187,7 +191,7 @@ __global__ void __launch_bounds__(PersistCfg<BN, EPI>::THREADS, 1)
       const int tok = tok0 + tl;
       const bool tok_ok = tok < p.M;
       const int tokc = tok_ok ? tok : p.M - 1;
-      const uint32_t tcol = tmem + buf * BN + c * 32 + (static_cast<uint32_t>(q * 32) << 16);
+      const uint32_t tcol = tmem + buf * BN + (static_cast<uint32_t>(q * 32) << 16);  // + 32 * chunk
 
       epi_bar_n<ET>();  // the previous tile's readers of s_bsc / s_nw / s_ss / stg are done
       float a_s = 1.0f;
@@ -225,66 +229,78 @@ __global__ void __launch_bounds__(PersistCfg<BN, EPI>::THREADS, 1)
           }
         }
       }
+      // the residual does not depend on this GEMM: its loads overlap the wait for the accumulator
+      constexpr int RPT = kUmmaTokens * (BN / 4) / ET;  // residual float4 per thread
+      float4 rpre[EPI == EPI_RESID ? RPT : 1];
+      if constexpr (EPI == EPI_RESID) {
+#pragma unroll
+        for (int u = 0; u < RPT; ++u) {
+          const int idx = et + u * ET;
+          const int row = idx / (BN / 4), col = 4 * (idx % (BN / 4));
+          const int t = tok0 + row, ch = ch0 + col;
+          rpre[u] = (t < p.M && ch < p.N) ? *reinterpret_cast<const float4*>(p.resid + static_cast<size_t>(t) * p.ldo + ch)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
       const bool ok = epi_bar_and<ET>(mbar_wait_bounded(smem_u32(&acc_full[buf]), (lt >> 1) & 1));
       if (!ok) failed = true;
       tc_fence_after();
-      // this warp's chunk, dequantised (the tile's s_bsc / s_nw / RoPE rows are visible: the
+      // this warp's chunks, dequantised (the tile's s_bsc / s_nw / RoPE rows are visible: the
       // barrier above also orders them)
-      float v[32];
-      {
+      float vv[CPW][32];
+#pragma unroll
+      for (int w = 0; w < CPW; ++w) {
+        const int cc = c + w * (Cfg::EPI_WARPS / 4);
         uint32_t r[32];
-        tmem_ld32(tcol, r);
+        tmem_ld32(tcol + cc * 32, r);
         tmem_wait_ld();
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          if constexpr (I8) v[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), a_s), s_bsc[c * 32 + j]);
-          else v[j] = __uint_as_float(r[j]);
-          if (!ok) v[j] = 0.f;
+          if constexpr (I8) vv[w][j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), a_s), s_bsc[cc * 32 + j]);
+          else vv[w][j] = __uint_as_float(r[j]);
+          if (!ok) vv[w][j] = 0.f;
         }
       }
       // the accumulator buffer is free for the MMAs of tile lt + 2 once every chunk is read
       tc_fence_before();
       mbar_arrive(smem_u32(&acc_empty[buf]));
       constexpr int SP = Cfg::SP;
+      float (&v)[32] = vv[0];
 
       if constexpr (EPI == EPI_RESID) {
 #pragma unroll
-        for (int j = 0; j < 32; j += 4)
-          *reinterpret_cast<float4*>(stg + tl * SP + c * 32 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        for (int w = 0; w < CPW; ++w) {
+          const int cc = c + w * (Cfg::EPI_WARPS / 4);
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(stg + tl * SP + cc * 32 + j) = make_float4(vv[w][j], vv[w][j + 1], vv[w][j + 2], vv[w][j + 3]);
+        }
         epi_bar_n<ET>();
-        // out may alias resid (in-place residual): each element is read and written by one thread
+        // out may alias resid (in-place residual): each element is read (above, before the
+        // accumulator) and written by one thread
         constexpr int C4 = BN / 4;
-        constexpr int PER_THREAD = kUmmaTokens * C4 / ET;
-        constexpr int UNR = PER_THREAD >= 8 ? 8 : PER_THREAD;
-        for (int it0 = 0; it0 < PER_THREAD; it0 += UNR) {
-          float4 r[UNR];
 #pragma unroll
-          for (int u = 0; u < UNR; ++u) {
-            const int idx = et + (it0 + u) * ET;
-            const int row = idx / C4, col = 4 * (idx % C4);
-            const int t = tok0 + row, ch = ch0 + col;
-            r[u] = (t < p.M && ch < p.N) ? *reinterpret_cast<const float4*>(p.resid + static_cast<size_t>(t) * p.ldo + ch)
-                                         : make_float4(0.f, 0.f, 0.f, 0.f);
-          }
-#pragma unroll
-          for (int u = 0; u < UNR; ++u) {
-            const int idx = et + (it0 + u) * ET;
-            const int row = idx / C4, col = 4 * (idx % C4);
-            const int t = tok0 + row, ch = ch0 + col;
-            if (t >= p.M || ch >= p.N) continue;
-            const float4 y = *reinterpret_cast<const float4*>(stg + row * SP + col);
-            *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + static_cast<size_t>(t) * p.ldo + ch) =
-                make_float4(resid_add(y.x, r[u].x, p.resid_scale), resid_add(y.y, r[u].y, p.resid_scale),
-                            resid_add(y.z, r[u].z, p.resid_scale), resid_add(y.w, r[u].w, p.resid_scale));
-          }
+        for (int u = 0; u < RPT; ++u) {
+          const int idx = et + u * ET;
+          const int row = idx / C4, col = 4 * (idx % C4);
+          const int t = tok0 + row, ch = ch0 + col;
+          if (t >= p.M || ch >= p.N) continue;
+          const float4 y = *reinterpret_cast<const float4*>(stg + row * SP + col);
+          *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + static_cast<size_t>(t) * p.ldo + ch) =
+              make_float4(resid_add(y.x, rpre[u].x, p.resid_scale), resid_add(y.y, rpre[u].y, p.resid_scale),
+                          resid_add(y.z, rpre[u].z, p.resid_scale), resid_add(y.w, rpre[u].w, p.resid_scale));
         }
       } else if constexpr (EPI == EPI_SWIGLU) {
-        float gg[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) gg[i] = swiglu_pair(v[2 * i], v[2 * i + 1], p.silu_form);
+        for (int w = 0; w < CPW; ++w) {
+          const int cc = c + w * (Cfg::EPI_WARPS / 4);
+          float gg[16];
 #pragma unroll
-        for (int i = 0; i < 16; i += 4)
-          *reinterpret_cast<float4*>(stg + tl * SP + c * 16 + i) = make_float4(gg[i], gg[i + 1], gg[i + 2], gg[i + 3]);
+          for (int i = 0; i < 16; ++i) gg[i] = swiglu_pair(vv[w][2 * i], vv[w][2 * i + 1], p.silu_form);
+#pragma unroll
+          for (int i = 0; i < 16; i += 4)
+            *reinterpret_cast<float4*>(stg + tl * SP + cc * 16 + i) = make_float4(gg[i], gg[i + 1], gg[i + 2], gg[i + 3]);
+        }
         epi_bar_n<ET>();
         constexpr int OUT_COLS = Cfg::OUT_COLS;
         const int F = p.N / 2, j0 = ch0 / 2;
