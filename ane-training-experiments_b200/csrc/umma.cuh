@@ -4,7 +4,7 @@
 //
 // Token-major tiles: the UMMA "A" operand is a 128-token tile of X and the "B" operand a
 // BN-channel tile of W (BN = 16..256), both K-major and 128-byte swizzled, written by TMA
-// (cp.async.bulk.tensor, no multicast).  The fp32/s32 accumulator lives in tensor memory
+// (cp.async.bulk.tensor, each CTA loading its own tiles).  The fp32/s32 accumulator lives in tensor memory
 // with TMEM lane = token and column = output channel, so in the epilogue every thread owns
 // one token and walks that token's channels in registers: QK-norm, RoPE, SwiGLU pairing and
 // the greedy argmax are per-thread loops over contiguous channels, and every store is a
