@@ -389,8 +389,7 @@ cudaError_t umma_persist_launch_t(const CUtensorMap& tx, const CUtensorMap& tw, 
 
 // Persistent prefill projections: QKV (one head per tile), residual and SwiGLU at 128 columns.
 bool umma_persist_supported(int epi, int bn) {
-  return (epi == EPI_QKV && (bn == 64 || bn == 128)) || (epi == EPI_RESID && bn == 128) ||
-         (epi == EPI_SWIGLU && (bn == 128 || bn == 256));
+  return (epi == EPI_QKV && (bn == 64 || bn == 128)) || ((epi == EPI_RESID || epi == EPI_SWIGLU) && bn == 128);
 }
 
 template <typename InT, typename OutT>
@@ -400,7 +399,6 @@ cudaError_t umma_persist_dispatch(const CUtensorMap& tx, const CUtensorMap& tw, 
   if (epi == EPI_QKV && bn == 128) return umma_persist_launch_t<InT, OutT, 128, EPI_QKV>(tx, tw, p, grid, s, prepare);
   if (epi == EPI_RESID && bn == 128) return umma_persist_launch_t<InT, OutT, 128, EPI_RESID>(tx, tw, p, grid, s, prepare);
   if (epi == EPI_SWIGLU && bn == 128) return umma_persist_launch_t<InT, OutT, 128, EPI_SWIGLU>(tx, tw, p, grid, s, prepare);
-  if (epi == EPI_SWIGLU && bn == 256) return umma_persist_launch_t<InT, OutT, 256, EPI_SWIGLU>(tx, tw, p, grid, s, prepare);
   return cudaErrorInvalidValue;
 }
 
@@ -1280,7 +1278,7 @@ int gemm(llm_ctx* c, bool in8, int epi, GemmParams p, cudaStream_t stream = null
   if (c->use_umma) {
     // Prefill chunks: the persistent kernel (tiles streamed through one ring per SM, epilogue
     // of one tile overlapping the next tile's mainloop)
-    const int pbn = epi == EPI_QKV ? c->cfg.head_dim : epi == EPI_SWIGLU && c->prefill_bn == 256 ? 256 : 128;
+    const int pbn = epi == EPI_QKV ? c->cfg.head_dim : 128;
     if (c->prefill_persist && p.M >= kPersistMinRows && umma_persist_supported(epi, pbn)) {
       const CUtensorMap* tx = tmap(c, p.A, esz, p.K, p.M, kUmmaTokens);
       const CUtensorMap* tw = tmap(c, p.B, esz, p.K, p.N, pbn);

@@ -16,19 +16,20 @@
 
 namespace llm {
 
-// Named barrier 1 over the NT epilogue threads; the _and form also ANDs a predicate across
-// them (a wait that expired on any thread ends the tile loop on all of them together).
+// Named barrier `id` over the NT threads of one epilogue group; the _and form also ANDs a
+// predicate across them (a wait that expired on any thread ends the group's tile loop on all
+// of its threads together).
 template <int NT>
-__device__ __forceinline__ void epi_bar_n() {
-  asm volatile("bar.sync 1, %0;\n" ::"n"(NT) : "memory");
+__device__ __forceinline__ void epi_bar_n(int id) {
+  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "n"(NT) : "memory");
 }
 template <int NT>
-__device__ __forceinline__ bool epi_bar_and(bool v) {
+__device__ __forceinline__ bool epi_bar_and(int id, bool v) {
   uint32_t r;
   asm volatile(
-      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}\n"
       : "=r"(r)
-      : "r"(static_cast<uint32_t>(v)), "n"(NT)
+      : "r"(static_cast<uint32_t>(v)), "r"(id), "n"(NT)
       : "memory");
   return r != 0;
 }
@@ -42,17 +43,23 @@ struct PersistCfg {
   static constexpr int SP = OUT_COLS + 4;  // staging pitch (floats)
   static constexpr int RP = BN / 2 + 4;    // RoPE staging pitch (floats)
   static constexpr int STG_BYTES = EPI == EPI_QKV ? kUmmaTokens * RP * 4 * 2 : kUmmaTokens * SP * 4;
-  static constexpr int BUDGET = 220 * 1024;
-  static constexpr int STAGES_RAW = (BUDGET - STG_BYTES - 1024) / STAGE_BYTES;
-  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + STG_BYTES + 1024;
-  static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulator buffers
-  // one epilogue warp per (TMEM lane quadrant, 32-column chunk), at most 16 (a warp then
-  // takes every 4th chunk)
-  static constexpr int EPI_WARPS = 4 * (BN / 32) > 16 ? 16 : 4 * (BN / 32);
-  static constexpr int CPW = 4 * (BN / 32) / EPI_WARPS;  // chunks per epilogue warp
-  static constexpr int EPI_THREADS = 32 * EPI_WARPS;
+  // Epilogue groups: with two, group g owns TMEM buffer g (every other tile), so two tiles'
+  // epilogues run at once and hide each other's latency; the residual projections (long K,
+  // few tiles per SM) keep one group and a deeper ring.
+  static constexpr int GROUPS = EPI == EPI_RESID ? 1 : 2;
+  static constexpr int NCH = BN / 32;
+  // warps per group: one per (TMEM lane quadrant, 32-column chunk), at most 16 / GROUPS (a
+  // warp then takes every (GW/4)-th chunk)
+  static constexpr int GW = 4 * NCH > 16 / GROUPS ? 16 / GROUPS : 4 * NCH;
+  static constexpr int CPW = 4 * NCH / GW;  // chunks per epilogue warp
+  static constexpr int GT = 32 * GW;        // threads per group
+  static constexpr int EPI_THREADS = GROUPS * GT;
   static constexpr int THREADS = 64 + EPI_THREADS;
+  static constexpr int BUDGET = 216 * 1024;  // dynamic shared memory (static arrays need the rest)
+  static constexpr int STAGES_RAW = (BUDGET - GROUPS * STG_BYTES - 1024) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + GROUPS * STG_BYTES + 1024;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulator buffers
   static_assert(STAGES >= 2, "ring too shallow");
   static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation");
 };
@@ -62,7 +69,6 @@ __global__ void __launch_bounds__(PersistCfg<BN, EPI>::THREADS, 1)
     umma_persist_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, GemmParams p) {
   using Cfg = PersistCfg<BN, EPI>;
   static_assert(EPI == EPI_QKV || EPI == EPI_RESID || EPI == EPI_SWIGLU, "prefill epilogues");
-  static_assert(EPI != EPI_QKV || Cfg::CPW == 1, "QKV: one chunk per epilogue warp");
   constexpr bool I8 = sizeof(InT) == 1;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int A_BYTES = Cfg::A_BYTES;
@@ -70,14 +76,14 @@ __global__ void __launch_bounds__(PersistCfg<BN, EPI>::THREADS, 1)
   constexpr int ESZ = sizeof(InT);
   constexpr int KSTEP_BYTES = 32;
   constexpr int NCH = BN / 32;
-  constexpr int ET = Cfg::EPI_THREADS;
+  constexpr int GROUPS = Cfg::GROUPS, GT = Cfg::GT;
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES], acc_full[2], acc_empty[2];
   __shared__ uint32_t s_tmem;
-  __shared__ float s_bsc[BN];
-  __shared__ float s_nw[BN];
-  __shared__ double s_ss[EPI == EPI_QKV ? NCH : 1][kUmmaTokens];  // QK-norm partial sums per chunk
+  __shared__ float s_bsc[GROUPS][BN];
+  __shared__ float s_nw[GROUPS][BN];
+  __shared__ double s_ss[GROUPS][EPI == EPI_QKV ? NCH : 1][kUmmaTokens];  // QK-norm partial sums per chunk
 
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
   float* const stg = reinterpret_cast<float*>(smem_raw + (sbase - smem_u32(smem_raw)) + STAGES * STAGE_BYTES);
@@ -95,7 +101,7 @@ __global__ void __launch_bounds__(PersistCfg<BN, EPI>::THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&acc_full[b]), 1);
-      mbar_init(smem_u32(&acc_empty[b]), ET);
+      mbar_init(smem_u32(&acc_empty[b]), GT);  // the threads of the group that drains buffer b
     }
     fence_mbar_init();
   }
@@ -177,15 +183,22 @@ __global__ void __launch_bounds__(PersistCfg<BN, EPI>::THREADS, 1)
     }
   } else {
     // ---------------------------------------------------------------- epilogue
-    // warp w >= 2 reads TMEM lanes 32 * (w % 4) .. + 31 (its quadrant) and chunk (w - 2) / 4
-    constexpr int CPW = Cfg::CPW;
+    // Epilogue warp ew = warp - 2 belongs to group g = ew / GW, which takes tiles lt = g, g +
+    // GROUPS, ... (TMEM buffer lt & 1).  Warp w reads TMEM lanes 32 * (w % 4) .. + 31 (its
+    // quadrant) and chunks cb, cb + GW/4, ... (cb = (ew % GW) / 4).
+    constexpr int GW = Cfg::GW, CPW = Cfg::CPW;
+    const int ew = warp - 2;
+    const int g = ew / GW;
     const int q = warp & 3;
-    const int c = (warp - 2) >> 2;       // first 32-column chunk of the accumulator
-    const int et = threadIdx.x - 64;     // 0 .. ET-1 among epilogue threads
+    const int cb = (ew % GW) >> 2;       // first 32-column chunk of this warp
+    const int gt = threadIdx.x - 64 - g * GT;  // 0 .. GT-1 within the group
     const int tl = q * 32 + lane;        // token within the tile (= TMEM lane)
+    const int bar_id = 1 + g;
+    float* const gstg = stg + g * (Cfg::STG_BYTES / 4);
+    float* const bsc = s_bsc[g];
+    float* const nwv = s_nw[g];
     griddep_wait();  // positions, scales and the residual come from earlier kernels
-    int lt = 0;
-    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++lt) {
+    for (int tile = blockIdx.x + g * gridDim.x, lt = g; tile < n_tiles; tile += GROUPS * gridDim.x, lt += GROUPS) {
       const int buf = lt & 1;
       const int tok0 = (tile % num_m) * kUmmaTokens, ch0 = (tile / num_m) * BN;
       const int tok = tok0 + tl;
@@ -193,12 +206,12 @@ __global__ void __launch_bounds__(PersistCfg<BN, EPI>::THREADS, 1)
       const int tokc = tok_ok ? tok : p.M - 1;
       const uint32_t tcol = tmem + buf * BN + (static_cast<uint32_t>(q * 32) << 16);  // + 32 * chunk
 
-      epi_bar_n<ET>();  // the previous tile's readers of s_bsc / s_nw / s_ss / stg are done
+      epi_bar_n<GT>(bar_id);  // the group's previous tile's readers of its shared arrays are done
       float a_s = 1.0f;
       if constexpr (I8) a_s = p.a_scale[tokc];
-      for (int j = et; j < BN; j += ET) {
+      for (int j = gt; j < BN; j += GT) {
         const int ch = ch0 + j;
-        if constexpr (I8) s_bsc[j] = ch < p.N ? p.b_scale[ch] : 0.0f;
+        if constexpr (I8) bsc[j] = ch < p.N ? p.b_scale[ch] : 0.0f;
       }
       int region = 0, head = 0, pos = 0, page = 0;
       if constexpr (EPI == EPI_QKV) {
@@ -213,50 +226,50 @@ __global__ void __launch_bounds__(PersistCfg<BN, EPI>::THREADS, 1)
         }
         if (region < 2 && p.qk_norm) {
           const float* nw = region == 0 ? p.q_norm : p.k_norm;
-          for (int j = et; j < BN; j += ET) s_nw[j] = nw[j];
+          for (int j = gt; j < BN; j += GT) nwv[j] = nw[j];
         }
         if (region < 2) {
-          // the tile's RoPE rows, coalesced: cos at stg[row * RP], sin at stg[(128 + row) * RP]
+          // the tile's RoPE rows, coalesced: cos at gstg[row * RP], sin at gstg[(128 + row) * RP]
           constexpr int RP = Cfg::RP, H4 = BN / 8;  // float4 per half-row
 #pragma unroll 4
-          for (int idx = et; idx < kUmmaTokens * H4; idx += ET) {
+          for (int idx = gt; idx < kUmmaTokens * H4; idx += GT) {
             const int row = idx / H4, c4 = idx % H4;
             const int t = min(tok0 + row, p.M - 1);
             const size_t off = static_cast<size_t>(p.positions[t]) * (BN / 2) + 4 * c4;
-            *reinterpret_cast<float4*>(stg + row * RP + 4 * c4) = *reinterpret_cast<const float4*>(p.rope_cos + off);
-            *reinterpret_cast<float4*>(stg + (kUmmaTokens + row) * RP + 4 * c4) =
+            *reinterpret_cast<float4*>(gstg + row * RP + 4 * c4) = *reinterpret_cast<const float4*>(p.rope_cos + off);
+            *reinterpret_cast<float4*>(gstg + (kUmmaTokens + row) * RP + 4 * c4) =
                 *reinterpret_cast<const float4*>(p.rope_sin + off);
           }
         }
       }
       // the residual does not depend on this GEMM: its loads overlap the wait for the accumulator
-      constexpr int RPT = kUmmaTokens * (BN / 4) / ET;  // residual float4 per thread
+      constexpr int RPT = kUmmaTokens * (BN / 4) / GT;  // residual float4 per thread
       float4 rpre[EPI == EPI_RESID ? RPT : 1];
       if constexpr (EPI == EPI_RESID) {
 #pragma unroll
         for (int u = 0; u < RPT; ++u) {
-          const int idx = et + u * ET;
+          const int idx = gt + u * GT;
           const int row = idx / (BN / 4), col = 4 * (idx % (BN / 4));
           const int t = tok0 + row, ch = ch0 + col;
           rpre[u] = (t < p.M && ch < p.N) ? *reinterpret_cast<const float4*>(p.resid + static_cast<size_t>(t) * p.ldo + ch)
                                           : make_float4(0.f, 0.f, 0.f, 0.f);
         }
       }
-      const bool ok = epi_bar_and<ET>(mbar_wait_bounded(smem_u32(&acc_full[buf]), (lt >> 1) & 1));
+      const bool ok = epi_bar_and<GT>(bar_id, mbar_wait_bounded(smem_u32(&acc_full[buf]), (lt >> 1) & 1));
       if (!ok) failed = true;
       tc_fence_after();
-      // this warp's chunks, dequantised (the tile's s_bsc / s_nw / RoPE rows are visible: the
-      // barrier above also orders them)
+      // this warp's chunks, dequantised (the tile's scales / norm weights / RoPE rows are
+      // visible: the barrier above also orders them)
       float vv[CPW][32];
 #pragma unroll
       for (int w = 0; w < CPW; ++w) {
-        const int cc = c + w * (Cfg::EPI_WARPS / 4);
+        const int cc = cb + w * (GW / 4);
         uint32_t r[32];
         tmem_ld32(tcol + cc * 32, r);
         tmem_wait_ld();
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          if constexpr (I8) vv[w][j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), a_s), s_bsc[cc * 32 + j]);
+          if constexpr (I8) vv[w][j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), a_s), bsc[cc * 32 + j]);
           else vv[w][j] = __uint_as_float(r[j]);
           if (!ok) vv[w][j] = 0.f;
         }
@@ -265,27 +278,26 @@ __global__ void __launch_bounds__(PersistCfg<BN, EPI>::THREADS, 1)
       tc_fence_before();
       mbar_arrive(smem_u32(&acc_empty[buf]));
       constexpr int SP = Cfg::SP;
-      float (&v)[32] = vv[0];
 
       if constexpr (EPI == EPI_RESID) {
 #pragma unroll
         for (int w = 0; w < CPW; ++w) {
-          const int cc = c + w * (Cfg::EPI_WARPS / 4);
+          const int cc = cb + w * (GW / 4);
 #pragma unroll
           for (int j = 0; j < 32; j += 4)
-            *reinterpret_cast<float4*>(stg + tl * SP + cc * 32 + j) = make_float4(vv[w][j], vv[w][j + 1], vv[w][j + 2], vv[w][j + 3]);
+            *reinterpret_cast<float4*>(gstg + tl * SP + cc * 32 + j) = make_float4(vv[w][j], vv[w][j + 1], vv[w][j + 2], vv[w][j + 3]);
         }
-        epi_bar_n<ET>();
+        epi_bar_n<GT>(bar_id);
         // out may alias resid (in-place residual): each element is read (above, before the
         // accumulator) and written by one thread
         constexpr int C4 = BN / 4;
 #pragma unroll
         for (int u = 0; u < RPT; ++u) {
-          const int idx = et + u * ET;
+          const int idx = gt + u * GT;
           const int row = idx / C4, col = 4 * (idx % C4);
           const int t = tok0 + row, ch = ch0 + col;
           if (t >= p.M || ch >= p.N) continue;
-          const float4 y = *reinterpret_cast<const float4*>(stg + row * SP + col);
+          const float4 y = *reinterpret_cast<const float4*>(gstg + row * SP + col);
           *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + static_cast<size_t>(t) * p.ldo + ch) =
               make_float4(resid_add(y.x, rpre[u].x, p.resid_scale), resid_add(y.y, rpre[u].y, p.resid_scale),
                           resid_add(y.z, rpre[u].z, p.resid_scale), resid_add(y.w, rpre[u].w, p.resid_scale));
@@ -293,34 +305,34 @@ __global__ void __launch_bounds__(PersistCfg<BN, EPI>::THREADS, 1)
       } else if constexpr (EPI == EPI_SWIGLU) {
 #pragma unroll
         for (int w = 0; w < CPW; ++w) {
-          const int cc = c + w * (Cfg::EPI_WARPS / 4);
+          const int cc = cb + w * (GW / 4);
           float gg[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) gg[i] = swiglu_pair(vv[w][2 * i], vv[w][2 * i + 1], p.silu_form);
 #pragma unroll
           for (int i = 0; i < 16; i += 4)
-            *reinterpret_cast<float4*>(stg + tl * SP + cc * 16 + i) = make_float4(gg[i], gg[i + 1], gg[i + 2], gg[i + 3]);
+            *reinterpret_cast<float4*>(gstg + tl * SP + cc * 16 + i) = make_float4(gg[i], gg[i + 1], gg[i + 2], gg[i + 3]);
         }
-        epi_bar_n<ET>();
+        epi_bar_n<GT>(bar_id);
         constexpr int OUT_COLS = Cfg::OUT_COLS;
         const int F = p.N / 2, j0 = ch0 / 2;
         if (p.swiglu_f32) {
           constexpr int C4 = OUT_COLS / 4;
-          for (int idx = et; idx < kUmmaTokens * C4; idx += ET) {
+          for (int idx = gt; idx < kUmmaTokens * C4; idx += GT) {
             const int row = idx / C4, col = 4 * (idx % C4);
             const int t = tok0 + row;
             if (t >= p.M || j0 + col >= F) continue;
             *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + static_cast<size_t>(t) * F + j0 + col) =
-                *reinterpret_cast<const float4*>(stg + row * SP + col);
+                *reinterpret_cast<const float4*>(gstg + row * SP + col);
           }
         } else {
           constexpr int C8 = OUT_COLS / 8;
-          for (int idx = et; idx < kUmmaTokens * C8; idx += ET) {
+          for (int idx = gt; idx < kUmmaTokens * C8; idx += GT) {
             const int row = idx / C8, col = 8 * (idx % C8);
             const int t = tok0 + row;
             if (t >= p.M || j0 + col >= F) continue;
-            const float4 a = *reinterpret_cast<const float4*>(stg + row * SP + col);
-            const float4 b = *reinterpret_cast<const float4*>(stg + row * SP + col + 4);
+            const float4 a = *reinterpret_cast<const float4*>(gstg + row * SP + col);
+            const float4 b = *reinterpret_cast<const float4*>(gstg + row * SP + col + 4);
             uint4 pk;
             pk.x = ActTraits<OutT>::pack2(a.x, a.y);
             pk.y = ActTraits<OutT>::pack2(a.z, a.w);
@@ -335,59 +347,68 @@ __global__ void __launch_bounds__(PersistCfg<BN, EPI>::THREADS, 1)
         float rr = 1.0f;
         if (region < 2 && p.qk_norm) {
           // sum of squares in f64: per chunk in order, then the chunks in order
-          double sc = 0.0;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) sc = __dadd_rn(sc, __dmul_rn((double)v[j], (double)v[j]));
-          s_ss[c][tl] = sc;
-          epi_bar_n<ET>();
-          double ss = s_ss[0][tl];
+          for (int w = 0; w < CPW; ++w) {
+            double sc = 0.0;
 #pragma unroll
-          for (int cc = 1; cc < NCH; ++cc) ss = __dadd_rn(ss, s_ss[cc][tl]);
+            for (int j = 0; j < 32; ++j) sc = __dadd_rn(sc, __dmul_rn((double)vv[w][j], (double)vv[w][j]));
+            s_ss[g][cb + w * (GW / 4)][tl] = sc;
+          }
+          epi_bar_n<GT>(bar_id);
+          double ss = s_ss[g][0][tl];
+#pragma unroll
+          for (int cc = 1; cc < NCH; ++cc) ss = __dadd_rn(ss, s_ss[g][cc][tl]);
           rr = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)hd), p.eps))));
         }
-        const int d0 = c * 32;  // first head dimension of the chunk
-        if (region < 2) {
-          if (p.qk_norm) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(__fmul_rn(v[j], rr), s_nw[d0 + j]);
-          }
-          float cs[16], sn[16];
-#pragma unroll
-          for (int i = 0; i < 16; i += 4) {
-            const float4 a = *reinterpret_cast<const float4*>(stg + tl * RP + d0 / 2 + i);
-            const float4 b = *reinterpret_cast<const float4*>(stg + (kUmmaTokens + tl) * RP + d0 / 2 + i);
-            cs[i] = a.x; cs[i + 1] = a.y; cs[i + 2] = a.z; cs[i + 3] = a.w;
-            sn[i] = b.x; sn[i + 1] = b.y; sn[i + 2] = b.z; sn[i + 3] = b.w;
-          }
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float a0 = v[2 * i], a1 = v[2 * i + 1];
-            v[2 * i] = __fsub_rn(__fmul_rn(a0, cs[i]), __fmul_rn(a1, sn[i]));
-            v[2 * i + 1] = __fadd_rn(__fmul_rn(a0, sn[i]), __fmul_rn(a1, cs[i]));
-          }
+        uint8_t* kv_base = nullptr;
+        if (region > 0 && tok_ok && page >= 0 && page < p.n_pages) {
+          const size_t blk = ((static_cast<size_t>(p.layer) * p.n_pages + page) * p.n_kv_heads + head) * 2 + (region - 1);
+          kv_base = reinterpret_cast<uint8_t*>(reinterpret_cast<OutT*>(p.kv_pool) + blk * 16 * hd);
+        } else if (region > 0 && tok_ok && cb == 0 && p.err) {
+          atomicExch(p.err, kDevBadPage);
         }
-        uint4 pk[4];
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          pk[h].x = ActTraits<OutT>::pack2(v[8 * h + 0], v[8 * h + 1]);
-          pk[h].y = ActTraits<OutT>::pack2(v[8 * h + 2], v[8 * h + 3]);
-          pk[h].z = ActTraits<OutT>::pack2(v[8 * h + 4], v[8 * h + 5]);
-          pk[h].w = ActTraits<OutT>::pack2(v[8 * h + 6], v[8 * h + 7]);
-        }
-        if (tok_ok) {
+        for (int w = 0; w < CPW; ++w) {
+          float (&v)[32] = vv[w];
+          const int d0 = (cb + w * (GW / 4)) * 32;  // first head dimension of the chunk
+          if (region < 2) {
+            if (p.qk_norm) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(__fmul_rn(v[j], rr), nwv[d0 + j]);
+            }
+            float cs[16], sn[16];
+#pragma unroll
+            for (int i = 0; i < 16; i += 4) {
+              const float4 a = *reinterpret_cast<const float4*>(gstg + tl * RP + d0 / 2 + i);
+              const float4 b = *reinterpret_cast<const float4*>(gstg + (kUmmaTokens + tl) * RP + d0 / 2 + i);
+              cs[i] = a.x; cs[i + 1] = a.y; cs[i + 2] = a.z; cs[i + 3] = a.w;
+              sn[i] = b.x; sn[i + 1] = b.y; sn[i + 2] = b.z; sn[i + 3] = b.w;
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float a0 = v[2 * i], a1 = v[2 * i + 1];
+              v[2 * i] = __fsub_rn(__fmul_rn(a0, cs[i]), __fmul_rn(a1, sn[i]));
+              v[2 * i + 1] = __fadd_rn(__fmul_rn(a0, sn[i]), __fmul_rn(a1, cs[i]));
+            }
+          }
+          uint4 pk[4];
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            pk[h].x = ActTraits<OutT>::pack2(v[8 * h + 0], v[8 * h + 1]);
+            pk[h].y = ActTraits<OutT>::pack2(v[8 * h + 2], v[8 * h + 3]);
+            pk[h].z = ActTraits<OutT>::pack2(v[8 * h + 4], v[8 * h + 5]);
+            pk[h].w = ActTraits<OutT>::pack2(v[8 * h + 6], v[8 * h + 7]);
+          }
+          if (!tok_ok) continue;
           if (region == 0) {
             uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<OutT*>(p.q_out) +
                                                   (static_cast<size_t>(tok) * p.n_heads + head) * hd + d0);
 #pragma unroll
             for (int h = 0; h < 4; ++h) dst[h] = pk[h];
-          } else if (page >= 0 && page < p.n_pages) {
-            const size_t blk = ((static_cast<size_t>(p.layer) * p.n_pages + page) * p.n_kv_heads + head) * 2 + (region - 1);
-            uint8_t* kv_base = reinterpret_cast<uint8_t*>(reinterpret_cast<OutT*>(p.kv_pool) + blk * 16 * hd);
+          } else if (kv_base) {
             const int slot = pos & 15;
 #pragma unroll
             for (int h = 0; h < 4; ++h) *reinterpret_cast<uint4*>(kv_base + kv_off(slot, (d0 >> 3) + h)) = pk[h];
-          } else if (c == 0 && p.err) {
-            atomicExch(p.err, kDevBadPage);
           }
         }
       }

@@ -283,7 +283,7 @@ def test_prefill_persistent_projections_bit_identical(cfg, dtype):
     lens = [300, 257, 211, 190, 133, 61]  # 1152 rows: 9 token tiles, the last one partial
     prompts = [rng.integers(3, cfg.vocab, L).tolist() for L in lens]
     out = {}
-    for persist, bn in ((1, 128), (1, 256), (0, 128)):  # 256: SwiGLU tiles of 256 channels
+    for persist, bn in ((1, 128), (0, 128), (0, 256)):  # per-tile kernel at 128 and 256 channels
         eng = engine(cfg, dtype, w, max_batch=len(lens), max_pos=320)
         eng.set_option(_abi.LLM_OPT_PREFILL_PERSIST, persist)
         eng.set_option(_abi.LLM_OPT_PREFILL_BN, bn)
@@ -291,8 +291,8 @@ def test_prefill_persistent_projections_bit_identical(cfg, dtype):
         kv = [eng.read_kv(l, s, p) for l in range(cfg.n_layers) for s in (0, 3, 5) for p in (0, lens[s] - 1)]
         eng.close()
         out[(persist, bn)] = (toks, logits, kv)
-    b = out[(0, 128)]
-    for key in ((1, 128), (1, 256)):
+    b = out[(1, 128)]
+    for key in ((0, 128), (0, 256)):
         a = out[key]
         assert a[0] == b[0], key
         for x, y in zip(a[1], b[1]):
