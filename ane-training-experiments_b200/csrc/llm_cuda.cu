@@ -550,6 +550,8 @@ struct llm_ctx {
   int n_pages = 0, max_seqs = 0, max_pos = 0, max_pages_per_seq = 0;
   int* d_block_table = nullptr;
   std::vector<int> h_block_table, seq_npages, free_pages;
+  std::vector<uint32_t> seq_stamp;  // duplicate-sequence check: seq_stamp[s] == stamp_gen once seen
+  uint32_t stamp_gen = 0;
 
   // activations (max_rows rows)
   int max_rows = 0;
@@ -1120,6 +1122,8 @@ extern "C" int llm_kv_alloc(llm_ctx* c, int max_seqs, int max_pos, int page_toke
   c->h_block_table.assign(static_cast<size_t>(max_seqs) * c->max_pages_per_seq, -1);
   CU(cudaMemcpy(c->d_block_table, c->h_block_table.data(), c->h_block_table.size() * 4, cudaMemcpyHostToDevice));
   c->seq_npages.assign(max_seqs, 0);
+  c->seq_stamp.assign(max_seqs, 0);
+  c->stamp_gen = 0;
   // free list in a scrambled order so block tables are never the identity map
   int stride = c->n_pages / 2 + 1;
   while (std::gcd(stride, c->n_pages) != 1) ++stride;
@@ -1199,12 +1203,34 @@ int ensure_pages(llm_ctx* c, int seq, int upto, std::vector<int>* dirty) {
 int upload_dirty(llm_ctx* c, std::vector<int>& dirty) {
   std::sort(dirty.begin(), dirty.end());
   dirty.erase(std::unique(dirty.begin(), dirty.end()), dirty.end());
-  for (int s : dirty)
-    CU(cudaMemcpyAsync(c->d_block_table + static_cast<size_t>(s) * c->max_pages_per_seq,
-                       c->h_block_table.data() + static_cast<size_t>(s) * c->max_pages_per_seq,
-                       c->max_pages_per_seq * 4, cudaMemcpyHostToDevice, c->stream));
+  const size_t row = c->max_pages_per_seq;
+  if (dirty.size() > 4) {
+    // many rows change at once (a batch crossing a page boundary together): one copy of the
+    // span of rows instead of one small copy per row
+    const size_t lo = dirty.front(), hi = dirty.back();
+    CU(cudaMemcpyAsync(c->d_block_table + lo * row, c->h_block_table.data() + lo * row, (hi - lo + 1) * row * 4,
+                       cudaMemcpyHostToDevice, c->stream));
+  } else {
+    for (int s : dirty)
+      CU(cudaMemcpyAsync(c->d_block_table + s * row, c->h_block_table.data() + s * row, row * 4,
+                         cudaMemcpyHostToDevice, c->stream));
+  }
   dirty.clear();
   return LLM_OK;
+}
+
+// Duplicate-sequence check of one call: start_stamp() once, then seen_before(seq) per sequence
+// (seq already range-checked) is true for its second appearance.
+void start_stamp(llm_ctx* c) {
+  if (++c->stamp_gen == 0) {
+    std::fill(c->seq_stamp.begin(), c->seq_stamp.end(), 0u);
+    c->stamp_gen = 1;
+  }
+}
+bool seen_before(llm_ctx* c, int seq) {
+  if (c->seq_stamp[seq] == c->stamp_gen) return true;
+  c->seq_stamp[seq] = c->stamp_gen;
+  return false;
 }
 
 int check_ready(llm_ctx* c) {
@@ -1789,10 +1815,10 @@ extern "C" int llm_decode_step(llm_ctx* c, const int32_t* seq_ids, const int32_t
   std::vector<int> dirty;
   int max_ctx = 0;
   double kv_positions = 0;
+  start_stamp(c);
   for (int i = 0; i < n; ++i) {
     RC(validate_row(c, seq_ids[i], tokens[i], positions[i]));
-    for (int j = 0; j < i; ++j)
-      if (seq_ids[j] == seq_ids[i]) return fail(LLM_ERR_INVALID, "sequence %d appears twice in one step", seq_ids[i]);
+    if (seen_before(c, seq_ids[i])) return fail(LLM_ERR_INVALID, "sequence %d appears twice in one step", seq_ids[i]);
     RC(ensure_pages(c, seq_ids[i], positions[i], &dirty));
     max_ctx = std::max(max_ctx, positions[i] + 1);
     kv_positions += positions[i] + 1.0;
@@ -1849,11 +1875,12 @@ int prefill_impl(llm_ctx* c, const int32_t* seq_ids, const int32_t* tokens, cons
   std::vector<Row> rows;
   std::vector<int> dirty;
   size_t off = 0;
+  start_stamp(c);
   for (int i = 0; i < nseq; ++i) {
     if (lens[i] <= 0) return fail(LLM_ERR_INVALID, "prompt %d is empty", i);
     const int p0 = start_pos ? start_pos[i] : 0;
-    for (int j = 0; j < i; ++j)
-      if (seq_ids[j] == seq_ids[i]) return fail(LLM_ERR_INVALID, "sequence %d appears twice", seq_ids[i]);
+    if (seq_ids[i] >= 0 && seq_ids[i] < c->max_seqs && seen_before(c, seq_ids[i]))
+      return fail(LLM_ERR_INVALID, "sequence %d appears twice", seq_ids[i]);
     for (int j = 0; j < lens[i]; ++j) {
       RC(validate_row(c, seq_ids[i], tokens[off + j], p0 + j));
       rows.push_back({seq_ids[i], tokens[off + j], p0 + j, i});
@@ -2057,12 +2084,12 @@ extern "C" int llm_generate_begin(llm_ctx* c, const int32_t* seq_ids, const int3
   std::vector<int> dirty;
   int max_ctx = 0;
   double kv_positions = 0;
+  start_stamp(c);
   for (int i = 0; i < n; ++i) {
     RC(validate_row(c, seq_ids[i], tokens[i], positions[i]));
     if (positions[i] + max_steps - 1 >= c->max_pos)
       return fail(LLM_ERR_POS_RANGE, "position out of range: %d", positions[i] + max_steps - 1);
-    for (int j = 0; j < i; ++j)
-      if (seq_ids[j] == seq_ids[i]) return fail(LLM_ERR_INVALID, "sequence %d appears twice", seq_ids[i]);
+    if (seen_before(c, seq_ids[i])) return fail(LLM_ERR_INVALID, "sequence %d appears twice", seq_ids[i]);
     RC(ensure_pages(c, seq_ids[i], positions[i] + max_steps - 1, &dirty));
     max_ctx = std::max(max_ctx, positions[i] + max_steps);
     kv_positions += positions[i] + 0.5 * max_steps + 0.5;
