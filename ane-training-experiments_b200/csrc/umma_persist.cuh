@@ -3,12 +3,15 @@
 // Same products and epilogues as umma_gemm_kernel (umma.cuh) for the projections of a prefill
 // chunk (QKV with QK-norm + RoPE + paged K/V write, residual add, SwiGLU), restated as one CTA
 // per SM that walks a static list of 128 x BN output tiles:
-//   warp 0      TMA producer: streams every tile's K slices through one STAGES-deep ring
-//               without draining between tiles
-//   warp 1      TMEM allocator + MMA issuer: accumulates tile i into TMEM buffer i & 1
-//   warps 2..5  epilogue: drains buffer i & 1 while the MMAs of tile i + 1 fill the other
-// so the epilogue of one tile overlaps the mainloop of the next, and the ring stays full.  The
-// coalesced-store staging area is its own shared-memory region (the ring is never idle).
+//   warp 0       TMA producer: streams every tile's K slices through one STAGES-deep ring
+//                without draining between tiles
+//   warp 1       TMEM allocator + MMA issuer: accumulates tile i into TMEM buffer i & 1
+//   warps 2..17  epilogue: one warp per (TMEM lane quadrant, 32-column chunk); for QKV and
+//                SwiGLU two groups of 8 warps, group g draining buffer g (every other tile),
+//                for the residual projections one group of 16
+// so the epilogue of one tile overlaps the mainloop of the next (and, with two groups, the
+// epilogue of the other buffer's tile), and the ring stays full.  Each group's coalesced-store
+// staging area is its own shared-memory region (the ring is never idle).
 // Per-element arithmetic is that of umma_gemm_kernel, so the outputs are bit-identical.
 // Reference: the projections of ane/stories/infer.go:213-262 (forwardLayer) for many rows.
 #pragma once

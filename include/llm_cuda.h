@@ -234,17 +234,19 @@ int llm_debug_sample(int device, const float *logits, int rows, int vocab, float
                                     micro-batch's projection chain (attention excluded)        */
 #define LLM_OPT_PREFILL_TILES 11 /* prefill attention by query tiles of 128/group positions (default 1);
                                      0 = the decode kernel's blocks of 8/group positions       */
-#define LLM_OPT_PREFILL_RING_KB 13 /* stage ring (KB) of prefill-sized tcgen05 GEMMs, so two CTAs
-                                      share an SM (default 64; 0 = the full ring)                */
-#define LLM_OPT_PREFILL_BN 14   /* channel tile of prefill-sized tcgen05 GEMMs (64, 128, 256;
-                                   default 128; 0 = the widest)                               */
+#define LLM_OPT_PREFILL_RING_KB 13 /* stage ring (KB) of prefill-sized per-tile tcgen05 GEMMs (those
+                                      the persistent kernel does not take), so two CTAs share an
+                                      SM (default 64; 0 = the full ring)                          */
+#define LLM_OPT_PREFILL_BN 14   /* channel tile of those per-tile GEMMs (64, 128, 256; default 128;
+                                   0 = the widest)                                            */
 #define LLM_OPT_PREFILL_TC 15   /* prefill query tiles on tcgen05 tensor cores (TMEM accumulators);
                                    0 = the mma.sync tile kernel (default 1)                   */
 #define LLM_OPT_PREFILL_PERSIST 16  /* projections of >= 1024-row chunks on the persistent tcgen05
                                        kernel (double-buffered TMEM accumulators; default 1) */
 #define LLM_OPT_ATTN_CHAIN 7   /* overlap mode: a micro-batch's attention launch starts once every CTA of
                                   the other's has started (1, default) or once it completed (0)  */
-/* Set an execution option (value 0/1).  Results do not depend on the options beyond fp32
+/* Set an execution option (0/1 switches; sizes and counts where noted).  Results do not depend
+ * on the options beyond fp32
  * summation order; cached graphs are dropped when an option changes.  No counterpart in the
  * reference (its ANE runtime has no such switches). */
 int llm_set_option(llm_ctx *ctx, int option, int value);
