@@ -246,8 +246,8 @@ int llm_debug_sample(int device, const float *logits, int rows, int vocab, float
 #define LLM_OPT_ATTN_CHAIN 7   /* overlap mode: a micro-batch's attention launch starts once every CTA of
                                   the other's has started (1, default) or once it completed (0)  */
 /* Set an execution option (0/1 switches; sizes and counts where noted).  Results do not depend
- * on the options beyond fp32
- * summation order; cached graphs are dropped when an option changes.  No counterpart in the
+ * on the options beyond fp32 summation order; cached graphs are dropped when an option
+ * changes.  No counterpart in the
  * reference (its ANE runtime has no such switches). */
 int llm_set_option(llm_ctx *ctx, int option, int value);
 
