@@ -87,6 +87,8 @@ __global__ void __launch_bounds__(PersistCfg<BN, EPI>::THREADS, 1)
   __shared__ float s_bsc[GROUPS][BN];
   __shared__ float s_nw[GROUPS][BN];
   __shared__ double s_ss[GROUPS][EPI == EPI_QKV ? NCH : 1][kUmmaTokens];  // QK-norm partial sums per chunk
+  __shared__ int s_rowpage[GROUPS][EPI == EPI_QKV ? kUmmaTokens : 1];      // QKV: a row's K/V page (-1: none)
+  __shared__ int s_rowpos[GROUPS][EPI == EPI_QKV ? kUmmaTokens : 1];       // QKV: a row's position
 
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
   float* const stg = reinterpret_cast<float*>(smem_raw + (sbase - smem_u32(smem_raw)) + STAGES * STAGE_BYTES);
@@ -363,13 +365,8 @@ __global__ void __launch_bounds__(PersistCfg<BN, EPI>::THREADS, 1)
           for (int cc = 1; cc < NCH; ++cc) ss = __dadd_rn(ss, s_ss[g][cc][tl]);
           rr = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)hd), p.eps))));
         }
-        uint8_t* kv_base = nullptr;
-        if (region > 0 && tok_ok && page >= 0 && page < p.n_pages) {
-          const size_t blk = ((static_cast<size_t>(p.layer) * p.n_pages + page) * p.n_kv_heads + head) * 2 + (region - 1);
-          kv_base = reinterpret_cast<uint8_t*>(reinterpret_cast<OutT*>(p.kv_pool) + blk * 16 * hd);
-        } else if (region > 0 && tok_ok && cb == 0 && p.err) {
-          atomicExch(p.err, kDevBadPage);
-        }
+        if (region > 0 && tok_ok && !(page >= 0 && page < p.n_pages) && cb == 0 && p.err) atomicExch(p.err, kDevBadPage);
+        uint4 pk[CPW][4];
 #pragma unroll
         for (int w = 0; w < CPW; ++w) {
           float (&v)[32] = vv[w];
@@ -394,24 +391,45 @@ __global__ void __launch_bounds__(PersistCfg<BN, EPI>::THREADS, 1)
               v[2 * i + 1] = __fadd_rn(__fmul_rn(a0, sn[i]), __fmul_rn(a1, cs[i]));
             }
           }
-          uint4 pk[4];
 #pragma unroll
           for (int h = 0; h < 4; ++h) {
-            pk[h].x = ActTraits<OutT>::pack2(v[8 * h + 0], v[8 * h + 1]);
-            pk[h].y = ActTraits<OutT>::pack2(v[8 * h + 2], v[8 * h + 3]);
-            pk[h].z = ActTraits<OutT>::pack2(v[8 * h + 4], v[8 * h + 5]);
-            pk[h].w = ActTraits<OutT>::pack2(v[8 * h + 6], v[8 * h + 7]);
+            pk[w][h].x = ActTraits<OutT>::pack2(v[8 * h + 0], v[8 * h + 1]);
+            pk[w][h].y = ActTraits<OutT>::pack2(v[8 * h + 2], v[8 * h + 3]);
+            pk[w][h].z = ActTraits<OutT>::pack2(v[8 * h + 4], v[8 * h + 5]);
+            pk[w][h].w = ActTraits<OutT>::pack2(v[8 * h + 6], v[8 * h + 7]);
           }
-          if (!tok_ok) continue;
+        }
+        // Coalesced stores: the tile's packed rows go through the group's staging area (its RoPE
+        // rows are no longer read once every thread has passed this barrier), then 16-byte
+        // pieces of each row are stored by consecutive threads, to q or to the row's K/V page.
+        constexpr int OP = BN * 2 + 16;  // staged row pitch (bytes): 16 B bank offset per row
+        constexpr int U = BN * 2 / 16;   // 16-byte pieces per row
+        uint8_t* const ost = reinterpret_cast<uint8_t*>(gstg);
+        epi_bar_n<GT>(bar_id);
+#pragma unroll
+        for (int w = 0; w < CPW; ++w) {
+          const int d0 = (cb + w * (GW / 4)) * 32;
+#pragma unroll
+          for (int h = 0; h < 4; ++h) *reinterpret_cast<uint4*>(ost + tl * OP + d0 * 2 + h * 16) = pk[w][h];
+        }
+        if (cb == 0) {  // the warps of chunk 0 cover all 128 rows
+          s_rowpage[g][tl] = (region > 0 && tok_ok && page >= 0 && page < p.n_pages) ? page : -1;
+          s_rowpos[g][tl] = pos;
+        }
+        epi_bar_n<GT>(bar_id);
+        for (int idx = gt; idx < kUmmaTokens * U; idx += GT) {
+          const int row = idx / U, cu = idx % U;
+          const int t = tok0 + row;
+          if (t >= p.M) continue;
+          const uint4 val = *reinterpret_cast<const uint4*>(ost + row * OP + cu * 16);
           if (region == 0) {
-            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<OutT*>(p.q_out) +
-                                                  (static_cast<size_t>(tok) * p.n_heads + head) * hd + d0);
-#pragma unroll
-            for (int h = 0; h < 4; ++h) dst[h] = pk[h];
-          } else if (kv_base) {
-            const int slot = pos & 15;
-#pragma unroll
-            for (int h = 0; h < 4; ++h) *reinterpret_cast<uint4*>(kv_base + kv_off(slot, (d0 >> 3) + h)) = pk[h];
+            *reinterpret_cast<uint4*>(reinterpret_cast<OutT*>(p.q_out) + (static_cast<size_t>(t) * p.n_heads + head) * hd + cu * 8) = val;
+          } else {
+            const int pg = s_rowpage[g][row];
+            if (pg < 0) continue;
+            const size_t blk = ((static_cast<size_t>(p.layer) * p.n_pages + pg) * p.n_kv_heads + head) * 2 + (region - 1);
+            uint8_t* kv_base = reinterpret_cast<uint8_t*>(reinterpret_cast<OutT*>(p.kv_pool) + blk * 16 * hd);
+            *reinterpret_cast<uint4*>(kv_base + kv_off(s_rowpos[g][row] & 15, cu)) = val;
           }
         }
       }
