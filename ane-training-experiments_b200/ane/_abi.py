@@ -52,7 +52,7 @@ EXPORTS = [
     "llm_stories_decode_batch", "llm_ctx_stream", "llm_synchronize", "llm_step_kernel_count", "llm_step_parts",
     "llm_memory_bytes", "llm_time_attention", "llm_profile_step", "llm_trace_step", "llm_trace_begin", "llm_trace_end", "llm_debug_norm_quant", "llm_debug_gemm_i8",
     "llm_debug_gemm_f16", "llm_debug_read_kv", "llm_gemm_i8_splitk_noalloc", "llm_set_option", "llm_set_sampling", "llm_sample_uniform", "llm_debug_sample", "llm_debug_wait_timeout",
-    "llm_eval_window",
+    "llm_eval_window", "llm_debug_exp2",
 ]
 
 LLM_OPT_CUDA_GRAPHS = 1
@@ -148,6 +148,7 @@ def lib() -> C.CDLL:
         "llm_debug_gemm_i8": (C.c_int, [C.c_int, C.POINTER(C.c_int8), C.POINTER(C.c_int8), C.c_int, C.c_int, C.c_int, C.c_int, i32p]),
         "llm_debug_gemm_f16": (C.c_int, [C.c_int, C.c_int, _FP, _FP, C.c_int, C.c_int, C.c_int, C.c_int, _FP]),
         "llm_debug_read_kv": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, _FP, _FP]),
+        "llm_debug_exp2": (C.c_int, [C.c_int, _FP, C.c_int, _FP]),
         "llm_set_option": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
         "llm_gemm_i8_splitk_noalloc": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                                                  C.c_void_p, C.c_void_p]),

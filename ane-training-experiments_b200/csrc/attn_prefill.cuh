@@ -199,16 +199,16 @@ __global__ void __launch_bounds__(kPrefillWarps * 32, 1) attn_prefill_kernel(Pre
       mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
       const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
       const float mu_a = mn_a == -INFINITY ? 0.f : mn_a, mu_b = mn_b == -INFINITY ? 0.f : mn_b;
-      const float al_a = exp2f(m_a - mu_a), al_b = exp2f(m_b - mu_b);
+      const float al_a = exp2_det(m_a - mu_a), al_b = exp2_det(m_b - mu_b);
       m_a = mn_a;
       m_b = mn_b;
       float rs_a = 0.f, rs_b = 0.f;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        sc[j][0] = exp2f(sc[j][0] - mu_a);
-        sc[j][1] = exp2f(sc[j][1] - mu_a);
-        sc[j][2] = exp2f(sc[j][2] - mu_b);
-        sc[j][3] = exp2f(sc[j][3] - mu_b);
+        sc[j][0] = exp2_det(sc[j][0] - mu_a);
+        sc[j][1] = exp2_det(sc[j][1] - mu_a);
+        sc[j][2] = exp2_det(sc[j][2] - mu_b);
+        sc[j][3] = exp2_det(sc[j][3] - mu_b);
         rs_a += sc[j][0] + sc[j][1];
         rs_b += sc[j][2] + sc[j][3];
       }

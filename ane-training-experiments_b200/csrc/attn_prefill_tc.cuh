@@ -290,23 +290,24 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(PrefillAttnPara
       for (int j = 0; j < 8; ++j) m8[j] = sv[j];
 #pragma unroll
       for (int j = 8; j < 64; ++j) m8[j & 7] = fmaxf(m8[j & 7], sv[j]);
-      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * sl2;  // scale > 0
+      const float mx = __fmul_rn(fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                                       fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))), sl2);  // scale > 0
       // move the reference max only past the gap; the first visible tile always sets it
-      const bool move = mx > m_ref + Cfg::RESCALE_LOG2;
+      const bool move = mx > __fadd_rn(m_ref, Cfg::RESCALE_LOG2);
       const float m_new = move ? mx : m_ref;
       const float mu = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = move ? ex2_approx(m_ref - mu) : 1.0f;
+      const float alpha = move ? exp2_det(__fsub_rn(m_ref, mu)) : 1.0f;
       float r8[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) r8[j] = 0.f;
 #pragma unroll
       for (int j = 0; j < 64; ++j) {
-        sv[j] = ex2_approx(fmaf(sv[j], sl2, -mu));
-        r8[j & 7] += sv[j];
+        sv[j] = exp2_det(__fmaf_rn(sv[j], sl2, -mu));
+        r8[j & 7] = __fadd_rn(r8[j & 7], sv[j]);
       }
-      const float rs = ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
-      l_run = l_run * alpha + rs;
+      const float rs = __fadd_rn(__fadd_rn(__fadd_rn(r8[0], r8[1]), __fadd_rn(r8[2], r8[3])),
+                                 __fadd_rn(__fadd_rn(r8[4], r8[5]), __fadd_rn(r8[6], r8[7])));
+      l_run = __fmaf_rn(l_run, alpha, rs);
       m_ref = m_new;
 
       // O holds PV of tiles < t: rescale rows whose reference moved, after PV_{t-1} completed
@@ -323,7 +324,7 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(PrefillAttnPara
           tmem_ld32(trow + 128 + c * 32, r);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * alpha);
+          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__fmul_rn(__uint_as_float(r[j]), alpha));
           tmem_st32(trow + 128 + c * 32, r);
         }
       }
@@ -366,7 +367,7 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(PrefillAttnPara
     }
     if (!ok) failed = true;
     // O row / l -> output row (fp32, or the activation type)
-    const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
+    const float inv = l_run > 0.f ? __fdiv_rn(1.0f, l_run) : 0.f;
 #pragma unroll
     for (int c = 0; c < HD / 32; ++c) {
       uint32_t r[32];
@@ -378,17 +379,17 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(PrefillAttnPara
         float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + oi);
 #pragma unroll
         for (int j = 0; j < 32; j += 4)
-          dst[j / 4] = make_float4(__uint_as_float(r[j]) * inv, __uint_as_float(r[j + 1]) * inv,
-                                   __uint_as_float(r[j + 2]) * inv, __uint_as_float(r[j + 3]) * inv);
+          dst[j / 4] = make_float4(__fmul_rn(__uint_as_float(r[j]), inv), __fmul_rn(__uint_as_float(r[j + 1]), inv),
+                                   __fmul_rn(__uint_as_float(r[j + 2]), inv), __fmul_rn(__uint_as_float(r[j + 3]), inv));
       } else {
         uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.out) + oi);
 #pragma unroll
         for (int j = 0; j < 32; j += 8) {
           uint4 v;
-          v.x = ActTraits<T>::pack2(__uint_as_float(r[j]) * inv, __uint_as_float(r[j + 1]) * inv);
-          v.y = ActTraits<T>::pack2(__uint_as_float(r[j + 2]) * inv, __uint_as_float(r[j + 3]) * inv);
-          v.z = ActTraits<T>::pack2(__uint_as_float(r[j + 4]) * inv, __uint_as_float(r[j + 5]) * inv);
-          v.w = ActTraits<T>::pack2(__uint_as_float(r[j + 6]) * inv, __uint_as_float(r[j + 7]) * inv);
+          v.x = ActTraits<T>::pack2(__fmul_rn(__uint_as_float(r[j]), inv), __fmul_rn(__uint_as_float(r[j + 1]), inv));
+          v.y = ActTraits<T>::pack2(__fmul_rn(__uint_as_float(r[j + 2]), inv), __fmul_rn(__uint_as_float(r[j + 3]), inv));
+          v.z = ActTraits<T>::pack2(__fmul_rn(__uint_as_float(r[j + 4]), inv), __fmul_rn(__uint_as_float(r[j + 5]), inv));
+          v.w = ActTraits<T>::pack2(__fmul_rn(__uint_as_float(r[j + 6]), inv), __fmul_rn(__uint_as_float(r[j + 7]), inv));
           dst[j / 8] = v;
         }
       }

@@ -7,7 +7,9 @@
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <math.h>
 #include <stdint.h>
+#include <string.h>
 
 namespace llm {
 
@@ -125,17 +127,42 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// 2^x by the MUFU unit (PTX ex2.approx.ftz.f32: relative error ~2^-22, 2^-inf = +0)
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
-  return y;
-}
-// 1/x by the MUFU unit (PTX rcp.approx.ftz.f32: within ~1 ulp; 1/inf = +0)
-__device__ __forceinline__ float rcp_approx(float x) {
-  float y;
-  asm("rcp.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
-  return y;
+// 2^x built only from IEEE round-to-nearest operations, so that a CPU restatement with the same
+// operations (C99 fmaf, rintf) gives the same bits: n = rint(x), f = x - n in [-0.5, 0.5],
+// 2^f by the degree-7 Taylor polynomial of exp(f ln 2) (coefficients (ln 2)^k / k! rounded to
+// f32; truncation error below 1e-8 on [-0.5, 0.5]) in Horner form with fused multiply-adds,
+// then one multiplication by 2^n.  Results below 2^-126 (x < -126, -inf included) are 0, x >=
+// 127.5 gives +inf; NaN gives 0.  Within 1 ulp of 2^x on [-126, 127.5).  Runs on the FMA pipe
+// (no MUFU), about 15 instructions.
+__host__ __device__ __forceinline__ float exp2_det(float x) {
+  const float xc = fminf(fmaxf(x, -126.0f), 127.5f);
+#ifdef __CUDA_ARCH__
+  const int n = __float2int_rn(xc);
+  const float f = __fsub_rn(xc, __int2float_rn(n));
+  float p = __fmaf_rn(0x1.ffcbfcp-17f, f, 0x1.430912p-13f);
+  p = __fmaf_rn(p, f, 0x1.5d87fep-10f);
+  p = __fmaf_rn(p, f, 0x1.3b2ab6p-7f);
+  p = __fmaf_rn(p, f, 0x1.c6b08ep-5f);
+  p = __fmaf_rn(p, f, 0x1.ebfbe0p-3f);
+  p = __fmaf_rn(p, f, 0x1.62e430p-1f);
+  p = __fmaf_rn(p, f, 1.0f);
+  const float r = __fmul_rn(p, __int_as_float((n + 127) << 23));
+#else
+  const int n = static_cast<int>(rintf(xc));
+  const float f = xc - static_cast<float>(n);
+  float p = fmaf(0x1.ffcbfcp-17f, f, 0x1.430912p-13f);
+  p = fmaf(p, f, 0x1.5d87fep-10f);
+  p = fmaf(p, f, 0x1.3b2ab6p-7f);
+  p = fmaf(p, f, 0x1.c6b08ep-5f);
+  p = fmaf(p, f, 0x1.ebfbe0p-3f);
+  p = fmaf(p, f, 0x1.62e430p-1f);
+  p = fmaf(p, f, 1.0f);
+  uint32_t bits = static_cast<uint32_t>(n + 127) << 23;
+  float s;
+  memcpy(&s, &bits, 4);
+  const float r = p * s;
+#endif
+  return x >= -126.0f ? (x >= 127.5f ? INFINITY : r) : 0.0f;
 }
 // Bounded wait: false when the bound ran out (the caller reports kDevWaitTimeout).
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {

@@ -75,18 +75,15 @@ struct GemmParams {
   int silu_form;
 };
 
-// SiLU gate of one (h1, h3) pair in the selected form (see GemmParams::silu_form).  Form 0 (the
-// decoder's h1 / (1 + exp(-h1)) * h3) runs on the MUFU unit: exp(-h1) = 2^(-h1 log2 e) by
-// ex2.approx and the quotient as h1 * rcp.approx(1 + exp(-h1)), a few ulp from the correctly
-// rounded value (about 8 instructions instead of ~30); form 1 keeps storiesane's exact
-// rounding steps.
+// SiLU gate of one (h1, h3) pair in the selected form (see GemmParams::silu_form), built from
+// IEEE round-to-nearest steps only so that the CPU oracle restates it bit for bit:
+// e = exp(-h1) as exp2_det(-h1 * f32(log2 e)); form 0 (stories.Decoder's silu, infer.go:324-326)
+// h1 / (1 + e) * h3, form 1 (storiesane, accel_other.go:66-71) (h1 * (1 / (1 + e))) * h3.
 __device__ __forceinline__ float swiglu_pair(float h1, float up, int form) {
-  if (form == 0) {
-    const float d = __fadd_rn(1.0f, ex2_approx(__fmul_rn(h1, -1.4426950408889634f)));
-    return __fmul_rn(__fmul_rn(h1, rcp_approx(d)), up);
-  }
-  const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-h1)));
-  return __fmul_rn(__fmul_rn(h1, sig), up);
+  const float e = exp2_det(__fmul_rn(h1, -1.4426950408889634f));
+  const float d = __fadd_rn(1.0f, e);
+  if (form == 0) return __fmul_rn(__fdiv_rn(h1, d), up);
+  return __fmul_rn(__fmul_rn(h1, __fdiv_rn(1.0f, d)), up);
 }
 // Residual update of one element (see GemmParams::resid_scale).
 __device__ __forceinline__ float resid_add(float y, float r, float scale) {

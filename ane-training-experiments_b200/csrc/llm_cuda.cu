@@ -1247,23 +1247,24 @@ int validate_row(llm_ctx* c, int seq, int tok, int pos) {
   return LLM_OK;
 }
 
+// Segments of the longest context the KV cache can hold: the segment stride of the split
+// attention workspace.
+int attn_ws_segs(const llm_ctx* c) {
+  return std::max(1, ((c->max_pos + 15) / 16 + kAttnSegPages - 1) / kAttnSegPages);
+}
+
+// CTAs per (query block, kv head) of a decode attention launch.  The attention arithmetic does
+// not depend on this choice (segments fold in a fixed order); it only spreads a small batch's
+// long contexts over more SMs.  Splitting needs every segment state in the workspace.
 int attn_splits_for(const llm_ctx* c, int n_blocks, int max_ctx) {
-  if (c->attn_splits > 0) {  // fixed by llm_set_option, bounded by the pages and the workspace
-    int s = std::min(c->attn_splits, std::max(1, (max_ctx + 15) / 16));
-    while (s > 1 && static_cast<size_t>(n_blocks) * c->cfg.n_kv_heads * s * 8 * (c->cfg.head_dim + 2) > c->ws_floats / kMaxParts) --s;
-    return s;
-  }
+  const int segs = std::max(1, ((max_ctx + 15) / 16 + kAttnSegPages - 1) / kAttnSegPages);
+  const size_t need = static_cast<size_t>(n_blocks) * c->cfg.n_kv_heads * attn_ws_segs(c) * 8 * (c->cfg.head_dim + 2);
+  if (need > c->ws_floats / kMaxParts) return 1;  // the workspace is divided between micro-batches
+  if (c->attn_splits > 0) return std::min(c->attn_splits, segs);  // fixed by llm_set_option
   const int ctas = n_blocks * c->cfg.n_kv_heads;
   const int target = 2 * c->n_sm;
   if (ctas >= target) return 1;
-  const int pages = (max_ctx + 15) / 16;
-  int s = (target + ctas - 1) / ctas;
-  s = std::min(s, std::max(1, pages / 4));
-  s = std::min(s, 64);
-  // the workspace is divided between the micro-batches of the overlapped schedule
-  auto need = [&](int sp) { return static_cast<size_t>(n_blocks) * c->cfg.n_kv_heads * sp * 8 * (c->cfg.head_dim + 2); };
-  while (s > 1 && need(s) > c->ws_floats / kMaxParts) --s;
-  return std::max(1, s);
+  return std::max(1, std::min({(target + ctas - 1) / ctas, segs, 64}));
 }
 
 // ---------------------------------------------------------------------------- forward
@@ -1555,6 +1556,7 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
     ap.layer = l;
     ap.n_pages = c->n_pages;
     ap.splits = rs.attn_splits;
+    ap.ws_segs = attn_ws_segs(c);
     ap.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(k.head_dim)));
     ap.out = bytes(c->attn, static_cast<size_t>(P.r0) * Q * (i8 ? 4 : ab));
     ap.out_f32 = i8 ? 1 : 0;
@@ -2426,6 +2428,7 @@ extern "C" int llm_time_attention(llm_ctx* c, int iters, double* us_per_launch, 
   ap.n_kv_heads = k.n_kv_heads;
   ap.n_pages = c->n_pages;
   ap.splits = c->gen_splits;
+  ap.ws_segs = attn_ws_segs(c);
   ap.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(k.head_dim)));
   ap.out = c->attn;
   ap.out_f32 = c->in8 ? 1 : 0;
@@ -2783,6 +2786,25 @@ extern "C" int llm_debug_sample(int device, const float* logits, int rows, int v
   CU(cudaGetLastError());
   CU(cudaDeviceSynchronize());
   CU(cudaMemcpy(out, dout.p, static_cast<size_t>(rows) * 4, cudaMemcpyDeviceToHost));
+  return LLM_OK;
+}
+
+__global__ void exp2_probe_kernel(const float* x, float* y, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = exp2_det(x[i]);
+}
+
+extern "C" int llm_debug_exp2(int device, const float* x, int n, float* out) {
+  if (!x || !out || n <= 0) return fail(LLM_ERR_INVALID, "bad arguments");
+  if (cudaSetDevice(device) != cudaSuccess) return fail(LLM_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+  DevBuf dx, dy;
+  CU(cudaMalloc(&dx.p, static_cast<size_t>(n) * 4));
+  CU(cudaMalloc(&dy.p, static_cast<size_t>(n) * 4));
+  CU(cudaMemcpy(dx.p, x, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice));
+  exp2_probe_kernel<<<(n + 255) / 256, 256>>>(static_cast<const float*>(dx.p), static_cast<float*>(dy.p), n);
+  CU(cudaGetLastError());
+  CU(cudaDeviceSynchronize());
+  CU(cudaMemcpy(out, dy.p, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToHost));
   return LLM_OK;
 }
 

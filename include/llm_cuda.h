@@ -317,6 +317,9 @@ int llm_debug_gemm_i8(int device, const int8_t *A, const int8_t *B, int M, int N
 /* 16-bit GEMM (dtype LLM_DTYPE_F16 / BF16; inputs given as fp32 and rounded) -> fp32 C. */
 int llm_debug_gemm_f16(int device, int dtype, const float *A, const float *B, int M, int N, int K,
                        int splits, float *C);
+/* The device's exp2_det (the softmax and SwiGLU exponential: 2^x from round-to-nearest f32
+ * steps, restated by the CPU oracle) on host values x[n]. */
+int llm_debug_exp2(int device, const float *x, int n, float *out);
 /* Read back cached K and V of (layer, seq, pos) as fp32 [kv_dim] each. */
 int llm_debug_read_kv(llm_ctx *ctx, int layer, int seq, int pos, float *k, float *v);
 

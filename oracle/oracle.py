@@ -60,6 +60,11 @@ def lib() -> C.CDLL:
         "oracle_model_new": (C.c_void_p, [C.POINTER(oracle_config), C.POINTER(oracle_weights_f32)]),
         "oracle_model_free": (None, [C.c_void_p]),
         "oracle_model_set_storiesane": (None, [C.c_void_p, C.c_int]),
+        "oracle_model_set_gpu_order": (None, [C.c_void_p, C.c_int]),
+        "oracle_seq_set_prefill": (None, [C.c_void_p, C.c_int]),
+        "oracle_exp2_det": (C.c_float, [C.c_float]),
+        "oracle_mma16": (C.c_float, [C.c_float, _FP, _FP, C.c_int, C.c_int]),
+        "oracle_gemm_mma": (None, [_FP, _FP, C.c_int, C.c_int, C.c_int, C.c_int, _FP]),
         "oracle_seq_new": (C.c_void_p, [C.c_void_p]),
         "oracle_seq_free": (None, [C.c_void_p]),
         "oracle_seq_reset": (None, [C.c_void_p]),
@@ -104,7 +109,9 @@ def f32(a):
 class Model:
     """oracle_model over fp32 weights given as a dict or as ane.stories.ModelWeights."""
 
-    def __init__(self, cfg: dict, weights, mode: str = "fp32", storiesane: bool = False):
+    def __init__(self, cfg: dict, weights, mode: str = "fp32", storiesane: bool = False, gpu_order: bool = False):
+        """gpu_order: restate the CUDA path's order of operations (bit-identical results in
+        the emulation modes); default: the reference's arithmetic at the mode's precision."""
         self.cfg = dict(cfg)
         self.vocab = cfg["vocab"]
         self.max_seq = cfg["max_seq"]
@@ -131,11 +138,14 @@ class Model:
             raise ValueError("oracle_model_new rejected the configuration")
         if storiesane:
             lib().oracle_model_set_storiesane(self.h, 1)
+        self.gpu_order = bool(gpu_order) and mode != "fp32"
+        if self.gpu_order:
+            lib().oracle_model_set_gpu_order(self.h, 1)
 
     def eval_window(self, tokens) -> np.ndarray:
         """ane/storiesane/engine.go:804-842: logits of every window position, channel-first
-        [vocab, len(tokens)] (positions 0..len-1 from an empty cache)."""
-        _, lg = self.seq().teacher_forced(list(tokens), want_logits=True)
+        [vocab, len(tokens)] (positions 0..len-1 from an empty cache; one prefill)."""
+        _, lg = self.seq().teacher_forced(list(tokens), want_logits=True, n_prefill=len(tokens))
         return np.ascontiguousarray(lg.T)
 
     def seq(self) -> "Seq":
@@ -179,7 +189,10 @@ class Seq:
             raise ValueError(f"oracle_decode failed: {rc}")
         return out[: n.value].tolist(), pl.value, bool(eos.value)
 
-    def teacher_forced(self, tokens, want_logits=False):
+    def teacher_forced(self, tokens, want_logits=False, n_prefill=0):
+        """n_prefill (GPU order): the first n_prefill positions were one prefill (the prompt);
+        the rest decode steps."""
+        lib().oracle_seq_set_prefill(self.h, int(n_prefill))
         t = np.ascontiguousarray(np.asarray(tokens, np.int32))
         am = np.zeros(len(t), np.int32)
         lg = np.zeros((len(t), self.m.vocab), np.float32) if want_logits else None
@@ -237,6 +250,24 @@ def gemm_i8(A, B):
     B = np.ascontiguousarray(B, np.int8)
     Cm = np.zeros((A.shape[0], B.shape[0]), np.int32)
     lib().oracle_gemm_i8(_p(A, C.c_int8), _p(B, C.c_int8), A.shape[0], B.shape[0], A.shape[1], _p(Cm, C.c_int32))
+    return Cm
+
+
+def exp2_det(x: float) -> float:
+    return lib().oracle_exp2_det(x)
+
+
+def mma16(c: float, a, b, act: int) -> float:
+    """One tensor-core MMA step (see oracle.h oracle_mma16); act 1 fp16, 2 bf16."""
+    a, b = f32(a), f32(b)
+    return lib().oracle_mma16(c, _p(a), _p(b), a.size, act)
+
+
+def gemm_mma(A, B, act: int):
+    """C = A . B^T as the 16-bit GEMM kernels form it (MMA chain over k, no split-K)."""
+    A, B = f32(A), f32(B)
+    Cm = np.zeros((A.shape[0], B.shape[0]), np.float32)
+    lib().oracle_gemm_mma(_p(A), _p(B), A.shape[0], B.shape[0], A.shape[1], act, _p(Cm))
     return Cm
 
 

@@ -1,0 +1,99 @@
+"""Bit-exact parity of the CUDA token loop with the oracle in GPU order.
+
+The oracle's GPU-order mode restates the CUDA path's arithmetic step for step: the measured
+rounding of the tensor-core MMA (exact products, terms truncated to a 26-bit window below the
+largest alignment exponent, the sum rounded toward zero), the deterministic exp2 of the softmax
+and SwiGLU gate, the row kernel's lane-ordered float64 RMS sums, and the fixed reduction orders
+of the prefill and decode attention kernels.  These tests check each piece on the device and
+then whole decodes, where logits and tokens must be identical bit for bit.  The decode
+attention's reduction order does not depend on the split count, so a sequence's results do not
+depend on the batch it runs in (reference rows are independent: ane/stories/infer.go:204-299)."""
+import numpy as np
+import pytest
+
+import oracle as O
+from ane import _abi
+from ane.stories import ModelConfig, SyntheticWeights
+from parity import gpu_order, gpu_run, oracle_check
+from test_gpu_decode import TINY_GQA, TINY_MHA, engine, weights
+
+pytestmark = pytest.mark.gpu
+
+
+def _act_values(rng, shape, act, kind):
+    if kind == "normal":
+        x = rng.standard_normal(shape)
+    else:  # exponents spread over 2^-12 .. 2^4, random signs
+        x = rng.choice([-1.0, 1.0], shape) * rng.uniform(1, 2, shape) * np.exp2(rng.integers(-12, 5, shape))
+    x = x.astype(np.float32)
+    r = O.round_f16 if act == 1 else O.round_bf16
+    return np.vectorize(r, otypes=[np.float32])(x)
+
+
+@pytest.mark.parametrize("act", [1, 2], ids=["fp16", "bf16"])
+@pytest.mark.parametrize("path", [-1, 1], ids=["tcgen05", "mma.sync"])
+@pytest.mark.parametrize("kind", ["normal", "wide"])
+def test_gemm_kernels_follow_the_tensor_core_model(act, path, kind):
+    """The 16-bit GEMM kernels (tcgen05 and mma.sync, no split-K) against O.gemm_mma: every
+    output bit-identical."""
+    rng = np.random.default_rng(10 * act + (path > 0) + (kind == "wide") * 100)
+    M, N, K = 128, 128, 256
+    A = _act_values(rng, (M, K), act, kind)
+    B = _act_values(rng, (N, K), act, kind)
+    C = np.zeros((M, N), np.float32)
+    _abi.check(_abi.lib().llm_debug_gemm_f16(0, act, _abi.ptr(A), _abi.ptr(B), M, N, K, path, _abi.ptr(C)))
+    want = O.gemm_mma(A, B, act)
+    bad = np.count_nonzero(C.view(np.uint32) != want.view(np.uint32))
+    assert bad == 0, f"{bad} of {C.size} outputs differ from the model"
+
+
+def test_device_exp2_equals_oracle():
+    rng = np.random.default_rng(3)
+    x = np.concatenate([np.linspace(-130, 130, 20001), rng.uniform(-30, 1, 20000), [-np.inf, np.inf, 0.0, -126.0,
+                                                                                   127.49, 127.5]]).astype(np.float32)
+    out = np.zeros_like(x)
+    _abi.check(_abi.lib().llm_debug_exp2(0, _abi.ptr(x), x.size, _abi.ptr(out)))
+    want = np.array([O.exp2_det(float(v)) for v in x], np.float32)
+    assert np.array_equal(out.view(np.uint32), want.view(np.uint32))
+    ok = (x > -120) & (x < 120)
+    rel = np.abs(out[ok].astype(np.float64) - np.exp2(x[ok].astype(np.float64))) / np.exp2(x[ok].astype(np.float64))
+    assert rel.max() < 2.5e-7  # within ~2 ulp of 2^x
+
+
+def _exact(cfg, dtype, w, prompts, steps, max_pos, splits=0):
+    eng = engine(cfg, dtype, w, max_batch=len(prompts), max_pos=max_pos)
+    if splits:
+        eng.set_option(_abi.LLM_OPT_ATTN_SPLITS, splits)
+    toks, logits = gpu_run(eng, prompts, steps)
+    eng.close()
+    return toks, logits
+
+
+@pytest.mark.parametrize("cfg", [TINY_MHA, TINY_GQA], ids=lambda c: c.name)
+@pytest.mark.parametrize("dtype", ["fp16", "bf16", "w8a8_fp16", "w8a8_bf16"])
+def test_tiny_decode_bit_exact(cfg, dtype):
+    """Prompts across prefill tiles (64 positions), decode continuing into a second 16-page
+    segment: logits and tokens equal the GPU-order oracle's bit for bit."""
+    w = weights(cfg)
+    rng = np.random.default_rng(7)
+    lens = [1, 17, 64, 65, 130, 250]
+    prompts = [rng.integers(3, cfg.vocab, L).tolist() for L in lens]
+    toks, logits = _exact(cfg, dtype, w, prompts, steps=20, max_pos=288)
+    m = gpu_order(cfg, w, dtype)
+    worst, agree, n = oracle_check(m, prompts, toks, logits)
+    print(f"{cfg.name} {dtype}: max|dlogit| vs GPU-order oracle = {worst:.3e}, top1 {agree:.4f} over {n}")
+    assert worst == 0.0 and agree == 1.0
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "w8a8_bf16"])
+def test_split_count_does_not_change_results(dtype):
+    """The same sequences decoded with 1, 2 and 3 CTAs per (sequence, kv head): identical."""
+    cfg = TINY_GQA
+    w = weights(cfg)
+    rng = np.random.default_rng(9)
+    prompts = [rng.integers(3, cfg.vocab, L).tolist() for L in (300, 420, 5)]
+    runs = [_exact(cfg, dtype, w, prompts, steps=12, max_pos=512, splits=s) for s in (1, 2, 3)]
+    for toks, logits in runs[1:]:
+        assert toks == runs[0][0]
+        for a, b in zip(logits, runs[0][1]):
+            assert np.array_equal(a, b)
