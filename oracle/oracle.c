@@ -466,9 +466,11 @@ struct oracle_seq {
   int8_t *qa;
   int n_prefill; /* GPU order: positions below this ran through the prefill attention kernel */
   int16_t *ksm, *kse, *vsm, *vse; /* GPU order: the KV cache split for the MMA model */
+  int logits_from; /* teacher-forced passes skip the classifier below this position */
 };
 
 void oracle_seq_set_prefill(oracle_seq *s, int n_prefill) { s->n_prefill = n_prefill; }
+void oracle_seq_set_logits_from(oracle_seq *s, int pos) { s->logits_from = pos; }
 
 static void mat_init(mat_t *mt, const float *src, int rows, int cols, int act, int i8) {
   memset(mt, 0, sizeof *mt);
@@ -619,6 +621,37 @@ static uint64_t splitmix64(uint64_t x) {
   x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
   x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
   return x ^ (x >> 31);
+}
+
+/* The synthetic-weight generator of the token loop's test and benchmark models, restated so
+ * the CPU legs need no other library: element i of stream `stream` is a function of
+ * (seed, stream, i) only.  key = SplitMix64(seed ^ SplitMix64(stream * C1 + C2)); pair j draws
+ * a = SplitMix64(key + 2j), b = SplitMix64(key + 2j + 1), u1 = (top 53 bits of a + 0.5) / 2^53,
+ * u2 = (top 53 bits of b) / 2^53 and applies Box-Muller in double:
+ * r = sqrt(-2 ln u1), elements 2j, 2j+1 = f32(stddev * scale * r * cos / sin(2 pi u2)). */
+void oracle_synth_normal(float *dst, uint64_t n, uint64_t seed, uint64_t stream, double stddev, double scale) {
+  const uint64_t key = splitmix64(seed ^ splitmix64(stream * 0xD1B54A32D192ED03ull + 0x8CB92BA72F3D8DD7ull));
+  const double mult = stddev * scale;
+  const int64_t pairs = (int64_t)((n + 1) / 2);
+#pragma omp parallel for schedule(static)
+  for (int64_t j = 0; j < pairs; j++) {
+    const double two_pi = 6.283185307179586476925286766559;
+    const uint64_t a = splitmix64(key + 2 * (uint64_t)j), b = splitmix64(key + 2 * (uint64_t)j + 1);
+    const double u1 = ((double)(a >> 11) + 0.5) * (1.0 / 9007199254740992.0);
+    const double u2 = (double)(b >> 11) * (1.0 / 9007199254740992.0);
+    const double r = sqrt(-2.0 * log(u1));
+    const double z0 = r * cos(two_pi * u2), z1 = r * sin(two_pi * u2);
+    dst[2 * j] = (float)(mult * z0);
+    if ((uint64_t)(2 * j + 1) < n) dst[2 * j + 1] = (float)(mult * z1);
+  }
+}
+
+/* Stream ids of the synthetic model's tensors: layer l, kind 0..6 = Wq Wk Wv Wo W1 W2 W3;
+ * kind 7 = the embedding, 8 = an untied classifier. */
+uint64_t oracle_synth_stream(int layer, int kind) {
+  if (kind == 7) return 1;
+  if (kind == 8) return 2;
+  return 100ull + 16ull * (uint64_t)layer + (uint64_t)kind;
 }
 
 /* The sampling uniform of the CUDA path's documented generator: a per-stream key from the
@@ -1081,6 +1114,11 @@ int oracle_forward(const oracle_model *m, oracle_seq *s, int token, int pos, flo
       for (int i = 0; i < D; i++) s->x[i] = s->x2[i] + m->resid_scale * s->y[i];
     else
       for (int i = 0; i < D; i++) s->x[i] = s->x2[i] + s->y[i];
+  }
+  if (pos < s->logits_from) { /* a teacher-forced position whose logits nobody reads */
+    memset(s->logits, 0, sizeof(float) * (size_t)c->vocab);
+    if (logits_out) memcpy(logits_out, s->logits, sizeof(float) * (size_t)c->vocab);
+    return ORACLE_OK;
   }
   norm_vec(m, s->xn, s->x, m->rms_final, D);
   round_vec(m->act, s->xn, D);

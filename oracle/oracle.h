@@ -112,6 +112,14 @@ void oracle_seq_free(oracle_seq *s);
 void oracle_seq_reset(oracle_seq *s);
 /* GPU order: positions [0, n_prefill) were computed by the prefill kernels (a prompt). */
 void oracle_seq_set_prefill(oracle_seq *s, int n_prefill);
+/* Forward passes at positions below `pos` skip the classifier (their logits read as zeros):
+ * for long teacher-forced prompts whose logits are not compared.  Default 0. */
+void oracle_seq_set_logits_from(oracle_seq *s, int pos);
+/* The seeded N(0, stddev) weight generator of the synthetic models (SplitMix64 -> Box-Muller in
+ * double, one rounding to f32; element i depends on (seed, stream, i) only) and its stream ids
+ * (layer l, kind 0..6 = Wq Wk Wv Wo W1 W2 W3; 7 embedding; 8 untied classifier). */
+void oracle_synth_normal(float *dst, uint64_t n, uint64_t seed, uint64_t stream, double stddev, double scale);
+uint64_t oracle_synth_stream(int layer, int kind);
 /* Fill the KV cache positions [0, n_pos) with seeded values (for timing samples only). */
 void oracle_seq_fill_kv_synthetic(const oracle_model *m, oracle_seq *s, int n_pos, uint64_t seed);
 /* forwardOne: returns ORACLE_OK or an error; logits_out may be NULL. */

@@ -29,6 +29,15 @@ class oracle_config(C.Structure):
 
 _FP = C.POINTER(C.c_float)
 
+# Model dimensions of the two reference models (ane/stories/config.go:3-10 with infer.go:102,307;
+# training/training_dynamic/models/qwen3_06b.h:6-16 with per-head QK-norm, theta 1e6, eps 1e-6).
+PRESETS = {
+    "stories110m": dict(dim=768, hidden=2048, n_layers=12, n_heads=12, n_kv_heads=12, head_dim=64, vocab=32000,
+                        max_seq=256, qk_norm=0, norm_eps=1e-5, rope_theta=10000.0, tied_embed=1),
+    "qwen3-0.6b": dict(dim=1024, hidden=3072, n_layers=28, n_heads=16, n_kv_heads=8, head_dim=128, vocab=151936,
+                       max_seq=4096, qk_norm=1, norm_eps=1e-6, rope_theta=1e6, tied_embed=1),
+}
+
 
 class oracle_layer_f32(C.Structure):
     _fields_ = [(n, _FP) for n in ("wq", "wk", "wv", "wo", "w1", "w2", "w3", "rms_att", "rms_ffn", "q_norm", "k_norm")]
@@ -62,6 +71,7 @@ def lib() -> C.CDLL:
         "oracle_model_set_storiesane": (None, [C.c_void_p, C.c_int]),
         "oracle_model_set_gpu_order": (None, [C.c_void_p, C.c_int]),
         "oracle_seq_set_prefill": (None, [C.c_void_p, C.c_int]),
+        "oracle_seq_set_logits_from": (None, [C.c_void_p, C.c_int]),
         "oracle_exp2_det": (C.c_float, [C.c_float]),
         "oracle_mma16": (C.c_float, [C.c_float, _FP, _FP, C.c_int, C.c_int]),
         "oracle_gemm_mma": (None, [_FP, _FP, C.c_int, C.c_int, C.c_int, C.c_int, _FP]),
@@ -87,6 +97,8 @@ def lib() -> C.CDLL:
         "oracle_gemm_i8": (None, [i8p, i8p, C.c_int, C.c_int, C.c_int, i32p]),
         "oracle_dequant": (C.c_float, [C.c_int32, C.c_float, C.c_float]),
         "oracle_set_threads": (None, [C.c_int]),
+        "oracle_synth_normal": (None, [_FP, C.c_uint64, C.c_uint64, C.c_uint64, C.c_double, C.c_double]),
+        "oracle_synth_stream": (C.c_uint64, [C.c_int, C.c_int]),
         "oracle_set_attn_reverse": (None, [C.c_int]),
         "oracle_set_matvec_reverse": (None, [C.c_int]),
         "oracle_get_threads": (C.c_int, []),
@@ -189,10 +201,12 @@ class Seq:
             raise ValueError(f"oracle_decode failed: {rc}")
         return out[: n.value].tolist(), pl.value, bool(eos.value)
 
-    def teacher_forced(self, tokens, want_logits=False, n_prefill=0):
+    def teacher_forced(self, tokens, want_logits=False, n_prefill=0, logits_from=0):
         """n_prefill (GPU order): the first n_prefill positions were one prefill (the prompt);
-        the rest decode steps."""
+        the rest decode steps.  Positions below logits_from skip the classifier (their logits
+        and argmax are not meaningful)."""
         lib().oracle_seq_set_prefill(self.h, int(n_prefill))
+        lib().oracle_seq_set_logits_from(self.h, int(logits_from))
         t = np.ascontiguousarray(np.asarray(tokens, np.int32))
         am = np.zeros(len(t), np.int32)
         lg = np.zeros((len(t), self.m.vocab), np.float32) if want_logits else None
@@ -291,6 +305,37 @@ def sample_from_logits(logits, temperature: float, u: float) -> int:
     """ane/stories/infer.go:347-371 with the uniform given."""
     a = f32(logits)
     return lib().oracle_sample_from_logits(_p(a), a.size, temperature, u)
+
+
+class _Layer:
+    def __init__(self, **kw):
+        self.__dict__.update(kw)
+
+
+class SynthWeights:
+    """The synthetic model's fp32 weights from oracle_synth_normal (the layout O.Model reads)."""
+
+    def __init__(self, cfg: dict, seed: int = 1234, out_proj_scale: float = 1.0, stddev: float = 0.02):
+        D, F, L = cfg["dim"], cfg["hidden"], cfg["n_layers"]
+        hd = cfg["head_dim"]
+        Q, KV = cfg["n_heads"] * hd, cfg["n_kv_heads"] * hd
+
+        def g(n, l, k, s=1.0):
+            out = np.empty(n, np.float32)
+            lib().oracle_synth_normal(_p(out), n, seed, lib().oracle_synth_stream(l, k), stddev, s)
+            return out
+
+        qk = bool(cfg.get("qk_norm", 0))
+        self.Layers = [_Layer(Wq=g(Q * D, l, 0).reshape(Q, D), Wk=g(KV * D, l, 1).reshape(KV, D),
+                              Wv=g(KV * D, l, 2).reshape(KV, D), Wo=g(D * Q, l, 3, out_proj_scale).reshape(D, Q),
+                              W1=g(F * D, l, 4).reshape(F, D), W2=g(D * F, l, 5, out_proj_scale).reshape(D, F),
+                              W3=g(F * D, l, 6).reshape(F, D), RMSAtt=np.ones(D, np.float32),
+                              RMSFFN=np.ones(D, np.float32), QNorm=np.ones(hd, np.float32) if qk else None,
+                              KNorm=np.ones(hd, np.float32) if qk else None) for l in range(L)]
+        self.RMSFinal = np.ones(D, np.float32)
+        self.Embed = g(cfg["vocab"] * D, 0, 7).reshape(cfg["vocab"], D)
+        self.SharedCL = bool(cfg.get("tied_embed", 1))
+        self.LMHead = None if self.SharedCL else g(cfg["vocab"] * D, 0, 8).reshape(cfg["vocab"], D)
 
 
 def set_attn_reverse(on: bool):

@@ -60,7 +60,7 @@ def oracle_check(model: "O.Model", prompts, toks, logits):
     for p, t, lg in zip(prompts, toks, logits):
         seq = list(p) + t[:-1]
         s = model.seq()
-        am, ol = s.teacher_forced(seq, want_logits=True, n_prefill=len(p))
+        am, ol = s.teacher_forced(seq, want_logits=True, n_prefill=len(p), logits_from=len(p) - 1)
         P = len(p)
         ref = ol[P - 1:]
         worst = max(worst, float(np.abs(ref - lg).max()))

@@ -407,3 +407,51 @@ def test_sample_from_logits_known_answers_and_restatement():
         t = float(rng.choice([0.0, 0.3, 0.8, 1.0, 1.7]))
         u = float(rng.random())
         assert O.sample_from_logits(lg, t, u) == _sample_py(lg, t, u)
+
+
+def test_oracle_weight_generator_equals_the_library():
+    """The CPU legs of bench.py build the synthetic model with the oracle's restatement of the
+    generator (so they load no product code): bit-identical to llm_synth_normal."""
+    from ane.stories import QWEN3_0_6B, ModelConfig, SyntheticWeights
+    cfg = ModelConfig(dim=64, hidden=96, n_layers=2, n_heads=4, n_kv_heads=2, head_dim=16, vocab=333, max_seq=32,
+                      qk_norm=True, tied_embed=False, name="gen")
+    a = SyntheticWeights(cfg, 99, 0.25, stddev=0.05)
+    b = O.SynthWeights(dict(cfg.oracle_dict(), tied_embed=0), 99, 0.25, stddev=0.05)
+    pairs = [(a.Embed, b.Embed), (a.LMHead, b.LMHead)]
+    for la, lb in zip(a.Layers, b.Layers):
+        pairs += [(getattr(la, k), getattr(lb, k)) for k in ("Wq", "Wk", "Wv", "Wo", "W1", "W2", "W3")]
+    for x, y in pairs:
+        assert x.shape == y.shape and np.array_equal(x.view(np.uint32), y.view(np.uint32))
+    q = O.PRESETS["qwen3-0.6b"]
+    assert (q["dim"], q["hidden"], q["n_layers"], q["n_heads"], q["n_kv_heads"], q["head_dim"], q["vocab"]) == (
+        QWEN3_0_6B.dim, QWEN3_0_6B.hidden, QWEN3_0_6B.n_layers, QWEN3_0_6B.n_heads, QWEN3_0_6B.n_kv_heads,
+        QWEN3_0_6B.head_dim, QWEN3_0_6B.vocab)
+
+
+def test_exp2_det_known_values_and_accuracy():
+    assert O.exp2_det(0.0) == 1.0 and O.exp2_det(1.0) == 2.0 and O.exp2_det(-1.0) == 0.5
+    assert O.exp2_det(-126.0) == 2.0 ** -126 and O.exp2_det(-126.5) == 0.0 and O.exp2_det(float("-inf")) == 0.0
+    assert O.exp2_det(127.5) == float("inf")
+    xs = np.random.default_rng(4).uniform(-100, 100, 20000).astype(np.float32)
+    got = np.array([O.exp2_det(float(x)) for x in xs], np.float64)
+    ref = np.exp2(xs.astype(np.float64))
+    assert (np.abs(got - ref) / ref).max() < 2.5e-7
+
+
+def test_mma_model_known_cases():
+    """The tensor-core step's rules on hand-made cases: exact products, a 26-bit window below
+    the largest alignment exponent with truncation toward zero, the sum rounded toward zero."""
+    one = np.zeros(16, np.float32)
+    a = one.copy(); b = one.copy()
+    a[0], b[0] = 1.0, 1.0
+    a[1], b[1] = 3 * 2.0 ** -13, 2.0 ** -12       # 0.75 ulp of 1.0
+    assert O.mma16(0.0, a, b, 2) == 1.0            # rounded toward zero (nearest would give 1 + 2^-23)
+    a[1], b[1] = -(2.0 ** -13), 2.0 ** -12         # 1 - 2^-25: exact sum just below 1
+    assert O.mma16(0.0, a, b, 2) == np.float32(1 - 2.0 ** -24)
+    a[1], b[1] = -(2.0 ** -20), 2.0 ** -10         # -2^-30: below the window of the product 1*1 -> dropped
+    assert O.mma16(0.0, a, b, 2) == 1.0
+    # the accumulator's alignment exponent is e(c) + 1
+    assert O.mma16(1.0, np.zeros(16, np.float32), np.zeros(16, np.float32), 2) == 1.0
+    c = np.float32(1.0 + 2.0 ** -23)
+    a = one.copy(); b = one.copy(); a[0], b[0] = 2.0 ** -24, 1.0
+    assert O.mma16(float(c), a, b, 2) == c         # adds less than an ulp: truncated
