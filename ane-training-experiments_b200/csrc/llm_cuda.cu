@@ -1200,6 +1200,23 @@ int ensure_pages(llm_ctx* c, int seq, int upto, std::vector<int>* dirty) {
   return LLM_OK;
 }
 
+int upload_dirty(llm_ctx* c, std::vector<int>& dirty);
+
+// Pages through position upto[i] for sequence seq[i], i < n (rows already validated).  If the
+// pool runs out part way, the rows changed so far are still uploaded, so the device block
+// table matches the host's before the error returns (those sequences keep their new pages).
+int reserve_rows(llm_ctx* c, int n, const int32_t* seq, const int* upto) {
+  std::vector<int> dirty;
+  for (int i = 0; i < n; ++i) {
+    const int rc = ensure_pages(c, seq[i], upto[i], &dirty);
+    if (rc) {
+      upload_dirty(c, dirty);
+      return rc;
+    }
+  }
+  return upload_dirty(c, dirty);
+}
+
 int upload_dirty(llm_ctx* c, std::vector<int>& dirty) {
   std::sort(dirty.begin(), dirty.end());
   dirty.erase(std::unique(dirty.begin(), dirty.end()), dirty.end());
@@ -1814,18 +1831,17 @@ extern "C" int llm_decode_step(llm_ctx* c, const int32_t* seq_ids, const int32_t
   if (!seq_ids || !tokens || !positions || !next_tokens) return fail(LLM_ERR_INVALID, "nil buffer");
   if (n <= 0 || n > c->max_seqs) return fail(LLM_ERR_INVALID, "batch %d out of range (1..%d)", n, c->max_seqs);
   RC(set_device(c));
-  std::vector<int> dirty;
   int max_ctx = 0;
   double kv_positions = 0;
   start_stamp(c);
+  // every row is checked before any page is reserved
   for (int i = 0; i < n; ++i) {
     RC(validate_row(c, seq_ids[i], tokens[i], positions[i]));
     if (seen_before(c, seq_ids[i])) return fail(LLM_ERR_INVALID, "sequence %d appears twice in one step", seq_ids[i]);
-    RC(ensure_pages(c, seq_ids[i], positions[i], &dirty));
     max_ctx = std::max(max_ctx, positions[i] + 1);
     kv_positions += positions[i] + 1.0;
   }
-  RC(upload_dirty(c, dirty));
+  RC(reserve_rows(c, n, seq_ids, positions));
   c->step_kv_positions = kv_positions;
   int32_t* h = c->h_pin;
   memcpy(h, seq_ids, n * 4);
@@ -1875,7 +1891,6 @@ int prefill_impl(llm_ctx* c, const int32_t* seq_ids, const int32_t* tokens, cons
   // rows (seq, tok, pos, owner)
   struct Row { int seq, tok, pos, owner; };
   std::vector<Row> rows;
-  std::vector<int> dirty;
   size_t off = 0;
   start_stamp(c);
   for (int i = 0; i < nseq; ++i) {
@@ -1887,10 +1902,13 @@ int prefill_impl(llm_ctx* c, const int32_t* seq_ids, const int32_t* tokens, cons
       RC(validate_row(c, seq_ids[i], tokens[off + j], p0 + j));
       rows.push_back({seq_ids[i], tokens[off + j], p0 + j, i});
     }
-    RC(ensure_pages(c, seq_ids[i], p0 + lens[i] - 1, &dirty));
     off += lens[i];
   }
-  RC(upload_dirty(c, dirty));
+  {  // every row is checked before any page is reserved
+    std::vector<int> upto(nseq);
+    for (int i = 0; i < nseq; ++i) upto[i] = (start_pos ? start_pos[i] : 0) + lens[i] - 1;
+    RC(reserve_rows(c, nseq, seq_ids, upto.data()));
+  }
   if (all_rows && rows.size() > static_cast<size_t>(c->max_rows))
     return fail(LLM_ERR_INVALID, "%zu rows exceed one chunk of %d", rows.size(), c->max_rows);
   if (all_rows) RC(ensure_logits(c, static_cast<int>(rows.size())));
@@ -2083,7 +2101,6 @@ extern "C" int llm_generate_begin(llm_ctx* c, const int32_t* seq_ids, const int3
   if (n <= 0 || n > c->max_seqs) return fail(LLM_ERR_INVALID, "batch %d out of range", n);
   if (max_steps <= 0) return fail(LLM_ERR_INVALID, "max_steps must be positive");
   RC(set_device(c));
-  std::vector<int> dirty;
   int max_ctx = 0;
   double kv_positions = 0;
   start_stamp(c);
@@ -2092,11 +2109,14 @@ extern "C" int llm_generate_begin(llm_ctx* c, const int32_t* seq_ids, const int3
     if (positions[i] + max_steps - 1 >= c->max_pos)
       return fail(LLM_ERR_POS_RANGE, "position out of range: %d", positions[i] + max_steps - 1);
     if (seen_before(c, seq_ids[i])) return fail(LLM_ERR_INVALID, "sequence %d appears twice", seq_ids[i]);
-    RC(ensure_pages(c, seq_ids[i], positions[i] + max_steps - 1, &dirty));
     max_ctx = std::max(max_ctx, positions[i] + max_steps);
     kv_positions += positions[i] + 0.5 * max_steps + 0.5;
   }
-  RC(upload_dirty(c, dirty));
+  {
+    std::vector<int> upto(n);
+    for (int i = 0; i < n; ++i) upto[i] = positions[i] + max_steps - 1;
+    RC(reserve_rows(c, n, seq_ids, upto.data()));
+  }
   if (sampling_on(c)) RC(ensure_logits(c, n));
   const size_t need = static_cast<size_t>(max_steps) * n;
   if (need > c->gen_out_cap) {

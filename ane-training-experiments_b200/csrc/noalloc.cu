@@ -79,6 +79,11 @@ int setup(int device, void** addr) {
 extern "C" int llm_gemm_i8_splitk_noalloc(int device, const int8_t* A, const int8_t* B, int M, int N, int K,
                                           int splits, int32_t* C, void* stream) {
   if (!A || !B || !C) return fail_fmt(LLM_ERR_INVALID, "nil device buffer");
+  // the kernel reads A and B with 16-byte copies and stores C as int32: a misaligned pointer
+  // (an FFI slice at an odd offset) would fault on the device instead of failing here
+  if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) % 16 != 0 ||
+      reinterpret_cast<uintptr_t>(C) % 4 != 0)
+    return fail_fmt(LLM_ERR_INVALID, "misaligned device buffer (A and B need 16-byte, C 4-byte alignment)");
   if (M <= 0 || N <= 0 || K <= 0 || K % 128)
     return fail_fmt(LLM_ERR_INVALID, "bad shape M=%d N=%d K=%d (K must be a positive multiple of 128)", M, N, K);
   if (device < 0 || device >= kNoAllocMaxDevices) return fail_fmt(LLM_ERR_INVALID, "device %d out of range", device);

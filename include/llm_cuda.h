@@ -2,7 +2,7 @@
  * llm_cuda.h -- C ABI of the B200 token loop (prefill + greedy decode) for the Llama-style
  * models of tmc/ane-training-experiments (Stories110M MHA, Qwen3-0.6B GQA).
  *
- * This is the boundary a cgo shim binds (see INTEGRATION.md).  Plain C types only: opaque
+ * This is the boundary a cgo shim binds.  Plain C types only: opaque
  * handles, int status codes, host pointers and sizes.  The context owns all device memory;
  * the caller owns every host buffer it passes.  Status: 0 = LLM_OK, negative = error, with
  * the message available from llm_last_error() (precedent: bridge/stories_trainer_bridge.h:32-36,
@@ -297,7 +297,8 @@ int llm_trace_end(llm_ctx *ctx, char *report, size_t report_len, double *span_us
  * run (a server whose KV page pool already holds the GPU's memory, a decode loop that must not
  * take cudaFree's device-wide synchronisation mid-step, an FFI host that owns the memory
  * policy).  A, B and C are caller-owned DEVICE pointers; the work is enqueued on `stream`
- * (NULL = default stream) and the call returns without waiting.  The split partials and tile
+ * (NULL = default stream) and the call returns without waiting.  A and B must be 16-byte and C
+ * 4-byte aligned (LLM_ERR_INVALID otherwise).  The split partials and tile
  * counters live in one fixed device array of 4 MiB + 1024 counters inside the library; a
  * shape/split combination needing more is rejected with LLM_ERR_INVALID.  The first call on a
  * device resolves that array's device address and sets kernel attributes, so make it before

@@ -139,6 +139,8 @@ def test_host_errors_before_launch():
         eng.decode_step([0], [5], [64])
     with pytest.raises(_abi.LLMError, match="appears twice"):
         eng.decode_step([1, 1], [5, 6], [0, 0])
+    # the rejected step reserved nothing half-way: sequence 1 still decodes
+    eng.decode_step([1], [5], [0])
     with pytest.raises(_abi.LLMError, match="out of range"):
         eng.decode_step([2], [5], [0])
     with pytest.raises(_abi.LLMError) as ei:
