@@ -65,8 +65,20 @@ struct AttnParams {
 };
 
 constexpr int kAttnWarps = 4;
-// Pages per segment of the fixed reduction order (256 positions).
-constexpr int kAttnSegPages = 16;
+// Pages per segment of the fixed reduction order (512 positions).  Fewer, larger segments mean
+// fewer four-warp folds per CTA: 16 / 32 / 64 pages measured 259 / 255 / 249 us per Qwen3 layer at
+// 256 sequences x 1536 positions; 32 keeps splits of 512 positions for small batches.
+#ifndef LLM_ATTN_SEG_PAGES
+#define LLM_ATTN_SEG_PAGES 32
+#endif
+constexpr int kAttnSegPages = LLM_ATTN_SEG_PAGES;
+// Resident CTAs per SM the register budget is sized for (head_dim 128: the shared-memory ring
+// allows three; head_dim 64: five).
+#ifndef LLM_ATTN_MINB_HD64
+#define LLM_ATTN_MINB_HD64 5
+#endif
+template <int HD>
+constexpr int attn_min_blocks() { return HD >= 128 ? 3 : LLM_ATTN_MINB_HD64; }
 
 // Page-ring depth per warp (pages of 16 positions in flight per warp).
 // Two pages (64 KB per CTA, three CTAs per SM) measured faster than three (96 KB, two per SM):
@@ -111,8 +123,9 @@ struct WarpState {
 __device__ __forceinline__ void fold_scales(float ma, float mb, float& M, float& fa, float& fb) {
   M = fmaxf(ma, mb);
   const float mu = M == -INFINITY ? 0.f : M;
-  fa = exp2_det(__fsub_rn(ma, mu));
-  fb = exp2_det(__fsub_rn(mb, mu));
+  const float2 f = exp2_det_lo2(sub2_rn(make_float2(ma, mb), make_float2(mu, mu)));
+  fa = f.x;
+  fb = f.y;
 }
 __device__ __forceinline__ float fold_val(float fa, float a, float fb, float b) {
   return __fmaf_rn(fb, b, __fmul_rn(fa, a));
@@ -225,7 +238,7 @@ __device__ void attn_quant_rows(const AttnParams& p, int r0, int nq, int group, 
 
 
 template <typename T, int HD>
-__global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_kernel(AttnParams p) {
+__global__ void __launch_bounds__(kAttnWarps * 32, attn_min_blocks<HD>()) attn_kernel(AttnParams p) {
   using Cfg = AttnCfg<T, HD>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int PB = Cfg::PAGE_BYTES;
@@ -368,9 +381,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_kernel(AttnParams p) 
       }
       const float mn0 = fmaxf(st.m0, pm0), mn1 = fmaxf(st.m1, pm1);
       const float mu0 = mn0 == -INFINITY ? 0.f : mn0, mu1 = mn1 == -INFINITY ? 0.f : mn1;
-      const float al0 = exp2_det(__fsub_rn(st.m0, mu0)), al1 = exp2_det(__fsub_rn(st.m1, mu1));
-      const float p0 = exp2_det(__fsub_rn(s0, mu0)), p1 = exp2_det(__fsub_rn(s1, mu1));
-      const float p2 = exp2_det(__fsub_rn(s2, mu0)), p3 = exp2_det(__fsub_rn(s3, mu1));
+      const float2 mu01 = make_float2(mu0, mu1);
+      const float2 al = exp2_det_lo2(sub2_rn(make_float2(st.m0, st.m1), mu01));
+      const float2 p01 = exp2_det_lo2(sub2_rn(make_float2(s0, s1), mu01));
+      const float2 p23 = exp2_det_lo2(sub2_rn(make_float2(s2, s3), mu01));
+      const float al0 = al.x, al1 = al.y, p0 = p01.x, p1 = p01.y, p2 = p23.x, p3 = p23.y;
       st.l0 = __fmaf_rn(st.l0, al0, __fadd_rn(p0, p2));
       st.l1 = __fmaf_rn(st.l1, al1, __fadd_rn(p1, p3));
       st.m0 = mn0;

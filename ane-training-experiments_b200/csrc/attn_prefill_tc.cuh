@@ -296,17 +296,24 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(PrefillAttnPara
       const bool move = mx > __fadd_rn(m_ref, Cfg::RESCALE_LOG2);
       const float m_new = move ? mx : m_ref;
       const float mu = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = move ? exp2_det(__fsub_rn(m_ref, mu)) : 1.0f;
-      float r8[8];
+      const float alpha = move ? exp2_det_lo(__fsub_rn(m_ref, mu)) : 1.0f;
+      // p = 2^(s * scale - ref) two positions at a time (packed f32 pairs); the row sum in 8
+      // interleaved partials r8[j & 7] (pairs r4[k] = (r8[2k], r8[2k + 1]))
+      float2 r4[4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) r8[j] = 0.f;
+      for (int k = 0; k < 4; ++k) r4[k] = make_float2(0.f, 0.f);
+      {
+        const float2 sl22 = make_float2(sl2, sl2), nmu = make_float2(-mu, -mu);
 #pragma unroll
-      for (int j = 0; j < 64; ++j) {
-        sv[j] = exp2_det(__fmaf_rn(sv[j], sl2, -mu));
-        r8[j & 7] = __fadd_rn(r8[j & 7], sv[j]);
+        for (int e = 0; e < 32; ++e) {
+          const float2 pe = exp2_det_lo2(fma2_rn(make_float2(sv[2 * e], sv[2 * e + 1]), sl22, nmu));
+          sv[2 * e] = pe.x;
+          sv[2 * e + 1] = pe.y;
+          r4[e & 3] = add2_rn(r4[e & 3], pe);
+        }
       }
-      const float rs = __fadd_rn(__fadd_rn(__fadd_rn(r8[0], r8[1]), __fadd_rn(r8[2], r8[3])),
-                                 __fadd_rn(__fadd_rn(r8[4], r8[5]), __fadd_rn(r8[6], r8[7])));
+      const float rs = __fadd_rn(__fadd_rn(__fadd_rn(r4[0].x, r4[0].y), __fadd_rn(r4[1].x, r4[1].y)),
+                                 __fadd_rn(__fadd_rn(r4[2].x, r4[2].y), __fadd_rn(r4[3].x, r4[3].y)));
       l_run = __fmaf_rn(l_run, alpha, rs);
       m_ref = m_new;
 

@@ -128,41 +128,104 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 // 2^x built only from IEEE round-to-nearest operations, so that a CPU restatement with the same
-// operations (C99 fmaf, rintf) gives the same bits: n = rint(x), f = x - n in [-0.5, 0.5],
-// 2^f by the degree-7 Taylor polynomial of exp(f ln 2) (coefficients (ln 2)^k / k! rounded to
-// f32; truncation error below 1e-8 on [-0.5, 0.5]) in Horner form with fused multiply-adds,
-// then one multiplication by 2^n.  Results below 2^-126 (x < -126, -inf included) are 0, x >=
-// 127.5 gives +inf; NaN gives 0.  Within 1 ulp of 2^x on [-126, 127.5).  Runs on the FMA pipe
-// (no MUFU), about 15 instructions.
-__host__ __device__ __forceinline__ float exp2_det(float x) {
-  const float xc = fminf(fmaxf(x, -126.0f), 127.5f);
+// operations (C99 fmaf) gives the same bits.  x is clamped to [-127, 127.49999]; n = rint(x)
+// by the 1.5 * 2^23 addition (t = x + 1.5*2^23 holds n in its low mantissa bits); f = x - n in
+// [-0.5, 0.5]; 2^f by the degree-7 Taylor polynomial of exp(f ln 2) (coefficients (ln 2)^k / k!
+// rounded to f32; truncation error below 1e-8 on [-0.5, 0.5]) in Horner form with fused
+// multiply-adds; then one multiplication by 2^n built from its exponent bits, which are 0 for
+// n = -127, so x < -126.5 (and -inf, NaN) gives 0.  Within 1 ulp of 2^x for x in [-125, 127.4];
+// results in [2^-126.5, 2^-125) are rounded subnormals; x >= 127.5 gives 2^127.49999.  Runs on
+// the FMA and integer pipes only (no MUFU, no conversion instructions), 15 instructions.
+constexpr float kExp2Magic = 12582912.0f;  // 1.5 * 2^23
+__host__ __device__ __forceinline__ float exp2_poly(float f) {
 #ifdef __CUDA_ARCH__
-  const int n = __float2int_rn(xc);
-  const float f = __fsub_rn(xc, __int2float_rn(n));
   float p = __fmaf_rn(0x1.ffcbfcp-17f, f, 0x1.430912p-13f);
   p = __fmaf_rn(p, f, 0x1.5d87fep-10f);
   p = __fmaf_rn(p, f, 0x1.3b2ab6p-7f);
   p = __fmaf_rn(p, f, 0x1.c6b08ep-5f);
   p = __fmaf_rn(p, f, 0x1.ebfbe0p-3f);
   p = __fmaf_rn(p, f, 0x1.62e430p-1f);
-  p = __fmaf_rn(p, f, 1.0f);
-  const float r = __fmul_rn(p, __int_as_float((n + 127) << 23));
+  return __fmaf_rn(p, f, 1.0f);
 #else
-  const int n = static_cast<int>(rintf(xc));
-  const float f = xc - static_cast<float>(n);
   float p = fmaf(0x1.ffcbfcp-17f, f, 0x1.430912p-13f);
   p = fmaf(p, f, 0x1.5d87fep-10f);
   p = fmaf(p, f, 0x1.3b2ab6p-7f);
   p = fmaf(p, f, 0x1.c6b08ep-5f);
   p = fmaf(p, f, 0x1.ebfbe0p-3f);
   p = fmaf(p, f, 0x1.62e430p-1f);
-  p = fmaf(p, f, 1.0f);
-  uint32_t bits = static_cast<uint32_t>(n + 127) << 23;
-  float s;
-  memcpy(&s, &bits, 4);
-  const float r = p * s;
+  return fmaf(p, f, 1.0f);
 #endif
-  return x >= -126.0f ? (x >= 127.5f ? INFINITY : r) : 0.0f;
+}
+// x already at most 127.49999 (e.g. a softmax exponent s - max <= 0): the same result as
+// exp2_det without the upper clamp.
+__device__ __forceinline__ float exp2_det_lo(float x) {
+  const float xc = fmaxf(x, -127.0f);
+  const float t = __fadd_rn(xc, kExp2Magic);
+  const float f = __fsub_rn(xc, __fsub_rn(t, kExp2Magic));
+  const float p = exp2_poly(f);
+  return __fmul_rn(p, __int_as_float((__float_as_int(t) + (127 - 0x4B400000)) << 23));
+}
+__host__ __device__ __forceinline__ float exp2_det(float x) {
+#ifdef __CUDA_ARCH__
+  return exp2_det_lo(fminf(x, 127.49999f));
+#else
+  const float xc = fminf(fmaxf(x, -127.0f), 127.49999f);
+  const float t = xc + kExp2Magic;
+  const float f = xc - (t - kExp2Magic);
+  const float p = exp2_poly(f);
+  int32_t ti;
+  memcpy(&ti, &t, 4);
+  const uint32_t bits = static_cast<uint32_t>(ti + (127 - 0x4B400000)) << 23;
+  float sc;
+  memcpy(&sc, &bits, 4);
+  return p * sc;
+#endif
+}
+
+// Packed pairs of f32 operations (sm_100: one instruction for two lanes' worth of f32 work).
+__device__ __forceinline__ uint64_t f2_bits(float2 v) {
+  return static_cast<uint64_t>(__float_as_uint(v.x)) | (static_cast<uint64_t>(__float_as_uint(v.y)) << 32);
+}
+__device__ __forceinline__ float2 bits_f2(uint64_t b) {
+  return make_float2(__uint_as_float(static_cast<uint32_t>(b)), __uint_as_float(static_cast<uint32_t>(b >> 32)));
+}
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;\n" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+  return bits_f2(d);
+}
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;\n" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return bits_f2(d);
+}
+__device__ __forceinline__ float2 sub2_rn(float2 a, float2 b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;\n" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return bits_f2(d);
+}
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;\n" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return bits_f2(d);
+}
+// exp2_det_lo of two values with packed f32 pairs: each lane's result is bit-identical to the
+// scalar function (the same round-to-nearest operations per element).
+__device__ __forceinline__ float2 exp2_det_lo2(float2 x) {
+  const float2 xc = make_float2(fmaxf(x.x, -127.0f), fmaxf(x.y, -127.0f));
+  const float2 mg = make_float2(kExp2Magic, kExp2Magic);
+  const float2 t = add2_rn(xc, mg);
+  const float2 f = sub2_rn(xc, sub2_rn(t, mg));
+  float2 p = fma2_rn(make_float2(0x1.ffcbfcp-17f, 0x1.ffcbfcp-17f), f, make_float2(0x1.430912p-13f, 0x1.430912p-13f));
+  p = fma2_rn(p, f, make_float2(0x1.5d87fep-10f, 0x1.5d87fep-10f));
+  p = fma2_rn(p, f, make_float2(0x1.3b2ab6p-7f, 0x1.3b2ab6p-7f));
+  p = fma2_rn(p, f, make_float2(0x1.c6b08ep-5f, 0x1.c6b08ep-5f));
+  p = fma2_rn(p, f, make_float2(0x1.ebfbe0p-3f, 0x1.ebfbe0p-3f));
+  p = fma2_rn(p, f, make_float2(0x1.62e430p-1f, 0x1.62e430p-1f));
+  p = fma2_rn(p, f, make_float2(1.0f, 1.0f));
+  const float2 sc = make_float2(__int_as_float((__float_as_int(t.x) + (127 - 0x4B400000)) << 23),
+                                __int_as_float((__float_as_int(t.y) + (127 - 0x4B400000)) << 23));
+  return mul2_rn(p, sc);
 }
 // Bounded wait: false when the bound ran out (the caller reports kDevWaitTimeout).
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {

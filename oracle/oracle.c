@@ -234,13 +234,14 @@ float oracle_dequant(int32_t acc, float sa, float sw) { return ((float)acc * sa)
 /* ------------------------------------------------------------------ GPU arithmetic */
 
 /* 2^x from IEEE round-to-nearest steps only, the same statements as the CUDA path's exp2_det:
- * n = rint(x), f = x - n, 2^f by the degree-7 Taylor polynomial of exp(f ln 2) (coefficients
- * (ln 2)^k / k! rounded to f32) in Horner form with fused multiply-adds, times 2^n; 0 for
- * x < -126 (and NaN), +inf for x >= 127.5. */
+ * x clamped to [-127, 127.49999]; t = x + 1.5*2^23 (n = rint(x) in t's low mantissa bits),
+ * f = x - (t - 1.5*2^23); 2^f by the degree-7 Taylor polynomial of exp(f ln 2) (coefficients
+ * (ln 2)^k / k! rounded to f32) in Horner form with fused multiply-adds; times 2^n built from
+ * the exponent bits n + 127 (0 for n = -127, so x < -126.5, -inf and NaN give 0). */
 float oracle_exp2_det(float x) {
-  const float xc = fminf(fmaxf(x, -126.0f), 127.5f);
-  const int n = (int)rintf(xc);
-  const float f = xc - (float)n;
+  const float xc = fminf(fmaxf(x, -127.0f), 127.49999f);
+  const float t = xc + 12582912.0f;
+  const float f = xc - (t - 12582912.0f);
   float p = fmaf(0x1.ffcbfcp-17f, f, 0x1.430912p-13f);
   p = fmaf(p, f, 0x1.5d87fep-10f);
   p = fmaf(p, f, 0x1.3b2ab6p-7f);
@@ -248,11 +249,12 @@ float oracle_exp2_det(float x) {
   p = fmaf(p, f, 0x1.ebfbe0p-3f);
   p = fmaf(p, f, 0x1.62e430p-1f);
   p = fmaf(p, f, 1.0f);
-  uint32_t bits = (uint32_t)(n + 127) << 23;
+  int32_t ti;
+  memcpy(&ti, &t, 4);
+  const uint32_t bits = (uint32_t)(ti + (127 - 0x4B400000)) << 23;
   float sc;
   memcpy(&sc, &bits, 4);
-  const float r = p * sc;
-  return x >= -126.0f ? (x >= 127.5f ? INFINITY : r) : 0.0f;
+  return p * sc;
 }
 
 /* Tensor-core MMA step (fp16 / bf16 inputs, f32 accumulator), as measured on B200 for both
@@ -882,7 +884,7 @@ static void attend(oracle_seq *s, int layer, int pos) {
 /* ---- attention in the CUDA path's order (GPU order).  Both kernels see q, K and V already
  * rounded to the activation type; every score and PV product is a tensor-core MMA step. */
 
-#define ATTN_SEG_PAGES 16 /* pages per segment of the decode kernel's fixed reduction order */
+#define ATTN_SEG_PAGES 32 /* pages per segment of the decode kernel's fixed reduction order */
 
 /* Online-softmax state folded the decode kernel's way: M = max(m, m'), a = 2^(m - M),
  * b = 2^(m' - M), l = fma(b, l', a*l), o = fma(b, o', a*o). */
@@ -896,7 +898,7 @@ static void fold_into(float *m, float *l, float *o, float m2, float l2, const fl
 }
 
 /* Decode kernel (attention.cuh attn_kernel) for one query row at `pos`, one q head: pages of
- * 16 positions; segments of 16 pages; inside a segment warp w (0..3) takes pages w, w+4, ...
+ * 16 positions; segments of ATTN_SEG_PAGES pages; inside a segment warp w (0..3) takes pages w, w+4, ...
  * with its own online softmax (per-page max, exp2_det, row-sum partials per token pair
  * (g, g+8) fused as fma(l, alpha, p_g + p_{g+8}) then an xor butterfly, P as hi + lo
  * activation-type terms, O += V^T P_hi then V^T P_lo); the segment state is

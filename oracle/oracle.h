@@ -104,7 +104,7 @@ void oracle_model_set_storiesane(oracle_model *m, int on);
  *   - exp as exp2_det, the SwiGLU gate h1 / (1 + e) (or storiesane's h1 * (1 / (1 + e)));
  *   - attention of positions below oracle_seq_set_prefill's count in the prefill kernel's
  *     order (64-position tiles, lazy reference max), later positions in the decode kernel's
- *     (16-page segments, 4 warps, fixed fold order). */
+ *     (32-page segments, 4 warps, fixed fold order). */
 void oracle_model_set_gpu_order(oracle_model *m, int on);
 void oracle_model_free(oracle_model *m);
 oracle_seq *oracle_seq_new(const oracle_model *m);

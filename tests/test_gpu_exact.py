@@ -72,13 +72,14 @@ def _exact(cfg, dtype, w, prompts, steps, max_pos, splits=0):
 @pytest.mark.parametrize("cfg", [TINY_MHA, TINY_GQA], ids=lambda c: c.name)
 @pytest.mark.parametrize("dtype", ["fp16", "bf16", "w8a8_fp16", "w8a8_bf16"])
 def test_tiny_decode_bit_exact(cfg, dtype):
-    """Prompts across prefill tiles (64 positions), decode continuing into a second 16-page
-    segment: logits and tokens equal the GPU-order oracle's bit for bit."""
+    """Prompts across prefill tiles (64 positions), decode continuing into a second 32-page
+    segment (512 positions): logits and tokens equal the GPU-order oracle's bit for bit."""
+    cfg = cfg.with_max_seq(640)
     w = weights(cfg)
     rng = np.random.default_rng(7)
-    lens = [1, 17, 64, 65, 130, 250]
+    lens = [1, 17, 64, 65, 130, 500]
     prompts = [rng.integers(3, cfg.vocab, L).tolist() for L in lens]
-    toks, logits = _exact(cfg, dtype, w, prompts, steps=20, max_pos=288)
+    toks, logits = _exact(cfg, dtype, w, prompts, steps=20, max_pos=544)
     m = gpu_order(cfg, w, dtype)
     worst, agree, n = oracle_check(m, prompts, toks, logits)
     print(f"{cfg.name} {dtype}: max|dlogit| vs GPU-order oracle = {worst:.3e}, top1 {agree:.4f} over {n}")
@@ -88,11 +89,11 @@ def test_tiny_decode_bit_exact(cfg, dtype):
 @pytest.mark.parametrize("dtype", ["bf16", "w8a8_bf16"])
 def test_split_count_does_not_change_results(dtype):
     """The same sequences decoded with 1, 2 and 3 CTAs per (sequence, kv head): identical."""
-    cfg = TINY_GQA
+    cfg = TINY_GQA.with_max_seq(1700)
     w = weights(cfg)
     rng = np.random.default_rng(9)
-    prompts = [rng.integers(3, cfg.vocab, L).tolist() for L in (300, 420, 5)]
-    runs = [_exact(cfg, dtype, w, prompts, steps=12, max_pos=512, splits=s) for s in (1, 2, 3)]
+    prompts = [rng.integers(3, cfg.vocab, L).tolist() for L in (1100, 1530, 5)]  # up to 4 segments
+    runs = [_exact(cfg, dtype, w, prompts, steps=12, max_pos=1600, splits=s) for s in (1, 2, 3)]
     for toks, logits in runs[1:]:
         assert toks == runs[0][0]
         for a, b in zip(logits, runs[0][1]):

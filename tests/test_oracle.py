@@ -430,8 +430,9 @@ def test_oracle_weight_generator_equals_the_library():
 
 def test_exp2_det_known_values_and_accuracy():
     assert O.exp2_det(0.0) == 1.0 and O.exp2_det(1.0) == 2.0 and O.exp2_det(-1.0) == 0.5
-    assert O.exp2_det(-126.0) == 2.0 ** -126 and O.exp2_det(-126.5) == 0.0 and O.exp2_det(float("-inf")) == 0.0
-    assert O.exp2_det(127.5) == float("inf")
+    assert O.exp2_det(-126.0) == 2.0 ** -126 and O.exp2_det(-127.0) == 0.0 and O.exp2_det(float("-inf")) == 0.0
+    assert O.exp2_det(-300.0) == 0.0 and 0.0 < O.exp2_det(-126.4) < 2.0 ** -126   # a rounded subnormal
+    assert O.exp2_det(127.5) == O.exp2_det(1e30) and abs(O.exp2_det(127.5) / 2.0 ** 127.49999 - 1) < 1e-5
     xs = np.random.default_rng(4).uniform(-100, 100, 20000).astype(np.float32)
     got = np.array([O.exp2_det(float(x)) for x in xs], np.float64)
     ref = np.exp2(xs.astype(np.float64))
