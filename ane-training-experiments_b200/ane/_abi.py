@@ -52,9 +52,11 @@ EXPORTS = [
     "llm_stories_decode_batch", "llm_ctx_stream", "llm_synchronize", "llm_step_kernel_count", "llm_step_parts",
     "llm_memory_bytes", "llm_time_attention", "llm_profile_step", "llm_trace_step", "llm_trace_begin", "llm_trace_end", "llm_debug_norm_quant", "llm_debug_gemm_i8",
     "llm_debug_gemm_f16", "llm_debug_read_kv", "llm_gemm_i8_splitk_noalloc", "llm_set_option", "llm_set_sampling", "llm_sample_uniform", "llm_debug_sample", "llm_debug_wait_timeout",
-    "llm_eval_window", "llm_debug_exp2",
+    "llm_eval_window", "llm_debug_exp2", "llm_shard_range", "llm_comm_unique_id", "llm_comm_create",
+    "llm_comm_destroy", "llm_gather_tokens", "llm_linear_create", "llm_linear_eval_cf", "llm_linear_destroy",
 ]
 
+LLM_COMM_ID_BYTES = 128
 LLM_OPT_CUDA_GRAPHS = 1
 LLM_OPT_TCGEN05_GEMM = 2
 LLM_OPT_PDL = 3
@@ -149,6 +151,15 @@ def lib() -> C.CDLL:
         "llm_debug_gemm_f16": (C.c_int, [C.c_int, C.c_int, _FP, _FP, C.c_int, C.c_int, C.c_int, C.c_int, _FP]),
         "llm_debug_read_kv": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, _FP, _FP]),
         "llm_debug_exp2": (C.c_int, [C.c_int, _FP, C.c_int, _FP]),
+        "llm_shard_range": (C.c_int, [C.c_int, C.c_int, C.c_int, i32p, i32p]),
+        "llm_comm_unique_id": (C.c_int, [C.c_char_p, C.c_size_t]),
+        "llm_comm_create": (C.c_int, [C.c_char_p, C.c_size_t, C.c_int, C.c_int, C.c_int, C.c_double,
+                                      C.POINTER(C.c_void_p)]),
+        "llm_comm_destroy": (C.c_int, [C.c_void_p]),
+        "llm_gather_tokens": (C.c_int, [C.c_void_p, i32p, C.c_int, C.c_int, C.c_int, i32p]),
+        "llm_linear_create": (C.c_int, [C.c_int, C.c_int, _FP, C.c_int, C.c_int, C.POINTER(C.c_void_p)]),
+        "llm_linear_eval_cf": (C.c_int, [C.c_void_p, _FP, C.c_int, _FP, C.POINTER(C.c_uint64)]),
+        "llm_linear_destroy": (C.c_int, [C.c_void_p]),
         "llm_set_option": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
         "llm_gemm_i8_splitk_noalloc": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                                                  C.c_void_p, C.c_void_p]),

@@ -62,3 +62,55 @@ def gather_tokens(tokens: np.ndarray, n_total: int, group=None, device: Optional
         rr = shard_range(n_total, world, r)
         out[:, rr.start:rr.stop] = part.cpu().numpy()[:, :len(rr)]
     return out
+
+
+class Comm:
+    """The library's communicator (llm_comm_create / llm_gather_tokens): NCCL inside
+    libllm_cuda.so, every wait bounded by timeout_s on the host.  This is the path a Go host
+    binds through cgo; gather_tokens above is the torch.distributed equivalent."""
+
+    def __init__(self, uid: bytes, nranks: int, rank: int, device: int = 0, timeout_s: float = 60.0):
+        import ctypes as C
+        from . import _abi
+        self._abi = _abi
+        self.nranks, self.rank = nranks, rank
+        h = C.c_void_p()
+        _abi.check(_abi.lib().llm_comm_create(uid, len(uid), nranks, rank, device, timeout_s, C.byref(h)))
+        self.h = h
+
+    @staticmethod
+    def unique_id() -> bytes:
+        import ctypes as C
+        from . import _abi
+        buf = C.create_string_buffer(_abi.LLM_COMM_ID_BYTES)
+        _abi.check(_abi.lib().llm_comm_unique_id(buf, len(buf)))
+        return buf.raw
+
+    def gather_tokens(self, tokens: np.ndarray, n_total: int) -> np.ndarray:
+        """This rank's [steps, n_local] block -> [steps, n_total] on every rank."""
+        import ctypes as C
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        if t.ndim != 2:
+            raise ValueError(f"tokens must be [steps, n_local], got shape {t.shape}")
+        out = np.empty((t.shape[0], n_total), np.int32)
+        i32p = C.POINTER(C.c_int32)
+        self._abi.check(self._abi.lib().llm_gather_tokens(self.h, t.ctypes.data_as(i32p), t.shape[0], t.shape[1],
+                                                          n_total, out.ctypes.data_as(i32p)))
+        return out
+
+    def close(self):
+        if getattr(self, "h", None):
+            self._abi.lib().llm_comm_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+
+def library_shard_range(n_total: int, world: int, rank: int) -> range:
+    """llm_shard_range through the C ABI (the same partition as shard_range)."""
+    import ctypes as C
+    from . import _abi
+    s, n = C.c_int32(), C.c_int32()
+    _abi.check(_abi.lib().llm_shard_range(n_total, world, rank, C.byref(s), C.byref(n)))
+    return range(s.value, s.value + n.value)

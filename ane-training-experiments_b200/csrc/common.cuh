@@ -130,29 +130,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // 2^x built only from IEEE round-to-nearest operations, so that a CPU restatement with the same
 // operations (C99 fmaf) gives the same bits.  x is clamped to [-127, 127.49999]; n = rint(x)
 // by the 1.5 * 2^23 addition (t = x + 1.5*2^23 holds n in its low mantissa bits); f = x - n in
-// [-0.5, 0.5]; 2^f by the degree-7 Taylor polynomial of exp(f ln 2) (coefficients (ln 2)^k / k!
-// rounded to f32; truncation error below 1e-8 on [-0.5, 0.5]) in Horner form with fused
-// multiply-adds; then one multiplication by 2^n built from its exponent bits, which are 0 for
-// n = -127, so x < -126.5 (and -inf, NaN) gives 0.  Within 1 ulp of 2^x for x in [-125, 127.4];
-// results in [2^-126.5, 2^-125) are rounded subnormals; x >= 127.5 gives 2^127.49999.  Runs on
-// the FMA and integer pipes only (no MUFU, no conversion instructions), 15 instructions.
+// [-0.5, 0.5]; 2^f by a degree-5 polynomial with constant term 1 (coefficients fitted to 2^f on
+// [-0.5, 0.5] by weighted least squares iterated toward the minimax relative error, then rounded
+// to f32; 1.6e-7 relative) in Horner form with fused multiply-adds; then one multiplication by
+// 2^n built from its exponent bits, which are 0 for n = -127, so x < -126.5 (and -inf, NaN)
+// gives 0.  Within 2.5e-7 relative of 2^x for x in [-125, 127.4]; results in [2^-126.5, 2^-125)
+// are rounded subnormals; x >= 127.5 gives 2^127.49999; exp2_det(0) = 1 exactly.  Runs on the FMA
+// and integer pipes only (no MUFU, no conversion instructions), 13 instructions.
 constexpr float kExp2Magic = 12582912.0f;  // 1.5 * 2^23
 __host__ __device__ __forceinline__ float exp2_poly(float f) {
 #ifdef __CUDA_ARCH__
-  float p = __fmaf_rn(0x1.ffcbfcp-17f, f, 0x1.430912p-13f);
-  p = __fmaf_rn(p, f, 0x1.5d87fep-10f);
-  p = __fmaf_rn(p, f, 0x1.3b2ab6p-7f);
-  p = __fmaf_rn(p, f, 0x1.c6b08ep-5f);
-  p = __fmaf_rn(p, f, 0x1.ebfbe0p-3f);
-  p = __fmaf_rn(p, f, 0x1.62e430p-1f);
+  float p = __fmaf_rn(0x1.5bb9e2p-10f, f, 0x1.3cea80p-7f);
+  p = __fmaf_rn(p, f, 0x1.c6b754p-5f);
+  p = __fmaf_rn(p, f, 0x1.ebf9bcp-3f);
+  p = __fmaf_rn(p, f, 0x1.62e42ap-1f);
   return __fmaf_rn(p, f, 1.0f);
 #else
-  float p = fmaf(0x1.ffcbfcp-17f, f, 0x1.430912p-13f);
-  p = fmaf(p, f, 0x1.5d87fep-10f);
-  p = fmaf(p, f, 0x1.3b2ab6p-7f);
-  p = fmaf(p, f, 0x1.c6b08ep-5f);
-  p = fmaf(p, f, 0x1.ebfbe0p-3f);
-  p = fmaf(p, f, 0x1.62e430p-1f);
+  float p = fmaf(0x1.5bb9e2p-10f, f, 0x1.3cea80p-7f);
+  p = fmaf(p, f, 0x1.c6b754p-5f);
+  p = fmaf(p, f, 0x1.ebf9bcp-3f);
+  p = fmaf(p, f, 0x1.62e42ap-1f);
   return fmaf(p, f, 1.0f);
 #endif
 }
@@ -216,12 +213,10 @@ __device__ __forceinline__ float2 exp2_det_lo2(float2 x) {
   const float2 mg = make_float2(kExp2Magic, kExp2Magic);
   const float2 t = add2_rn(xc, mg);
   const float2 f = sub2_rn(xc, sub2_rn(t, mg));
-  float2 p = fma2_rn(make_float2(0x1.ffcbfcp-17f, 0x1.ffcbfcp-17f), f, make_float2(0x1.430912p-13f, 0x1.430912p-13f));
-  p = fma2_rn(p, f, make_float2(0x1.5d87fep-10f, 0x1.5d87fep-10f));
-  p = fma2_rn(p, f, make_float2(0x1.3b2ab6p-7f, 0x1.3b2ab6p-7f));
-  p = fma2_rn(p, f, make_float2(0x1.c6b08ep-5f, 0x1.c6b08ep-5f));
-  p = fma2_rn(p, f, make_float2(0x1.ebfbe0p-3f, 0x1.ebfbe0p-3f));
-  p = fma2_rn(p, f, make_float2(0x1.62e430p-1f, 0x1.62e430p-1f));
+  float2 p = fma2_rn(make_float2(0x1.5bb9e2p-10f, 0x1.5bb9e2p-10f), f, make_float2(0x1.3cea80p-7f, 0x1.3cea80p-7f));
+  p = fma2_rn(p, f, make_float2(0x1.c6b754p-5f, 0x1.c6b754p-5f));
+  p = fma2_rn(p, f, make_float2(0x1.ebf9bcp-3f, 0x1.ebf9bcp-3f));
+  p = fma2_rn(p, f, make_float2(0x1.62e42ap-1f, 0x1.62e42ap-1f));
   p = fma2_rn(p, f, make_float2(1.0f, 1.0f));
   const float2 sc = make_float2(__int_as_float((__float_as_int(t.x) + (127 - 0x4B400000)) << 23),
                                 __int_as_float((__float_as_int(t.y) + (127 - 0x4B400000)) << 23));

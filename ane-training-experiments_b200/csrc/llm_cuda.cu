@@ -12,6 +12,7 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <memory>
 #include <numeric>
 #include <string>
 #include <thread>
@@ -603,6 +604,7 @@ struct llm_ctx {
   int overlap = 1;  // 0 off, 1 when the step's K/V time covers the host launches, 2 always
   int overlap_ring_kb = 64;   // tcgen05 stage ring in overlap mode: fits beside two attention CTAs
   int attn_splits = 0;        // decode attention splits per sequence (0 = chosen per batch)
+  bool null_tokens = false;   // llm_eval_window: token id -1 = a zero embedding row
   // how one micro-batch's attention launch waits for the other's: 0 = its completion,
   // 1 = all of its CTAs having started (launch-completion event)
   int attn_chain = 1;
@@ -776,9 +778,11 @@ extern "C" int llm_ctx_create(const llm_model_config* cfg, int dtype, int device
   if (!rc) rc = dalloc_t(c, &c->rope_sin, hs.size() * 4, &c->bytes_other);
   if (!rc) rc = dalloc_t(c, &c->d_err, 4, &c->bytes_other);
   if (rc) return bail(rc);
-  if (cudaMemcpy(c->rope_cos, hc.data(), hc.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
-      cudaMemcpy(c->rope_sin, hs.data(), hs.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
-      cudaMemset(c->d_err, 0, 4) != cudaSuccess)
+  // every upload is ordered on the context's (non-blocking) stream: a synchronous copy on the
+  // legacy stream may still be in flight when that stream's kernels start
+  if (cudaMemcpyAsync(c->rope_cos, hc.data(), hc.size() * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
+      cudaMemcpyAsync(c->rope_sin, hs.data(), hs.size() * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
+      cudaMemsetAsync(c->d_err, 0, 4, c->stream) != cudaSuccess || cudaStreamSynchronize(c->stream) != cudaSuccess)
     return bail(fail(LLM_ERR_CUDA, "table upload failed"));
   rc = prepare_kernels(c);
   if (rc) return bail(rc);
@@ -825,10 +829,12 @@ int upload_convert(llm_ctx* c, float* dtmp, const float* src, int rows, int cols
 int upload_f32(llm_ctx* c, float** dst, const float* src, size_t n, float fill) {
   RC(dalloc_t(c, dst, n * 4, &c->bytes_weights));
   if (src) {
-    CU(cudaMemcpy(*dst, src, n * 4, cudaMemcpyHostToDevice));
+    CU(cudaMemcpyAsync(*dst, src, n * 4, cudaMemcpyHostToDevice, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
   } else {
     std::vector<float> ones(n, fill);
-    CU(cudaMemcpy(*dst, ones.data(), n * 4, cudaMemcpyHostToDevice));
+    CU(cudaMemcpyAsync(*dst, ones.data(), n * 4, cudaMemcpyHostToDevice, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
   }
   return LLM_OK;
 }
@@ -1117,10 +1123,12 @@ extern "C" int llm_kv_alloc(llm_ctx* c, int max_seqs, int max_pos, int page_toke
   c->n_pages = max_seqs * c->max_pages_per_seq;
   const size_t page_bytes = static_cast<size_t>(k.n_kv_heads) * 2 * 16 * k.head_dim * act_bytes(c);
   RC(dalloc(c, &c->kv_pool, static_cast<size_t>(k.n_layers) * c->n_pages * page_bytes, &c->bytes_kv));
-  CU(cudaMemset(c->kv_pool, 0, static_cast<size_t>(k.n_layers) * c->n_pages * page_bytes));
+  CU(cudaMemsetAsync(c->kv_pool, 0, static_cast<size_t>(k.n_layers) * c->n_pages * page_bytes, c->stream));
   RC(dalloc_t(c, &c->d_block_table, static_cast<size_t>(max_seqs) * c->max_pages_per_seq * 4, &c->bytes_other));
   c->h_block_table.assign(static_cast<size_t>(max_seqs) * c->max_pages_per_seq, -1);
-  CU(cudaMemcpy(c->d_block_table, c->h_block_table.data(), c->h_block_table.size() * 4, cudaMemcpyHostToDevice));
+  CU(cudaMemcpyAsync(c->d_block_table, c->h_block_table.data(), c->h_block_table.size() * 4, cudaMemcpyHostToDevice,
+                     c->stream));
+  CU(cudaStreamSynchronize(c->stream));
   c->seq_npages.assign(max_seqs, 0);
   c->seq_stamp.assign(max_seqs, 0);
   c->stamp_gen = 0;
@@ -1153,13 +1161,13 @@ extern "C" int llm_kv_alloc(llm_ctx* c, int max_seqs, int max_pos, int page_toke
                    &c->d_sampled})
     RC(dalloc_t(c, p, R * 4, o));
   RC(dalloc_t(c, &c->d_draws, static_cast<size_t>(max_seqs) * 8, o));
-  CU(cudaMemset(c->d_draws, 0, static_cast<size_t>(max_seqs) * 8));
+  CU(cudaMemsetAsync(c->d_draws, 0, static_cast<size_t>(max_seqs) * 8, c->stream));
   c->ws_floats = 16u << 20;  // 64 MB split-K / split-attention workspace
   RC(dalloc_t(c, &c->ws, c->ws_floats * 4, o));
   RC(dalloc_t(c, &c->counters, kCounters * 4, o));
-  CU(cudaMemset(c->counters, 0, kCounters * 4));
+  CU(cudaMemsetAsync(c->counters, 0, kCounters * 4, c->stream));
   RC(dalloc_t(c, &c->row_counters, static_cast<size_t>(R) * 4, o));
-  CU(cudaMemset(c->row_counters, 0, static_cast<size_t>(R) * 4));
+  CU(cudaMemsetAsync(c->row_counters, 0, static_cast<size_t>(R) * 4, c->stream));
   c->h_pin_ints = static_cast<size_t>(R) * 8;
   CU(cudaMallocHost(&c->h_pin, c->h_pin_ints * 4));
   c->kv_ready = true;
@@ -1259,7 +1267,8 @@ int check_ready(llm_ctx* c) {
 
 int validate_row(llm_ctx* c, int seq, int tok, int pos) {
   if (seq < 0 || seq >= c->max_seqs) return fail(LLM_ERR_INVALID, "sequence %d out of range", seq);
-  if (tok < 0 || tok >= c->cfg.vocab) return fail(LLM_ERR_TOKEN_RANGE, "token out of range: %d", tok);
+  if ((tok < 0 || tok >= c->cfg.vocab) && !(tok == -1 && c->null_tokens))
+    return fail(LLM_ERR_TOKEN_RANGE, "token out of range: %d", tok);
   if (pos < 0 || pos >= c->max_pos) return fail(LLM_ERR_POS_RANGE, "position out of range: %d", pos);
   return LLM_OK;
 }
@@ -2041,8 +2050,18 @@ extern "C" int llm_eval_window(llm_ctx* c, int slot, const int32_t* tokens, int 
     c->silu_form = 1;
   }
   RC(llm_seq_release(c, slot));
+  // a token outside [0, vocab) gives its position a zero embedding column, as EmbedLookup
+  // (ane/stories/cpu.go:41-72) does for the storiesane forward (engine.go:818)
+  std::vector<int32_t> toks(tokens, tokens + seq);
+  for (int32_t& t : toks)
+    if (t < 0 || t >= c->cfg.vocab) t = -1;
+  struct NullScope {
+    llm_ctx* c;
+    ~NullScope() { c->null_tokens = false; }
+  } nscope{c};
+  c->null_tokens = true;
   int32_t len = seq, nt = 0;
-  int rc = prefill_impl(c, &slot, tokens, &len, nullptr, 1, &nt, nullptr, true);
+  int rc = prefill_impl(c, &slot, toks.data(), &len, nullptr, 1, &nt, nullptr, true);
   if (!rc) {
     const int V = c->cfg.vocab;
     int32_t* h = c->h_pin;
@@ -2294,7 +2313,7 @@ extern "C" int llm_set_sampling(llm_ctx* c, float temperature, uint64_t seed, in
   c->sample_temp = temperature > 0.f ? temperature : 0.f;
   c->sample_inv_t = c->sample_temp > 0.f ? static_cast<double>(1.0f / c->sample_temp) : 0.0;
   c->sample_seed = seed;
-  if (reset_draws && c->d_draws) CU(cudaMemset(c->d_draws, 0, static_cast<size_t>(c->max_seqs) * 8));
+  if (reset_draws && c->d_draws) CU(cudaMemsetAsync(c->d_draws, 0, static_cast<size_t>(c->max_seqs) * 8, c->stream));
   // the temperature and seed are kernel arguments baked into captured steps
   for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
   c->graphs.clear();
@@ -2556,8 +2575,8 @@ int trace_begin(llm_ctx* c) {
   RC(set_device(c));
   if (!c->d_trace) RC(dalloc_t(c, &c->d_trace, kTraceCap * sizeof(TraceRec), &c->bytes_other));
   std::vector<TraceRec> h(kTraceCap, TraceRec{~0ull, 0ull, 0ull, 0ull});
+  CU(cudaMemcpyAsync(c->d_trace, h.data(), kTraceCap * sizeof(TraceRec), cudaMemcpyHostToDevice, c->stream));
   CU(cudaStreamSynchronize(c->stream));
-  CU(cudaMemcpy(c->d_trace, h.data(), kTraceCap * sizeof(TraceRec), cudaMemcpyHostToDevice));
   c->trace_labels.clear();
   c->tracing = true;
   return LLM_OK;
@@ -2862,4 +2881,167 @@ extern "C" int llm_debug_gemm_f16(int device, int dtype, const float* A, const f
   CU(cudaMemcpy(ha.data(), hA.p, na * 2, cudaMemcpyDeviceToHost));
   CU(cudaMemcpy(hb.data(), hB.p, nb * 2, cudaMemcpyDeviceToHost));
   return debug_gemm(device, false, act, ha.data(), hb.data(), 2, M, N, K, splits, EPI_F32, C, splits < 0);
+}
+
+// ============================================================================ linear kernels
+// model.Compile / Kernel.WriteInputF32 / EvalWithStats / ReadOutputF32 of a 1x1 convolution
+// (ane/model/model_darwin.go:138-414, ane/forward/conv.go:11-48): y[out][t] = sum_i W[out][i] x[i][t]
+// on channel-first fp32 tensors, run as one tcgen05 GEMM with the token loop's arithmetic
+// (16-bit: inputs and weights rounded, f32 accumulate; W8A8: per-row int8 weights, per-token int8
+// inputs, int32 accumulate, (acc * s_x) * s_w).
+struct llm_linear {
+  int device = 0, act = 2, in8 = 0, out_dim = 0, in_dim = 0, bn = 16;
+  void* w = nullptr;
+  float* w_scale = nullptr;
+  CUtensorMap tw{};
+  int cap = 0;  // tokens the buffers below hold
+  float *x_cf = nullptr, *x_t = nullptr, *y = nullptr, *y_cf = nullptr, *xs = nullptr;
+  void* xa = nullptr;
+  int* err = nullptr;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+};
+
+namespace {
+void linear_free_bufs(llm_linear* k) {
+  for (void* p : {static_cast<void*>(k->x_cf), static_cast<void*>(k->x_t), static_cast<void*>(k->y),
+                  static_cast<void*>(k->y_cf), static_cast<void*>(k->xs), k->xa})
+    if (p) cudaFree(p);
+  k->x_cf = k->x_t = k->y = k->y_cf = k->xs = nullptr;
+  k->xa = nullptr;
+  k->cap = 0;
+}
+}  // namespace
+
+extern "C" int llm_linear_destroy(llm_linear* k) {
+  if (!k) return LLM_OK;
+  cudaSetDevice(k->device);
+  if (k->stream) cudaStreamSynchronize(k->stream);
+  linear_free_bufs(k);
+  if (k->w) cudaFree(k->w);
+  if (k->w_scale) cudaFree(k->w_scale);
+  if (k->err) cudaFree(k->err);
+  if (k->e0) cudaEventDestroy(k->e0);
+  if (k->e1) cudaEventDestroy(k->e1);
+  if (k->stream) cudaStreamDestroy(k->stream);
+  delete k;
+  return LLM_OK;
+}
+
+extern "C" int llm_linear_create(int device, int dtype, const float* w, int out_dim, int in_dim, llm_linear** out) {
+  if (!w || !out) return fail(LLM_ERR_INVALID, "nil argument");
+  if (dtype < LLM_DTYPE_F16 || dtype > LLM_DTYPE_W8A8_BF16) return fail(LLM_ERR_INVALID, "unknown dtype %d", dtype);
+  if (out_dim <= 0 || in_dim <= 0 || out_dim % 16 || in_dim % 128)
+    return fail(LLM_ERR_INVALID, "linear %dx%d: out_dim must be a multiple of 16 and in_dim of 128", out_dim, in_dim);
+  if (cudaSetDevice(device) != cudaSuccess) return fail(LLM_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+  std::unique_ptr<llm_linear, int (*)(llm_linear*)> k(new llm_linear(), llm_linear_destroy);
+  k->device = device;
+  k->in8 = dtype == LLM_DTYPE_W8A8_F16 || dtype == LLM_DTYPE_W8A8_BF16;
+  k->act = (dtype == LLM_DTYPE_F16 || dtype == LLM_DTYPE_W8A8_F16) ? 1 : 2;
+  k->out_dim = out_dim;
+  k->in_dim = in_dim;
+  CU(cudaStreamCreateWithFlags(&k->stream, cudaStreamNonBlocking));
+  CU(cudaEventCreate(&k->e0));
+  CU(cudaEventCreate(&k->e1));
+  CU(cudaMalloc(&k->err, 4));
+  CU(cudaMemsetAsync(k->err, 0, 4, k->stream));
+  const size_t n = static_cast<size_t>(out_dim) * in_dim;
+  CU(cudaMalloc(&k->w, n * (k->in8 ? 1 : 2)));
+  if (k->in8) CU(cudaMalloc(&k->w_scale, static_cast<size_t>(out_dim) * 4));
+  DevBuf tmp;
+  CU(cudaMalloc(&tmp.p, n * 4));
+  // on the kernel's own (non-blocking) stream: a synchronous copy from pageable memory may
+  // return before its DMA lands, and that stream does not wait for the legacy stream
+  CU(cudaMemcpyAsync(tmp.p, w, n * 4, cudaMemcpyHostToDevice, k->stream));
+  ConvertParams cp{static_cast<const float*>(tmp.p), out_dim, in_dim, 1, 0, k->w, k->w_scale};
+  const dim3 grid((out_dim + 7) / 8);
+  if (k->in8) convert_rows_kernel<int8_t><<<grid, 256, 0, k->stream>>>(cp);
+  else if (k->act == 1) convert_rows_kernel<__half><<<grid, 256, 0, k->stream>>>(cp);
+  else convert_rows_kernel<__nv_bfloat16><<<grid, 256, 0, k->stream>>>(cp);
+  CU(cudaGetLastError());
+  CU(cudaStreamSynchronize(k->stream));
+  *out = k.release();
+  return LLM_OK;
+}
+
+extern "C" int llm_linear_eval_cf(llm_linear* k, const float* x_cf, int s, float* y_cf, uint64_t* hw_ns) {
+  if (!k || !x_cf || !y_cf) return fail(LLM_ERR_INVALID, "nil argument");
+  if (s <= 0) return fail(LLM_ERR_INVALID, "sequence length %d must be positive", s);
+  CU(cudaSetDevice(k->device));
+  const int I = k->in_dim, O = k->out_dim;
+  if (s > k->cap) {
+    CU(cudaStreamSynchronize(k->stream));
+    linear_free_bufs(k);
+    const size_t si = static_cast<size_t>(s) * I, so = static_cast<size_t>(s) * O;
+    CU(cudaMalloc(&k->x_cf, si * 4));
+    CU(cudaMalloc(&k->x_t, si * 4));
+    CU(cudaMalloc(&k->xa, si * (k->in8 ? 1 : 2)));
+    CU(cudaMalloc(&k->xs, static_cast<size_t>(s) * 4));
+    CU(cudaMalloc(&k->y, so * 4));
+    CU(cudaMalloc(&k->y_cf, so * 4));
+    k->cap = s;
+  }
+  cudaDeviceProp prop{};
+  CU(cudaGetDeviceProperties(&prop, k->device));
+  const int esz = k->in8 ? 1 : 2;
+  const int bn = umma_bn_for(s, O, EPI_F32, 0, prop.multiProcessorCount);
+  CUtensorMap tx{}, tw{};
+  RC(make_kmajor_map(&tx, k->xa, esz, k->act == 2, I, s, kUmmaTokens));
+  RC(make_kmajor_map(&tw, k->w, esz, k->act == 2, I, O, bn));
+  GemmParams p{};
+  p.A = k->xa;
+  p.B = k->w;
+  p.M = s;
+  p.N = O;
+  p.K = I;
+  p.a_scale = k->xs;
+  p.b_scale = k->w_scale;
+  p.out = k->y;
+  p.ldo = O;
+  p.k_splits = 1;
+  p.k_tiles_per_split = I * esz / 128;
+  p.err = k->err;
+  CU(umma_any(k->act, k->in8, tx, tw, p, EPI_F32, bn, dim3(1), k->stream, true));
+  CU(cudaMemcpyAsync(k->x_cf, x_cf, static_cast<size_t>(s) * I * 4, cudaMemcpyHostToDevice, k->stream));
+  CU(cudaEventRecord(k->e0, k->stream));
+  // channel-first [I][s] -> token rows [s][I]
+  transpose_rows_kernel<<<dim3((s + 31) / 32, (I + 31) / 32), dim3(32, 8), 0, k->stream>>>(k->x_cf, I, s, k->x_t);
+  CU(cudaGetLastError());
+  if (k->in8) {
+    NormParams np_{};
+    np_.x = k->x_t;
+    np_.w = nullptr;  // the per-token quantiser alone
+    np_.D = I;
+    np_.rows = s;
+    np_.q = static_cast<int8_t*>(k->xa);
+    np_.scale = k->xs;
+    CU(norm_any(k->act, true, np_, k->stream));
+  } else if (k->act == 1) {
+    f32_to_act_kernel<__half><<<(static_cast<size_t>(s) * I + 255) / 256, 256, 0, k->stream>>>(
+        k->x_t, static_cast<__half*>(k->xa), static_cast<size_t>(s) * I);
+  } else {
+    f32_to_act_kernel<__nv_bfloat16><<<(static_cast<size_t>(s) * I + 255) / 256, 256, 0, k->stream>>>(
+        k->x_t, static_cast<__nv_bfloat16*>(k->xa), static_cast<size_t>(s) * I);
+  }
+  CU(cudaGetLastError());
+  const dim3 grid((s + kUmmaTokens - 1) / kUmmaTokens, (O + bn - 1) / bn, 1);
+  CU(umma_any(k->act, k->in8, tx, tw, p, EPI_F32, bn, grid, k->stream, false));
+  // token rows [s][O] -> channel-first [O][s]
+  transpose_rows_kernel<<<dim3((O + 31) / 32, (s + 31) / 32), dim3(32, 8), 0, k->stream>>>(k->y, s, O, k->y_cf);
+  CU(cudaGetLastError());
+  CU(cudaEventRecord(k->e1, k->stream));
+  CU(cudaMemcpyAsync(y_cf, k->y_cf, static_cast<size_t>(s) * O * 4, cudaMemcpyDeviceToHost, k->stream));
+  int herr = 0;
+  CU(cudaMemcpyAsync(&herr, k->err, 4, cudaMemcpyDeviceToHost, k->stream));
+  CU(cudaStreamSynchronize(k->stream));
+  if (herr) {
+    cudaMemsetAsync(k->err, 0, 4, k->stream);
+    return fail(LLM_ERR_DEVICE, "linear kernel reported device error %d", herr);
+  }
+  if (hw_ns) {
+    float ms = 0.f;
+    CU(cudaEventElapsedTime(&ms, k->e0, k->e1));
+    *hw_ns = static_cast<uint64_t>(static_cast<double>(ms) * 1e6);
+  }
+  return LLM_OK;
 }

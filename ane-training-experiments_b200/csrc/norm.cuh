@@ -61,11 +61,14 @@ __global__ void __launch_bounds__(1024) norm_rows_kernel(NormParams p) {
 
   float4 v[NV];
   if (p.embed != nullptr) {
-    const T* e = reinterpret_cast<const T*>(p.embed) + static_cast<size_t>(p.tokens[row]) * D;
+    // a negative token id (a window's out-of-range token, ane/stories/cpu.go:59-64) gathers a
+    // zero row
+    const int tok = p.tokens[row];
+    const T* e = reinterpret_cast<const T*>(p.embed) + static_cast<size_t>(tok < 0 ? 0 : tok) * D;
     float* xo = p.x_out + static_cast<size_t>(row) * D;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
-      v[j] = load4_act<T>(e + 4 * t + 4 * nt * j);
+      v[j] = tok < 0 ? make_float4(0.f, 0.f, 0.f, 0.f) : load4_act<T>(e + 4 * t + 4 * nt * j);
       *reinterpret_cast<float4*>(xo + 4 * t + 4 * nt * j) = v[j];
     }
   } else {

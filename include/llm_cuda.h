@@ -185,8 +185,9 @@ int llm_stories_decode_batch(llm_ctx *ctx, const int32_t *prompts, const int32_t
  * `slot` (released before and after): every position's logits, written channel-first as
  * logits_cf[vocab][seq] when non-NULL (the layout of storiesane.Engine.EvalLogits,
  * engine.go:363-376), and the next token after the last position in *next_token (greedy, or
- * sampled per llm_set_sampling from the slot's stream).  seq <= the KV cache's max_pos.
- * Replaces Engine.evalLogitsInto (engine.go:734-747) / evalLogitsCPUInto (:804-842); the
+ * sampled per llm_set_sampling from the slot's stream).  seq <= the KV cache's max_pos.  A
+ * token outside [0, vocab) gives its position a zero embedding column (EmbedLookup,
+ * ane/stories/cpu.go:41-72).  Replaces Engine.evalLogitsInto (engine.go:734-747) / evalLogitsCPUInto (:804-842); the
  * windowed Engine.Decode (decode.go:18-94) calls it once per generated token. */
 int llm_eval_window(llm_ctx *ctx, int slot, const int32_t *tokens, int seq, int arithmetic,
                     int32_t *next_token, float *logits_cf);
@@ -290,6 +291,46 @@ int llm_trace_step(llm_ctx *ctx, char *report, size_t report_len, double *step_u
  * CUDA graph replay), so every launch carries its record. */
 int llm_trace_begin(llm_ctx *ctx);
 int llm_trace_end(llm_ctx *ctx, char *report, size_t report_len, double *span_us);
+
+/* ---------------------------------------------------------------- linear kernels */
+/* A 1x1 convolution y = W x on channel-first fp32 tensors, the unit the reference compiles and
+ * evaluates per layer (model.Compile / Kernel.WriteInputF32 / EvalWithStats / ReadOutputF32,
+ * ane/model/model_darwin.go:138-414; forward.ConvEval, ane/forward/conv.go:11-48), run as one
+ * tcgen05 GEMM with the token loop's arithmetic: fp16 / bf16 round the weights and inputs and
+ * accumulate in f32; W8A8 quantises each weight row and each input column (token) with the
+ * bridge rule and accumulates in int32, y = (acc * s_x) * s_w. */
+typedef struct llm_linear llm_linear;
+/* Weights w [out_dim][in_dim] fp32 (row-major, the reference's layout), converted on `device`;
+ * out_dim a multiple of 16, in_dim of 128. */
+int llm_linear_create(int device, int dtype, const float *w, int out_dim, int in_dim, llm_linear **out);
+/* x_cf [in_dim][s] -> y_cf [out_dim][s] (host buffers); hw_ns (optional) receives the device
+ * time of the evaluation (EvalStats.HWExecutionNS). */
+int llm_linear_eval_cf(llm_linear *k, const float *x_cf, int s, float *y_cf, uint64_t *hw_ns);
+int llm_linear_destroy(llm_linear *k);
+
+/* ---------------------------------------------------------------- multi-GPU jobs */
+/* Sequences are independent (ane/stories/infer.go:136-245), so a multi-GPU job splits its
+ * n_total sequences across ranks (one process per GPU) in contiguous blocks and gathers the
+ * generated token ids once at the end; nothing crosses ranks while tokens are generated.
+ * No counterpart in the reference (it decodes one sequence in one process). */
+/* Rank `rank`'s block of an n_total-sequence job: [start, start + count); the first
+ * n_total % nranks ranks hold one sequence more. */
+int llm_shard_range(int n_total, int nranks, int rank, int *start, int *count);
+typedef struct llm_comm llm_comm;
+#define LLM_COMM_ID_BYTES 128
+/* A new communicator id (on one rank; the host hands the bytes to every rank).  NCCL is
+ * loaded on first use (LLM_ERR_UNSUPPORTED without it). */
+int llm_comm_unique_id(unsigned char *id, size_t id_bytes);
+/* Join communicator `id` as `rank` of `nranks` on CUDA device `device`.  Every wait of the
+ * communicator is bounded by timeout_s seconds (<= 0: 60): a rank that never joins or never
+ * takes part in a gather makes the others fail with LLM_ERR_DEVICE instead of hanging. */
+int llm_comm_create(const unsigned char *id, size_t id_bytes, int nranks, int rank, int device, double timeout_s,
+                    llm_comm **out);
+int llm_comm_destroy(llm_comm *comm);
+/* The job's one collective: every rank passes its [steps][n_local] host block of token ids
+ * (n_local = its llm_shard_range count) and receives [steps][n_total] in global sequence order
+ * (an all-gather over NVLink / NVSwitch; every rank must call it). */
+int llm_gather_tokens(llm_comm *comm, const int32_t *tokens, int steps, int n_local, int n_total, int32_t *out);
 
 /* ---------------------------------------------------------------- allocation-free entry point */
 /* No counterpart in the reference.  Split-K int8 GEMM C[M,N] = A[M,K] . B[N,K]^T with int32

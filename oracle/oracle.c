@@ -235,19 +235,18 @@ float oracle_dequant(int32_t acc, float sa, float sw) { return ((float)acc * sa)
 
 /* 2^x from IEEE round-to-nearest steps only, the same statements as the CUDA path's exp2_det:
  * x clamped to [-127, 127.49999]; t = x + 1.5*2^23 (n = rint(x) in t's low mantissa bits),
- * f = x - (t - 1.5*2^23); 2^f by the degree-7 Taylor polynomial of exp(f ln 2) (coefficients
- * (ln 2)^k / k! rounded to f32) in Horner form with fused multiply-adds; times 2^n built from
+ * f = x - (t - 1.5*2^23); 2^f by the CUDA path's degree-5 polynomial (constant term 1, the other
+ * coefficients fitted to 2^f on [-0.5, 0.5] toward minimax relative error, rounded to f32) in
+ * Horner form with fused multiply-adds; times 2^n built from
  * the exponent bits n + 127 (0 for n = -127, so x < -126.5, -inf and NaN give 0). */
 float oracle_exp2_det(float x) {
   const float xc = fminf(fmaxf(x, -127.0f), 127.49999f);
   const float t = xc + 12582912.0f;
   const float f = xc - (t - 12582912.0f);
-  float p = fmaf(0x1.ffcbfcp-17f, f, 0x1.430912p-13f);
-  p = fmaf(p, f, 0x1.5d87fep-10f);
-  p = fmaf(p, f, 0x1.3b2ab6p-7f);
-  p = fmaf(p, f, 0x1.c6b08ep-5f);
-  p = fmaf(p, f, 0x1.ebfbe0p-3f);
-  p = fmaf(p, f, 0x1.62e430p-1f);
+  float p = fmaf(0x1.5bb9e2p-10f, f, 0x1.3cea80p-7f);
+  p = fmaf(p, f, 0x1.c6b754p-5f);
+  p = fmaf(p, f, 0x1.ebf9bcp-3f);
+  p = fmaf(p, f, 0x1.62e42ap-1f);
   p = fmaf(p, f, 1.0f);
   int32_t ti;
   memcpy(&ti, &t, 4);
@@ -394,6 +393,17 @@ void oracle_gemm_mma(const float *A, const float *B, int M, int N, int K, int ac
     for (int n = 0; n < N; n++)
       Cout[(size_t)m * N + n] = mma_dot16(am + (size_t)m * K, ae + (size_t)m * K, bm + (size_t)n * K, be + (size_t)n * K, K, 2 * mb);
   free(am); free(ae); free(bm); free(be);
+}
+
+/* ane/stories/cpu.go:41-72 EmbedLookup: channel-first out[d][t] = embed[tokens[t]][d], a
+ * token outside [0, vocab) zeroes its column (vocab = the table's rows). */
+void oracle_embed_lookup_cf(float *out, const float *embed, int vocab, const int32_t *tokens, int dim, int seq) {
+  if (dim <= 0 || seq <= 0) return;
+  for (int t = 0; t < seq; t++) {
+    const int tok = tokens[t];
+    for (int d = 0; d < dim; d++)
+      out[(size_t)d * seq + t] = (tok < 0 || tok >= vocab) ? 0.0f : embed[(size_t)tok * dim + d];
+  }
 }
 
 /* ------------------------------------------------------------------ model */
@@ -1051,11 +1061,14 @@ static void attend_gpu(oracle_seq *s, int layer, int pos) {
 int oracle_forward(const oracle_model *m, oracle_seq *s, int token, int pos, float *logits_out) {
   if (!m || !s) return ORACLE_EINVAL;
   const oracle_config *c = &m->c;
-  if (token < 0 || token >= c->vocab) return ORACLE_ERANGE_TOKEN;
+  /* stories.Decoder rejects an out-of-range token (infer.go:205-207); the storiesane window
+   * forward gives it a zero embedding column (EmbedLookup, ane/stories/cpu.go:59-64) */
+  if ((token < 0 || token >= c->vocab) && !m->silu_form) return ORACLE_ERANGE_TOKEN;
   if (pos < 0 || pos >= c->max_seq) return ORACLE_ERANGE_POS;
   int D = c->dim, F = c->hidden, hd = c->head_dim;
 
-  memcpy(s->x, m->embed + (size_t)token * D, sizeof(float) * (size_t)D);
+  if (token < 0 || token >= c->vocab) memset(s->x, 0, sizeof(float) * (size_t)D);
+  else memcpy(s->x, m->embed + (size_t)token * D, sizeof(float) * (size_t)D);
   for (int l = 0; l < c->n_layers; l++) {
     const layer_t *L = &m->layers[l];
     norm_vec(m, s->xn, s->x, L->rms_att, D);

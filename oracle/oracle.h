@@ -167,6 +167,9 @@ float oracle_mma16(float c, const float *a, const float *b, int n, int act);
 /* C[m][n] = the MMA chain (oracle_mma16 over 16-term k slices in order, the first without
  * accumulator) of A[m][:] and B[n][:], K a multiple of 16: a 16-bit GEMM without split-K. */
 void oracle_gemm_mma(const float *A, const float *B, int M, int N, int K, int act, float *C);
+/* ane/stories/cpu.go:41-72 EmbedLookup (channel-first [dim][seq]; out-of-range tokens zero
+ * their column). */
+void oracle_embed_lookup_cf(float *out, const float *embed, int vocab, const int32_t *tokens, int dim, int seq);
 /* Exact int8 GEMM: C[m][n] = sum_k A[m][k]*B[n][k]. */
 void oracle_gemm_i8(const int8_t *A, const int8_t *B, int M, int N, int K, int32_t *C);
 /* Dequantise an int32 accumulator the way the CUDA epilogue does: (float)acc*sa*sw. */

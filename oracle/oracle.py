@@ -75,6 +75,7 @@ def lib() -> C.CDLL:
         "oracle_exp2_det": (C.c_float, [C.c_float]),
         "oracle_mma16": (C.c_float, [C.c_float, _FP, _FP, C.c_int, C.c_int]),
         "oracle_gemm_mma": (None, [_FP, _FP, C.c_int, C.c_int, C.c_int, C.c_int, _FP]),
+        "oracle_embed_lookup_cf": (None, [_FP, _FP, C.c_int, i32p, C.c_int, C.c_int]),
         "oracle_seq_new": (C.c_void_p, [C.c_void_p]),
         "oracle_seq_free": (None, [C.c_void_p]),
         "oracle_seq_reset": (None, [C.c_void_p]),
@@ -283,6 +284,15 @@ def gemm_mma(A, B, act: int):
     Cm = np.zeros((A.shape[0], B.shape[0]), np.float32)
     lib().oracle_gemm_mma(_p(A), _p(B), A.shape[0], B.shape[0], A.shape[1], act, _p(Cm))
     return Cm
+
+
+def embed_lookup_cf(embed, tokens, dim: int, seq: int):
+    """ane/stories/cpu.go:41-72 EmbedLookup: [dim * seq] channel-first."""
+    e = f32(embed)
+    t = np.ascontiguousarray(np.asarray(tokens, np.int32))
+    out = np.full(dim * seq, np.nan, np.float32)
+    lib().oracle_embed_lookup_cf(_p(out), _p(e), e.size // dim, _p(t, C.c_int32), dim, seq)
+    return out
 
 
 def round_f16(x: float) -> float:

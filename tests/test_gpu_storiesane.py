@@ -86,3 +86,16 @@ def test_open_from_llama2c_file(tmp_path):
     eng.Close()
     with pytest.raises(_abi.LLMError, match="storiesane open: load model"):
         Open(Options(ModelPath=str(tmp_path / "missing.bin"), Seq=16, Config=TINY))
+
+
+def test_out_of_range_window_token_is_a_zero_embedding_column():
+    """EmbedLookup (ane/stories/cpu.go:41-72): a window token outside [0, vocab) contributes a
+    zero embedding column instead of an error; bit-identical to the GPU-order oracle."""
+    cfg = TINY_MHA
+    w = weights(cfg)
+    seq = 16
+    eng = Open(Options(Weights=w, Seq=seq, DType="bf16"))
+    window = [1, 5, 40000, 7] + [9] * (seq - 4)
+    got = eng.EvalLogits(window).reshape(cfg.vocab, seq)
+    eng.Close()
+    np.testing.assert_array_equal(got, gpu_order(cfg, w, "bf16", storiesane=True).eval_window(window))

@@ -108,3 +108,11 @@ def test_rank_leaving_before_gather_fails_survivor_within_timeout():
     status, payload = res.get(0, (None, None))
     assert status == "error", res
     assert time.time() - t0 < 60
+
+
+def test_library_shard_range_equals_python_partition():
+    from ane.shard import library_shard_range
+    for n_total in (0, 1, 7, 2048, 2049):
+        for world in (1, 2, 3, 8):
+            for r in range(world):
+                assert library_shard_range(n_total, world, r) == shard_range(n_total, world, r)
