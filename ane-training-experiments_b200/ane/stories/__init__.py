@@ -350,6 +350,7 @@ class Engine:
     def __init__(self, cfg: ModelConfig, dtype: str = "bf16", device: int = 0):
         self.cfg = cfg
         self.dtype = dtype
+        self.device = device
         h = C.c_void_p()
         _abi.check(_abi.lib().llm_ctx_create(C.byref(cfg.c_struct()), _abi.DTYPES[dtype], device, C.byref(h)))
         self.h = h

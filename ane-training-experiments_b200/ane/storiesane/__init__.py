@@ -42,6 +42,27 @@ class Options:
     Device: int = 0
 
 
+@dataclass
+class Diagnostics:
+    """ane/storiesane/diagnostics.go:4-20: best-effort runtime state of an Engine."""
+
+    UseANE: bool = False
+    LayerForwardRequested: bool = False
+    LayerForwardEnabled: bool = False
+    CompiledLayers: int = 0
+    LayerInitError: str = ""
+    FinalHeadOffloadEnabled: bool = False
+    HybridBackwardRequested: bool = False
+    HybridBackwardEnabled: bool = False
+    BackwardInitError: str = ""
+    HasRMSForward: bool = False
+    HasClassifierForward: bool = False
+    HasSoftmax: bool = False
+    HasClassifierBackward: bool = False
+    HasRMSBackward: bool = False
+    OffloadDiagnostics: str = ""
+
+
 def fillDecodeWindow(dst: List[int], tokens: List[int]) -> None:
     """decode.go:83-94: BOS everywhere, then the last len(dst) tokens right-aligned."""
     for i in range(len(dst)):
@@ -57,11 +78,26 @@ class Engine:
     """storiesane.Engine's evaluation API on one CUDA context (one sequence slot, a KV cache
     of one window)."""
 
-    def __init__(self, cuda: _CudaEngine, seq: int, seed: int):
+    def __init__(self, cuda: _CudaEngine, seq: int, seed: int, use_ane: bool = False):
         self._e = cuda
         self.seq = seq
         self.seed = seed
         self.vocab = cuda.cfg.vocab
+        self.use_ane = use_ane
+
+    def Diagnostics(self) -> Diagnostics:
+        """diagnostics.go:23-54.  On CUDA every layer's forward and the final head (RMSNorm,
+        classifier, softmax / sampling) run on the device once the engine is open; there is no
+        training path, so the backward fields stay false."""
+        if self._e is None:
+            return Diagnostics()
+        cfg = self._e.cfg
+        return Diagnostics(
+            UseANE=self.use_ane, LayerForwardRequested=self.use_ane, LayerForwardEnabled=True,
+            CompiledLayers=cfg.n_layers, FinalHeadOffloadEnabled=True, HasRMSForward=True,
+            HasClassifierForward=True, HasSoftmax=True,
+            OffloadDiagnostics=f"cuda device {self._e.device}: {cfg.name} {self._e.dtype}, "
+                               f"{cfg.n_layers} layers, window {self.seq}")
 
     def EvalLogits(self, tokens) -> np.ndarray:
         """engine.go:363-376: tokens of length seq -> logits [Vocab * seq], channel-first
@@ -147,4 +183,4 @@ def Open(opts: Options) -> Engine:
     except Exception:
         eng.close()
         raise
-    return Engine(eng, seq, seed)
+    return Engine(eng, seq, seed, opts.UseANE)

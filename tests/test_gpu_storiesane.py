@@ -99,3 +99,13 @@ def test_out_of_range_window_token_is_a_zero_embedding_column():
     got = eng.EvalLogits(window).reshape(cfg.vocab, seq)
     eng.Close()
     np.testing.assert_array_equal(got, gpu_order(cfg, w, "bf16", storiesane=True).eval_window(window))
+
+
+def test_diagnostics_report_the_device_forward():
+    cfg = TINY_MHA
+    eng = Open(Options(Weights=weights(cfg), Seq=8, DType="fp16", UseANE=True))
+    d = eng.Diagnostics()
+    assert d.UseANE and d.LayerForwardRequested and d.LayerForwardEnabled
+    assert d.CompiledLayers == cfg.n_layers and d.HasClassifierForward and not d.HybridBackwardEnabled
+    eng.Close()
+    assert eng.Diagnostics().CompiledLayers == 0
