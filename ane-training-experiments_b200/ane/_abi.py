@@ -53,7 +53,7 @@ EXPORTS = [
     "llm_memory_bytes", "llm_time_attention", "llm_profile_step", "llm_trace_step", "llm_trace_begin", "llm_trace_end", "llm_debug_norm_quant", "llm_debug_gemm_i8",
     "llm_debug_gemm_f16", "llm_debug_read_kv", "llm_gemm_i8_splitk_noalloc", "llm_set_option", "llm_set_sampling", "llm_sample_uniform", "llm_debug_sample", "llm_debug_wait_timeout",
     "llm_eval_window", "llm_debug_exp2", "llm_shard_range", "llm_comm_unique_id", "llm_comm_create",
-    "llm_comm_destroy", "llm_gather_tokens", "llm_linear_create", "llm_linear_eval_cf", "llm_linear_destroy",
+    "llm_comm_destroy", "llm_gather_tokens", "llm_comm_last_gather_ms", "llm_linear_create", "llm_linear_eval_cf", "llm_linear_destroy",
 ]
 
 LLM_COMM_ID_BYTES = 128
@@ -157,6 +157,7 @@ def lib() -> C.CDLL:
                                       C.POINTER(C.c_void_p)]),
         "llm_comm_destroy": (C.c_int, [C.c_void_p]),
         "llm_gather_tokens": (C.c_int, [C.c_void_p, i32p, C.c_int, C.c_int, C.c_int, i32p]),
+        "llm_comm_last_gather_ms": (C.c_int, [C.c_void_p, C.POINTER(C.c_double)]),
         "llm_linear_create": (C.c_int, [C.c_int, C.c_int, _FP, C.c_int, C.c_int, C.POINTER(C.c_void_p)]),
         "llm_linear_eval_cf": (C.c_int, [C.c_void_p, _FP, C.c_int, _FP, C.POINTER(C.c_uint64)]),
         "llm_linear_destroy": (C.c_int, [C.c_void_p]),

@@ -98,6 +98,13 @@ class Comm:
                                                           n_total, out.ctypes.data_as(i32p)))
         return out
 
+    def last_gather_ms(self) -> float:
+        """Device time of the last gather (llm_comm_last_gather_ms)."""
+        import ctypes as C
+        v = C.c_double()
+        self._abi.check(self._abi.lib().llm_comm_last_gather_ms(self.h, C.byref(v)))
+        return v.value
+
     def close(self):
         if getattr(self, "h", None):
             self._abi.lib().llm_comm_destroy(self.h)

@@ -83,6 +83,8 @@ struct llm_comm {
   cudaStream_t stream = nullptr;
   int32_t *d_send = nullptr, *d_recv = nullptr;
   size_t cap = 0;  // int32 elements of d_send
+  cudaEvent_t e0 = nullptr, e1 = nullptr;  // around the last gather's copy-in and all-gather
+  bool timed = false;
 };
 
 namespace {
@@ -107,19 +109,24 @@ int wait_comm(llm_comm* c, const char* what) {
   }
 }
 
-// Wait for the collective on c->stream, polling the stream and the communicator; bounded.
+// Wait for the collective on c->stream; bounded.  A non-blocking communicator may still be
+// enqueueing the collective when the call returns (ncclInProgress): the stream is only polled
+// once the communicator reports the enqueue done, else an idle stream would look finished.
 int wait_stream(llm_comm* c, const char* what) {
   const auto t0 = Clock::now();
   for (;;) {
-    const cudaError_t e = cudaStreamQuery(c->stream);
-    if (e == cudaSuccess) return LLM_OK;
-    if (e != cudaErrorNotReady) return fail_fmt(LLM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
     ncclResult_t st = ncclSuccess;
-    g_nccl.async_error(c->comm, &st);
-    if (st != ncclSuccess && st != ncclInProgress) {
+    const ncclResult_t r = g_nccl.async_error(c->comm, &st);
+    if (r != ncclSuccess || (st != ncclSuccess && st != ncclInProgress)) {
+      const ncclResult_t bad = r != ncclSuccess ? r : st;
       g_nccl.abort(c->comm);
       c->comm = nullptr;
-      return fail_fmt(LLM_ERR_DEVICE, "%s: %s", what, g_nccl.error_string(st));
+      return fail_fmt(LLM_ERR_DEVICE, "%s: %s", what, g_nccl.error_string(bad));
+    }
+    if (st == ncclSuccess) {
+      const cudaError_t e = cudaStreamQuery(c->stream);
+      if (e == cudaSuccess) return LLM_OK;
+      if (e != cudaErrorNotReady) return fail_fmt(LLM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
     }
     if (std::chrono::duration<double>(Clock::now() - t0).count() > c->timeout_s) {
       g_nccl.abort(c->comm);  // ends the collective's kernels; the communicator is unusable
@@ -165,7 +172,9 @@ extern "C" int llm_comm_create(const unsigned char* id, size_t id_bytes, int nra
   c->rank = rank;
   c->device = device;
   c->timeout_s = timeout_s > 0 ? timeout_s : 60.0;
-  if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+  if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreate(&c->e0) != cudaSuccess || cudaEventCreate(&c->e1) != cudaSuccess) {
+    if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
     return fail_fmt(LLM_ERR_CUDA, "stream creation failed");
   }
@@ -196,8 +205,19 @@ extern "C" int llm_comm_destroy(llm_comm* c) {
   if (c->comm) g_nccl.destroy(c->comm);
   if (c->d_send) cudaFree(c->d_send);
   if (c->d_recv) cudaFree(c->d_recv);
+  if (c->e0) cudaEventDestroy(c->e0);
+  if (c->e1) cudaEventDestroy(c->e1);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
+  return LLM_OK;
+}
+
+extern "C" int llm_comm_last_gather_ms(llm_comm* c, double* ms) {
+  if (!c || !ms) return fail_fmt(LLM_ERR_INVALID, "nil argument");
+  if (!c->timed) return fail_fmt(LLM_ERR_STATE, "no gather has completed");
+  float v = 0.f;
+  if (cudaEventElapsedTime(&v, c->e0, c->e1) != cudaSuccess) return fail_fmt(LLM_ERR_CUDA, "event timing failed");
+  *ms = v;
   return LLM_OK;
 }
 
@@ -229,12 +249,17 @@ extern "C" int llm_gather_tokens(llm_comm* c, const int32_t* tokens, int steps, 
   // this rank's block padded to the largest shard with -1
   std::vector<int32_t> send(per, -1);
   for (int s = 0; s < steps; ++s) memcpy(send.data() + static_cast<size_t>(s) * width, tokens + static_cast<size_t>(s) * n_local, n_local * 4);
+  c->timed = false;
+  cudaEventRecord(c->e0, c->stream);
   if (cudaMemcpyAsync(c->d_send, send.data(), per * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
     return fail_fmt(LLM_ERR_CUDA, "copy of the token block failed");
   const ncclResult_t r = g_nccl.all_gather(c->d_send, c->d_recv, per, ncclInt32, c->comm, c->stream);
   if (r != ncclSuccess && r != ncclInProgress) return fail_fmt(LLM_ERR_DEVICE, "ncclAllGather: %s", g_nccl.error_string(r));
   rc = wait_stream(c, "token gather");
   if (rc) return rc;
+  cudaEventRecord(c->e1, c->stream);
+  cudaEventSynchronize(c->e1);
+  c->timed = true;
   std::vector<int32_t> recv(per * c->nranks);
   if (cudaMemcpy(recv.data(), c->d_recv, per * 4 * c->nranks, cudaMemcpyDeviceToHost) != cudaSuccess)
     return fail_fmt(LLM_ERR_CUDA, "copy of the gathered tokens failed");

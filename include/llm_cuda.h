@@ -331,6 +331,9 @@ int llm_comm_destroy(llm_comm *comm);
  * (n_local = its llm_shard_range count) and receives [steps][n_total] in global sequence order
  * (an all-gather over NVLink / NVSwitch; every rank must call it). */
 int llm_gather_tokens(llm_comm *comm, const int32_t *tokens, int steps, int n_local, int n_total, int32_t *out);
+/* Device time (CUDA events on the communicator's stream) of the last completed gather: the
+ * copy of the block to the device and the all-gather. */
+int llm_comm_last_gather_ms(llm_comm *comm, double *ms);
 
 /* ---------------------------------------------------------------- allocation-free entry point */
 /* No counterpart in the reference.  Split-K int8 GEMM C[M,N] = A[M,K] . B[N,K]^T with int32
