@@ -309,8 +309,22 @@ cudaError_t attn_any(int act, int hd, const AttnParams& p, cudaStream_t s, bool 
 template <typename T, bool Q>
 cudaError_t norm_launch(const NormParams& p, cudaStream_t s) {
   (void)cudaGetLastError();
+  const int G = norm_groups_per_thread(p.D), W = norm_threads(p.D) / 32;
+  const dim3 wgrid((p.rows + kNormWarpRows - 1) / kNormWarpRows), wblock(kNormWarpRows * 32);
+  // One warp per row for prefill-sized RMSNorms (measured: 4096 rows x 1024, 14.4 -> 8.2 us); the
+  // CTA-per-row kernel for decode-sized launches and the quantise-only rows, where its shorter
+  // per-thread float64 chains measured faster (Stories W8A8 decode step 0.99 vs 1.07 ms, SwiGLU
+  // output 3072 wide: 16.7 vs 28 us).
+  if (p.w != nullptr && p.rows >= 1024) {
+#define LLM_NORM_WARP(g, w) \
+  if (G == g && W == w) return launch_pdl(norm_rows_warp_kernel<T, Q, g, w>, wgrid, wblock, 0, s, p);
+  LLM_NORM_WARP(1, 1) LLM_NORM_WARP(1, 2) LLM_NORM_WARP(1, 3)
+  LLM_NORM_WARP(2, 2) LLM_NORM_WARP(2, 3) LLM_NORM_WARP(2, 4) LLM_NORM_WARP(2, 6) LLM_NORM_WARP(2, 8)
+  LLM_NORM_WARP(2, 12)
+#undef LLM_NORM_WARP
+  }
   const dim3 block(norm_threads(p.D));
-  if (norm_groups_per_thread(p.D) == 2) return launch_pdl(norm_rows_kernel<T, Q, 2>, dim3(p.rows), block, 0, s, p);
+  if (G == 2) return launch_pdl(norm_rows_kernel<T, Q, 2>, dim3(p.rows), block, 0, s, p);
   return launch_pdl(norm_rows_kernel<T, Q, 1>, dim3(p.rows), block, 0, s, p);
 }
 

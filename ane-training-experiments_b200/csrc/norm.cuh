@@ -151,6 +151,114 @@ __global__ void __launch_bounds__(1024) norm_rows_kernel(NormParams p) {
   trace_end(p.trace);
 }
 
+// The same row computation with one warp per row and no block-wide barriers (the decode-sized
+// launches are latency-bound: the CTA-per-row kernel spends most of its time in dependent
+// loads and __syncthreads).  Lane l plays the virtual threads t = l + 32 v (v < W) of the
+// CTA-per-row layout above, so every float64 partial, the butterfly of each virtual warp and
+// the in-order sum of the virtual warps' totals are the same operations in the same order:
+// bit-identical results.  kNormWarpRows rows per CTA.
+constexpr int kNormWarpRows = 4;
+
+template <typename T, bool QUANT, int G, int W>
+__global__ void __launch_bounds__(kNormWarpRows * 32) norm_rows_warp_kernel(NormParams p) {
+  griddep_launch_dependents();
+  trace_start(p.trace);
+  griddep_wait();
+  constexpr int TT = 32 * W;  // virtual threads per row
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kNormWarpRows + (threadIdx.x >> 5);
+  const int D = p.D;
+  if (row < p.rows) {
+    float4 v[W][G];
+    if (p.embed != nullptr) {
+      const int tok = p.tokens[row];  // negative: a zero row (ane/stories/cpu.go:59-64)
+      const T* e = reinterpret_cast<const T*>(p.embed) + static_cast<size_t>(tok < 0 ? 0 : tok) * D;
+      float* xo = p.x_out + static_cast<size_t>(row) * D;
+#pragma unroll
+      for (int vw = 0; vw < W; ++vw)
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+          const int i = 4 * (32 * vw + lane) + 4 * TT * j;
+          v[vw][j] = tok < 0 ? make_float4(0.f, 0.f, 0.f, 0.f) : load4_act<T>(e + i);
+          *reinterpret_cast<float4*>(xo + i) = v[vw][j];
+        }
+    } else {
+      const int src = p.row_index ? p.row_index[row] : row;
+      const float* xr = p.x + static_cast<size_t>(src) * D;
+#pragma unroll
+      for (int vw = 0; vw < W; ++vw)
+#pragma unroll
+        for (int j = 0; j < G; ++j) v[vw][j] = *reinterpret_cast<const float4*>(xr + 4 * (32 * vw + lane) + 4 * TT * j);
+    }
+    if (p.w != nullptr) {
+      double tot = 0.0;
+#pragma unroll
+      for (int vw = 0; vw < W; ++vw) {
+        double acc = 0.0;
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+          acc = __dadd_rn(acc, __dmul_rn((double)v[vw][j].x, (double)v[vw][j].x));
+          acc = __dadd_rn(acc, __dmul_rn((double)v[vw][j].y, (double)v[vw][j].y));
+          acc = __dadd_rn(acc, __dmul_rn((double)v[vw][j].z, (double)v[vw][j].z));
+          acc = __dadd_rn(acc, __dmul_rn((double)v[vw][j].w, (double)v[vw][j].w));
+        }
+        acc = warp_sum_f64(acc);
+        tot = vw == 0 ? acc : __dadd_rn(tot, acc);
+      }
+      const double mean = __dadd_rn(__ddiv_rn(tot, (double)D), p.eps);
+      const float rrms = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(mean)));
+#pragma unroll
+      for (int vw = 0; vw < W; ++vw)
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+          const float4 w = *reinterpret_cast<const float4*>(p.w + 4 * (32 * vw + lane) + 4 * TT * j);
+          v[vw][j].x = __fmul_rn(__fmul_rn(v[vw][j].x, rrms), w.x);
+          v[vw][j].y = __fmul_rn(__fmul_rn(v[vw][j].y, rrms), w.y);
+          v[vw][j].z = __fmul_rn(__fmul_rn(v[vw][j].z, rrms), w.z);
+          v[vw][j].w = __fmul_rn(__fmul_rn(v[vw][j].w, rrms), w.w);
+        }
+    }
+    if constexpr (!QUANT) {
+      T* o = reinterpret_cast<T*>(p.out) + static_cast<size_t>(row) * D;
+#pragma unroll
+      for (int vw = 0; vw < W; ++vw)
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+          uint2 packed;
+          packed.x = ActTraits<T>::pack2(v[vw][j].x, v[vw][j].y);
+          packed.y = ActTraits<T>::pack2(v[vw][j].z, v[vw][j].w);
+          *reinterpret_cast<uint2*>(o + 4 * (32 * vw + lane) + 4 * TT * j) = packed;
+        }
+    } else {
+      float mx = 0.0f;
+#pragma unroll
+      for (int vw = 0; vw < W; ++vw)
+#pragma unroll
+        for (int j = 0; j < G; ++j)
+          mx = fmaxf(fmaxf(fmaxf(mx, fabsf(v[vw][j].x)), fmaxf(fabsf(v[vw][j].y), fabsf(v[vw][j].z))),
+                     fabsf(v[vw][j].w));
+      mx = warp_max(mx);
+      float sc = __fdiv_rn(mx, 127.0f);
+      if (sc == 0.0f) sc = 1.0f;
+      const float inv = __fdiv_rn(1.0f, sc);
+      if (lane == 0) p.scale[row] = sc;
+      int8_t* qo = p.q + static_cast<size_t>(row) * D;
+#pragma unroll
+      for (int vw = 0; vw < W; ++vw)
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+          char4 c;
+          c.x = quant_bridge_fast(v[vw][j].x, sc, inv);
+          c.y = quant_bridge_fast(v[vw][j].y, sc, inv);
+          c.z = quant_bridge_fast(v[vw][j].z, sc, inv);
+          c.w = quant_bridge_fast(v[vw][j].w, sc, inv);
+          *reinterpret_cast<char4*>(qo + 4 * (32 * vw + lane) + 4 * TT * j) = c;
+        }
+    }
+  }
+  trace_end(p.trace);
+}
+
 // Weight conversion: fp32 rows -> act type (rounded) or int8 with per-row scales.
 // dst_row(r) maps source row r to its destination row (used to interleave W1/W3).
 struct ConvertParams {

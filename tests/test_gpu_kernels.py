@@ -25,9 +25,10 @@ def dev_norm_quant(x, w, eps):
 
 
 @pytest.mark.parametrize("cols", [128, 768, 1024, 2048, 3072])
-def test_norm_quant_bit_exact(cols):
+@pytest.mark.parametrize("rows", [37, 1100])  # 1100: the warp-per-row kernel of prefill-sized RMSNorms
+def test_norm_quant_bit_exact(cols, rows):
     rng = np.random.default_rng(cols)
-    x = (rng.standard_normal((37, cols)) * rng.uniform(1e-3, 30, (37, 1))).astype(np.float32)
+    x = (rng.standard_normal((rows, cols)) * rng.uniform(1e-3, 30, (rows, 1))).astype(np.float32)
     x[3] = 0.0  # all-zero row: scale falls back to 1
     w = (1 + 0.3 * rng.standard_normal(cols)).astype(np.float32)
     for eps in (1e-5, 1e-6):
