@@ -60,6 +60,12 @@ struct AttnParams {
   int8_t* q8;                 // [rows][n_heads * HD]
   float* q8_scale;            // [rows]
   int* row_counters;          // [rows]
+  // Nonzero when nothing the preceding kernels of this launch chain write can change the
+  // block tables, positions, sequence ids or the K/V pages before each block's first query
+  // position (decode steps whose inputs were complete before the step began): those pages are
+  // then requested before the programmatic wait for the preceding kernel (the QKV projection),
+  // which writes only q and the K/V at the query positions.
+  int early_kv;
   int* err;
   TraceRec* trace;            // llm_trace_step
 };
@@ -102,7 +108,7 @@ struct AttnCfg {
   static constexpr int SLOT_FLOATS = 32 * (4 + 4 * KS);
   static constexpr int FOLD_BYTES = 2 * SLOT_FLOATS * 4;  // two slots for the segment fold
   static constexpr int SMEM = kAttnWarps * WARP_BYTES + FOLD_BYTES;
-  static_assert(FOLD_BYTES >= 8 * HD * 4, "output staging must fit in the fold area");
+  static_assert(FOLD_BYTES >= (8 * HD + 8) * 4, "output staging must fit in the fold area");
 };
 
 // Online-softmax state of one warp in mma fragment order: lane (g, t) holds columns c0 = 2t and
@@ -253,7 +259,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, attn_min_blocks<HD>()) attn_k
 
   griddep_launch_dependents();
   trace_start(p.trace);
-  griddep_wait();
+  if (!p.early_kv) griddep_wait();
   const int blk = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -278,19 +284,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32, attn_min_blocks<HD>()) attn_k
   const int seg0 = split * per, seg1 = min(n_seg, seg0 + per);
   const int p_begin = seg0 * kAttnSegPages, p_end = min(n_pg, seg1 * kAttnSegPages);
 
-  // Q^T fragments: column g of the B operand is (query g/group, head g%group).
-  uint32_t qb[KS][2];
-  {
-    const int qi = g / group, h = g % group;
-    const bool ok = qi < nq;
-    const T* qrow = reinterpret_cast<const T*>(p.q) +
-                    (static_cast<size_t>(r0 + (ok ? qi : 0)) * p.n_heads + kvh * group + h) * HD;
-#pragma unroll
-    for (int ks = 0; ks < KS; ++ks) {
-      qb[ks][0] = ok ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 2 * t) : 0u;
-      qb[ks][1] = ok ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 8 + 2 * t) : 0u;
-    }
-  }
   // causal limits of this lane's two score columns (2t, 2t+1); invalid columns mask all
   const int c0 = 2 * t, c1 = 2 * t + 1;
   const int lim0 = (c0 / group) < nq ? pos0 + c0 / group : -1;
@@ -320,14 +313,41 @@ __global__ void __launch_bounds__(kAttnWarps * 32, attn_min_blocks<HD>()) attn_k
     fence_mbar_init();
   }
   __syncwarp();
+  // The ring's first pages: with early_kv those wholly before the first query position go out
+  // before the wait for the preceding kernel, the rest after it.
+  const int stable_end = p.early_kv ? min(p_end, pos0 >> 4) : 0;
   if (lane == 0) {
 #pragma unroll
     for (int s = 0; s < STAGES; ++s) {
       const int lp = p_begin + warp + kAttnWarps * s;
-      if (lp < p_end) {
+      if (lp < stable_end) {
         mbar_arrive_expect_tx(bar0 + 8 * s, PB);
         bulk_g2s(wbase + s * PB, page_src(lp), PB, bar0 + 8 * s);
       }
+    }
+  }
+  if (p.early_kv) griddep_wait();
+  if (lane == 0) {
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s) {
+      const int lp = p_begin + warp + kAttnWarps * s;
+      if (lp >= stable_end && lp < p_end) {
+        mbar_arrive_expect_tx(bar0 + 8 * s, PB);
+        bulk_g2s(wbase + s * PB, page_src(lp), PB, bar0 + 8 * s);
+      }
+    }
+  }
+  // Q^T fragments: column g of the B operand is (query g/group, head g%group).
+  uint32_t qb[KS][2];
+  {
+    const int qi = g / group, h = g % group;
+    const bool ok = qi < nq;
+    const T* qrow = reinterpret_cast<const T*>(p.q) +
+                    (static_cast<size_t>(r0 + (ok ? qi : 0)) * p.n_heads + kvh * group + h) * HD;
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      qb[ks][0] = ok ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 2 * t) : 0u;
+      qb[ks][1] = ok ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 8 + 2 * t) : 0u;
     }
   }
 
@@ -488,25 +508,33 @@ __global__ void __launch_bounds__(kAttnWarps * 32, attn_min_blocks<HD>()) attn_k
 
   const int ncols = min(8, nq * group);
   if (!multi) {
-    // out = o / l, staged through the fold area so the rows are stored coalesced
+    // out = o / l: o and l staged through the fold area, then every thread divides and stores
+    // its own elements (only the block's ncols valid columns), coalesced along the rows
     float* stage = fold_area;
+    float* stage_l = fold_area + 8 * HD;
     if (warp == 0) {
 #pragma unroll
       for (int mt = 0; mt < KS; ++mt) {
         const int d = mt * 16 + g;
-        stage[c0 * HD + d] = run.l0 > 0.f ? __fdiv_rn(run.o[mt][0], run.l0) : 0.f;
-        stage[c1 * HD + d] = run.l1 > 0.f ? __fdiv_rn(run.o[mt][1], run.l1) : 0.f;
-        stage[c0 * HD + d + 8] = run.l0 > 0.f ? __fdiv_rn(run.o[mt][2], run.l0) : 0.f;
-        stage[c1 * HD + d + 8] = run.l1 > 0.f ? __fdiv_rn(run.o[mt][3], run.l1) : 0.f;
+        stage[c0 * HD + d] = run.o[mt][0];
+        stage[c1 * HD + d] = run.o[mt][1];
+        stage[c0 * HD + d + 8] = run.o[mt][2];
+        stage[c1 * HD + d + 8] = run.o[mt][3];
+      }
+      if (g == 0) {  // every lane of a column holds the same row sum
+        stage_l[c0] = run.l0;
+        stage_l[c1] = run.l1;
       }
     }
     __syncthreads();
     for (int i = threadIdx.x; i < ncols * HD; i += kAttnWarps * 32) {
       const int c = i / HD, d = i % HD;
+      const float l = stage_l[c];
+      const float v = l > 0.f ? __fdiv_rn(stage[i], l) : 0.f;
       const int row = r0 + c / group, head = kvh * group + c % group;
       const size_t oi = (static_cast<size_t>(row) * p.n_heads + head) * HD + d;
-      if (p.out_f32) reinterpret_cast<float*>(p.out)[oi] = stage[i];
-      else reinterpret_cast<T*>(p.out)[oi] = ActTraits<T>::from_f(stage[i]);
+      if (p.out_f32) reinterpret_cast<float*>(p.out)[oi] = v;
+      else reinterpret_cast<T*>(p.out)[oi] = ActTraits<T>::from_f(v);
     }
     attn_quant_rows<HD>(p, r0, nq, group, s_rowlast, s_wmax);
     trace_end(p.trace);

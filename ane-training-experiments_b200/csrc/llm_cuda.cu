@@ -1323,6 +1323,9 @@ struct RowsSpec {
   int gen_cap = 0;
   bool sample = false;  // draw the next token with sample_kernel (temperature sampling)
   bool prefill_tiles = false;  // blocks are query tiles of attn_prefill_kernel (<= 128/group rows)
+  // the step's inputs (tables, positions, K/V of earlier positions) were complete before its
+  // first launch: decode attention may request those pages before its programmatic wait
+  bool early_kv = false;
 };
 
 const CUtensorMap* tmap(llm_ctx* c, const void* ptr, int esz, int k, int rows, int box) {
@@ -1596,6 +1599,7 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
     ap.layer = l;
     ap.n_pages = c->n_pages;
     ap.splits = rs.attn_splits;
+    ap.early_kv = rs.early_kv ? 1 : 0;
     ap.ws_segs = attn_ws_segs(c);
     ap.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(k.head_dim)));
     ap.out = bytes(c->attn, static_cast<size_t>(P.r0) * Q * (i8 ? 4 : ab));
@@ -1821,8 +1825,15 @@ int run_step(llm_ctx* c, int n, int splits, int mode) {
   }
   // overlapped micro-batch steps launch eagerly unless LLM_OPT_OVERLAP_GRAPHS: their
   // cross-stream schedule measured faster from eager launches than from a replayed graph
-  if (!c->use_graphs || c->tracing || (overlap_applies(c, n, true) && !c->overlap_graphs))
+  if (!c->use_graphs || c->tracing || (overlap_applies(c, n, true) && !c->overlap_graphs)) {
+    // A host-driven step's inputs arrive by stream-ordered copies before its first launch.  An
+    // eager device-resident step (mode 2) may start its first launches while the previous
+    // step's last kernel (which advances the positions) still runs, so it keeps the wait first.
+    rs.early_kv = mode != 2 && !c->tracing;
     return enqueue_forward(c, rs);
+  }
+  // successive graph launches are stream-ordered as a whole
+  rs.early_kv = true;
   GraphKey key{n, splits, mode | (rs.sample ? 8 : 0)};
   auto it = c->graphs.find(key);
   if (it == c->graphs.end()) {

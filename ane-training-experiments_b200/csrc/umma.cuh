@@ -145,9 +145,13 @@ constexpr int kUmmaThreads = 192;
 constexpr int kUmmaTokens = 128;  // token rows per tile (UMMA M)
 
 // Stage ring of ~192 KB: one CTA per SM, all stages in flight.
+#ifndef LLM_UMMA_MAX_STAGES
+#define LLM_UMMA_MAX_STAGES 11
+#endif
 template <int BN>
 constexpr int umma_stages() {
-  return (192 * 1024) / ((kUmmaTokens + BN) * 128) > 11 ? 11 : (192 * 1024) / ((kUmmaTokens + BN) * 128);
+  return (192 * 1024) / ((kUmmaTokens + BN) * 128) > LLM_UMMA_MAX_STAGES ? LLM_UMMA_MAX_STAGES
+                                                                          : (192 * 1024) / ((kUmmaTokens + BN) * 128);
 }
 template <int BN>
 constexpr int umma_smem_bytes() {

@@ -278,10 +278,18 @@ def test_prefill_query_tiles_long_prompts(cfg, dtype):
         print(f"{cfg.name} {dtype} tiles={tiles} tc={tc}: vs reference order max|dlogit|={worst:.3e} top1={agree:.4f}")
         assert worst <= REF_ORDER_TOL[dtype] and agree >= REF_ORDER_TOP1[dtype], (tiles, tc, worst, agree)
         assert np.abs(lg[0] - logits[-1][0]).max() <= REF_ORDER_TOL[dtype]
-        results[(tiles, tc)] = logits
+        results[(tiles, tc)] = (toks, logits)
+    # The three prefill kernels differ in summation order, so a near-tie may pick another greedy
+    # token; rows are compared while both runs have fed the same tokens (the prompt's logits
+    # always).
+    t0, l0 = results[(0, 0)]
     for key in ((1, 1), (1, 0)):
-        for a, b in zip(results[(0, 0)], results[key]):
-            assert np.abs(a - b).max() <= REF_ORDER_TOL[dtype], key
+        tk, lk = results[key]
+        for i in range(len(prompts)):
+            same = 1
+            while same < len(l0[i]) and np.array_equal(t0[i][:same], tk[i][:same]):
+                same += 1
+            assert np.abs(l0[i][:same] - lk[i][:same]).max() <= REF_ORDER_TOL[dtype], key
 
 
 @pytest.mark.parametrize("cfg,dtype", [(TINY_GQA, "bf16"), (TINY_GQA, "w8a8_bf16"), (TINY_MHA, "fp16"),
