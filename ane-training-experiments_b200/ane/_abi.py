@@ -72,6 +72,7 @@ LLM_OPT_PREFILL_RING_KB = 13
 LLM_OPT_PREFILL_BN = 14
 LLM_OPT_PREFILL_TC = 15
 LLM_OPT_PREFILL_PERSIST = 16
+LLM_OPT_DECODE_SPLITK = 17
 
 
 class LLMError(RuntimeError):

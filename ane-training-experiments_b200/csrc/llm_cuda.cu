@@ -192,6 +192,8 @@ thread_local int t_prio = 0;
 // When set, the next launch records this event once all its CTAs have begun execution
 // (launch completion); the overlapped schedule chains the micro-batches' attention launches on it.
 thread_local cudaEvent_t t_lc_event = nullptr;
+// When > 1, the next launch groups its CTAs in clusters of this many along grid z.
+thread_local int t_cluster_z = 1;
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
   cudaLaunchConfig_t cfg{};
@@ -199,8 +201,15 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[3];
+  cudaLaunchAttribute attr[4];
   int na = 0;
+  if (t_cluster_z > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = static_cast<unsigned>(t_cluster_z);
+    ++na;
+  }
   if (t_lc_event != nullptr) {
     attr[na].id = cudaLaunchAttributeLaunchCompletionEvent;
     attr[na].val.launchCompletionEvent.event = t_lc_event;
@@ -469,15 +478,15 @@ cudaError_t umma_any(int act, bool in8, const CUtensorMap& tx, const CUtensorMap
 // Channel-tile width of a tcgen05 projection: QKV one head, argmax 256; otherwise the
 // narrowest tile that still keeps the grid within one CTA per SM (decode: the most SMs
 // streaming weights), or 256 when even that grid is larger (prefill).
-int umma_bn_for(int M, int N, int epi, int head_dim, int n_sm) {
+int umma_bn_for(int M, int N, int epi, int head_dim, int n_sm, int max_bn = 256) {
   if (epi == EPI_QKV) return head_dim;
   if (epi == EPI_ARGMAX) return 256;
   const long long tm = (M + kUmmaTokens - 1) / kUmmaTokens;
   for (int bn : {16, 32, 64, 128, 256}) {
-    if (!umma_bn_supported(epi, bn)) continue;
-    if (tm * ((N + bn - 1) / bn) <= n_sm) return bn;
+    if (!umma_bn_supported(epi, bn) || bn > max_bn) continue;
+    if (tm * ((N + bn - 1) / bn) <= n_sm || bn == max_bn) return bn;
   }
-  return 256;
+  return max_bn;
 }
 
 // The greedy-argmax partials: one key per (row, lm_head channel tile).
@@ -618,6 +627,7 @@ struct llm_ctx {
   int overlap = 1;  // 0 off, 1 when the step's K/V time covers the host launches, 2 always
   int overlap_ring_kb = 64;   // tcgen05 stage ring in overlap mode: fits beside two attention CTAs
   int attn_splits = 0;        // decode attention splits per sequence (0 = chosen per batch)
+  bool decode_splitk = true;  // LLM_OPT_DECODE_SPLITK
   bool null_tokens = false;   // llm_eval_window: token id -1 = a zero embedding row
   // how one micro-batch's attention launch waits for the other's: 0 = its completion,
   // 1 = all of its CTAs having started (launch-completion event)
@@ -1337,6 +1347,8 @@ const CUtensorMap* tmap(llm_ctx* c, const void* ptr, int esz, int k, int rows, i
   return &c->tmaps.emplace(key, m).first->second;
 }
 
+// CTAs of one wave of split-K clusters of 4 or 8 (decode_splits).
+constexpr int kSplitPlanSMs = 128;
 // Rows from which a projection runs on the persistent kernel (prefill chunks).
 constexpr int kPersistMinRows = 1024;
 
@@ -1360,25 +1372,43 @@ int gemm(llm_ctx* c, bool in8, int epi, GemmParams p, cudaStream_t stream = null
       CU(umma_persist_any(c->act, in8, *tx, *tw, p, epi, pbn, dim3(std::min(tiles, c->n_sm)), stream, false));
       return LLM_OK;
     }
-    int bn = umma_bn_for(p.M, p.N, epi, c->cfg.head_dim, c->n_sm);
+    // split-K over a cluster of k_splits CTAs (decode rows): the narrowest channel tile whose
+    // grid, times the splits, still fits one CTA per SM
+    const int ksplit = p.k_splits > 1 && (epi == EPI_QKV || epi == EPI_RESID || epi == EPI_SWIGLU) ? p.k_splits : 1;
+    // (two splits: tiles up to 128 channels, so the partial and summed tiles fit the ring)
+    // (one wave: clusters of two pack 144 of the 148 SMs, larger ones 128)
+    const int wave = ksplit == 1 ? c->n_sm : std::min(c->n_sm, ksplit == 2 ? 144 : kSplitPlanSMs);
+    int bn = umma_bn_for(p.M, p.N, epi, c->cfg.head_dim, std::max(1, wave / ksplit), ksplit == 2 ? 128 : 256);
     // Prefill-sized GEMMs (more tiles than SMs): a smaller stage ring lets two CTAs share an SM,
     // so one CTA's epilogue overlaps the other's mainloop; 128-wide channel tiles keep the
     // staged (coalesced) epilogue within that ring.
     const long long tm = (p.M + kUmmaTokens - 1) / kUmmaTokens;
-    if (c->prefill_ring_kb > 0 && tm * ((p.N + 255) / 256) > c->n_sm) {
+    if (ksplit == 1 && c->prefill_ring_kb > 0 && tm * ((p.N + 255) / 256) > c->n_sm) {
       if (c->prefill_bn > 0 && umma_bn_supported(epi, c->prefill_bn) && epi != EPI_QKV && epi != EPI_ARGMAX)
         bn = c->prefill_bn;
       if (ring_kb <= 0) ring_kb = c->prefill_ring_kb;
     }
     if (ring_kb > 0) p.stages = std::max(2, (ring_kb * 1024 - 1024) / ((kUmmaTokens + bn) * 128));
+    if (ksplit > 1) {
+      // a ring of this CTA's K slices (less shared memory: two CTAs may share an SM), large
+      // enough for the partial and summed tiles written to it once idle
+      const int stage = (kUmmaTokens + bn) * 128;
+      const int need = ((kUmmaTokens + kUmmaTokens / ksplit) * (bn + 4) * 4 + stage - 1) / stage;
+      const int slices = (p.K * esz / 128 + ksplit - 1) / ksplit;
+      const int want = std::max(need, p.stages > 0 ? std::min(p.stages, slices) : slices);
+      p.stages = std::max(2, want);
+    }
     const CUtensorMap* tx = tmap(c, p.A, esz, p.K, p.M, kUmmaTokens);
     const CUtensorMap* tw = tmap(c, p.B, esz, p.K, p.N, bn);
     if (!tw || !tx) return LLM_ERR_CUDA;
-    p.k_splits = 1;
-    p.k_tiles_per_split = p.K * esz / 128;
+    p.k_splits = ksplit;
+    p.k_tiles_per_split = p.K * esz / 128 / ksplit;
     p.err = c->d_err;
-    dim3 grid((p.M + kUmmaTokens - 1) / kUmmaTokens, (p.N + bn - 1) / bn, 1);
-    CU(umma_any(c->act, in8, *tx, *tw, p, epi, bn, grid, stream, false));
+    dim3 grid((p.M + kUmmaTokens - 1) / kUmmaTokens, (p.N + bn - 1) / bn, ksplit);
+    t_cluster_z = ksplit;
+    const cudaError_t e = umma_any(c->act, in8, *tx, *tw, p, epi, bn, grid, stream, false);
+    t_cluster_z = 1;
+    CU(e);
     return LLM_OK;
   }
   GemmPlan pl = plan_gemm(p.M, p.N, p.K, esz, c->n_sm, 0, c->ws_floats);
@@ -1419,6 +1449,32 @@ int overlap_parts(const llm_ctx* c, int R, bool decode_rows) {
   return 1;
 }
 bool overlap_applies(const llm_ctx* c, int R, bool decode_rows) { return overlap_parts(c, R, decode_rows) > 1; }
+// Split-K of a decode step's residual projections (Wo, W2) over a cluster
+// (LLM_OPT_DECODE_SPLITK).  A decode-sized CTA loads the whole activation tile (128 rows x K)
+// for its few output channels, and one SM streams only ~50 GB/s into shared memory, so these
+// long-K, narrow-N projections take their per-CTA bytes / 50 GB/s; splitting K divides them.
+// Fixed per model and projection (never by the batch or the device), so a row's arithmetic
+// does not depend on either: the power of two <= min(LLM_SPLITK_MAX, K slices / 2) and
+// <= 128 / (channel tiles at the widest tile) (128: the CTAs of one wave of 4- or 8-CTA
+// clusters at one CTA per SM on B200's graphics processing clusters).  Restated by the oracle
+// (oracle_decode_splits).  Measured (Qwen3 bf16, 128 rows): step 3.63 -> 3.23 ms with at most
+// four CTAs per cluster (3.46 ms with eight: larger clusters wait longer for whole groups of
+// free SMs); QKV and W1/W3 (short K, wide N) measured no faster, and the int8 projections
+// (half the bytes) slower, so they stay whole.
+#ifndef LLM_SPLITK_MAX
+#define LLM_SPLITK_MAX 4
+#endif
+int decode_splits(const llm_ctx* c, int epi, int N, int K, bool overlapped) {
+  (void)overlapped;
+  if (!c->use_umma || !c->decode_splitk || c->in8 || epi != EPI_RESID) return 1;
+  const int nkt = K * (c->in8 ? 1 : 2) / 128;
+  const int bnmax = epi == EPI_QKV ? c->cfg.head_dim : 256;
+  const int tiles = (N + bnmax - 1) / bnmax;
+  const int lim = std::min({LLM_SPLITK_MAX, nkt / 2, kSplitPlanSMs / std::max(1, tiles)});
+  int sk = 1;
+  while (sk * 2 <= lim) sk *= 2;
+  return sk;
+}
 // Temperature sampling replaces the greedy argmax (sampleFromLogits, infer.go:347-349).
 bool sampling_on(const llm_ctx* c) { return c->sample_temp > 1e-6f; }
 // Launch timeline records one traced step may use.
@@ -1544,6 +1600,7 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
     p.trace = tr("qkv", l, P);
     t_prio = prio;
     t_use_pdl = chain_pdl;
+    p.k_splits = decode_rows ? decode_splits(c, EPI_QKV, p.N, p.K, overlap) : 1;
     return gemm(c, i8, EPI_QKV, p, P.s, ring_kb);
   };
 
@@ -1643,6 +1700,7 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
       p.trace = tr("wo", l, P);
       t_prio = prio;
       t_use_pdl = chain_pdl;
+      p.k_splits = decode_rows ? decode_splits(c, EPI_RESID, p.N, p.K, overlap) : 1;
       RC(gemm(c, i8, EPI_RESID, p, P.s, ring_kb));
       RC(mark("wo_gemm+resid"));
     }
@@ -1663,6 +1721,7 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
       p.trace = tr("w13", l, P);
       t_prio = prio;
       t_use_pdl = chain_pdl;
+      p.k_splits = decode_rows ? decode_splits(c, EPI_SWIGLU, p.N, p.K, overlap) : 1;
       RC(gemm(c, i8, EPI_SWIGLU, p, P.s, ring_kb));
       RC(mark("w13_gemm+swiglu"));
     }
@@ -1696,6 +1755,7 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
       p.trace = tr("w2", l, P);
       t_prio = prio;
       t_use_pdl = chain_pdl;
+      p.k_splits = decode_rows ? decode_splits(c, EPI_RESID, p.N, p.K, overlap) : 1;
       RC(gemm(c, i8, EPI_RESID, p, P.s, ring_kb));
       RC(mark("w2_gemm+resid"));
     }
@@ -2367,6 +2427,7 @@ extern "C" int llm_set_option(llm_ctx* c, int option, int value) {
     case LLM_OPT_PREFILL_TILES: flag = &c->prefill_tiles; break;
     case LLM_OPT_PREFILL_TC: flag = &c->prefill_tc; break;
     case LLM_OPT_PREFILL_PERSIST: flag = &c->prefill_persist; break;
+    case LLM_OPT_DECODE_SPLITK: flag = &c->decode_splitk; break;
     case LLM_OPT_ATTN_CHAIN:
       if (value < 0 || value > 1) return fail(LLM_ERR_INVALID, "attention chain mode %d out of range [0, 1]", value);
       if (c->attn_chain != value) {
@@ -2767,8 +2828,15 @@ int debug_gemm(int device, bool in8, int act, const void* hA, const void* hB, si
   p.out = dC.p;
   p.ldo = N;
   if (umma_path) {
-    // splits: -1 = the model's channel tile, -bn = that tile width
-    const int bn = splits <= -2 ? -splits : umma_bn_for(M, N, epi, 0, prop.multiProcessorCount);
+    // splits: -1 = the model's channel tile, -bn = that tile width, -(1000 + S) = split-K over
+    // clusters of S = 2, 4 or 8 CTAs (the decode projections' form)
+    const int ks = splits <= -1000 ? -splits - 1000 : 1;
+    if (ks != 1 && ks != 2 && ks != 4 && ks != 8) return fail(LLM_ERR_INVALID, "split-K %d not in {2, 4, 8}", ks);
+    if (ks > 1 && (N % 4 || (K * static_cast<int>(esz) / 128) < ks))
+      return fail(LLM_ERR_INVALID, "split-K %d needs channels in fours and a K slice per split", ks);
+    const int bn = splits <= -2 && splits > -1000 ? -splits
+                                                  : umma_bn_for(M, N, epi, 0, std::max(1, prop.multiProcessorCount / ks),
+                                                                ks == 2 ? 128 : 256);
     if (!umma_bn_supported(epi, bn)) return fail(LLM_ERR_INVALID, "unsupported tcgen05 channel tile %d", bn);
     CUtensorMap tw{}, tx{};
     RC(make_kmajor_map(&tx, dA.p, static_cast<int>(esz), act == 2, K, M, kUmmaTokens));
@@ -2776,12 +2844,15 @@ int debug_gemm(int device, bool in8, int act, const void* hA, const void* hB, si
     DevBuf derr;
     CU(cudaMalloc(&derr.p, 4));
     CU(cudaMemset(derr.p, 0, 4));
-    p.k_splits = 1;
-    p.k_tiles_per_split = K * static_cast<int>(esz) / 128;
+    p.k_splits = ks;
+    p.k_tiles_per_split = K * static_cast<int>(esz) / 128 / ks;
     p.err = static_cast<int*>(derr.p);
-    dim3 grid((M + kUmmaTokens - 1) / kUmmaTokens, (N + bn - 1) / bn, 1);
+    dim3 grid((M + kUmmaTokens - 1) / kUmmaTokens, (N + bn - 1) / bn, ks);
     CU(umma_any(act, in8, tx, tw, p, epi, bn, grid, 0, true));
-    CU(umma_any(act, in8, tx, tw, p, epi, bn, grid, 0, false));
+    t_cluster_z = ks;
+    const cudaError_t le = umma_any(act, in8, tx, tw, p, epi, bn, grid, 0, false);
+    t_cluster_z = 1;
+    CU(le);
     CU(cudaDeviceSynchronize());
     int herr = 0;
     CU(cudaMemcpy(&herr, derr.p, 4, cudaMemcpyDeviceToHost));
@@ -2874,8 +2945,9 @@ extern "C" int llm_debug_exp2(int device, const float* x, int n, float* out) {
 
 extern "C" int llm_debug_gemm_i8(int device, const int8_t* A, const int8_t* B, int M, int N, int K, int splits, int32_t* C) {
   if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0 || K % 128) return fail(LLM_ERR_INVALID, "bad arguments (K %% 128 == 0)");
-  // splits < 0 selects the tcgen05 kernel (-1: the model's channel tile, -bn: tile width bn),
-  // otherwise the warp-level kernel with that split (0: its automatic plan)
+  // splits < 0 selects the tcgen05 kernel (-1: the model's channel tile, -bn: tile width bn,
+  // -(1000 + S): split-K over clusters of S CTAs), otherwise the warp-level kernel with that
+  // split (0: its automatic plan)
   return debug_gemm(device, true, 2, A, B, 1, M, N, K, splits, EPI_S32, C, splits < 0);
 }
 

@@ -114,6 +114,25 @@ __device__ __forceinline__ uint64_t sw128_desc_mn(uint32_t saddr, uint32_t lbo, 
   return d;
 }
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;\n" ::: "memory"); }
+// Cluster-wide barrier (every thread of every CTA of the cluster), release / acquire ordering
+// of shared-memory writes before it and distributed shared-memory reads after it.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire;\n" ::: "memory");
+}
+// Address of the same shared-memory location in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t dsmem_addr(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ uint4 ld_dsmem_u4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];\n"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
 __device__ __forceinline__ void prefetch_l2(const void* ptr) { asm volatile("prefetch.global.L2 [%0];\n" ::"l"(ptr)); }
 
 // Shared-memory matrix descriptor for a K-major operand tile whose rows are 128 bytes,
@@ -174,6 +193,47 @@ __device__ __forceinline__ uint32_t float_key_fast(float f) {
   return u ^ (static_cast<uint32_t>(static_cast<int>(u) >> 31) | 0x80000000u);
 }
 
+// Split-K reduction of one cluster CTA's rows: rows row0 .. row0+rp-1 of the tile, summed over
+// the S partial tiles (pitch PP floats at part_s in every CTA of the cluster) in rank order
+// (int32 exactly, fp32 rounded to nearest at each addition), written to this CTA's red_s
+// (same pitch, rp rows).  Each of the 128 epilogue threads keeps 16 distributed-shared-memory
+// loads in flight.
+template <int S, bool I8, int PP>
+__device__ __forceinline__ void splitk_reduce(uint32_t part_s, uint32_t red_s, int row0, int rp, int c4, int et) {
+  constexpr int G = 16 / S;  // items per batch
+  const int total = rp * c4;
+  for (int base = et; base < total; base += 128 * G) {
+    uint4 v[G][S];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const int idx = base + g * 128;
+      if (idx < total) {
+        const uint32_t off = part_s + ((row0 + idx / c4) * PP + 4 * (idx % c4)) * 4;
+#pragma unroll
+        for (int z = 0; z < S; ++z) v[g][z] = ld_dsmem_u4(dsmem_addr(off, static_cast<uint32_t>(z)));
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const int idx = base + g * 128;
+      if (idx >= total) continue;
+      uint32_t r[4] = {v[g][0].x, v[g][0].y, v[g][0].z, v[g][0].w};
+#pragma unroll
+      for (int z = 1; z < S; ++z) {
+        const uint32_t w[4] = {v[g][z].x, v[g][z].y, v[g][z].z, v[g][z].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if constexpr (I8) r[j] = static_cast<uint32_t>(static_cast<int>(r[j]) + static_cast<int>(w[j]));
+          else r[j] = __float_as_uint(__fadd_rn(__uint_as_float(r[j]), __uint_as_float(w[j])));
+        }
+      }
+      asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};\n" ::"r"(red_s + ((idx / c4) * PP + 4 * (idx % c4)) * 4),
+                   "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3])
+                   : "memory");
+    }
+  }
+}
+
 template <typename InT, typename OutT, int BN, int EPI>
 __global__ void __launch_bounds__(kUmmaThreads, 2)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, GemmParams p) {
@@ -197,7 +257,13 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tok0 = blockIdx.x * kUmmaTokens, ch0 = blockIdx.y * BN;
-  const int nkt = p.K * ESZ / 128;
+  // Split-K (k_splits > 1): the CTAs blockIdx.z = 0 .. k_splits-1 of one cluster take
+  // contiguous ranges of the 128-byte K slices and exchange their partial tiles through
+  // distributed shared memory (splitk_epilogue below).
+  const int n_split = p.k_splits > 1 ? p.k_splits : 1;
+  const int nkt_all = p.K * ESZ / 128;
+  const int kt0 = static_cast<int>(blockIdx.z) * nkt_all / n_split;
+  const int nkt = (static_cast<int>(blockIdx.z) + 1) * nkt_all / n_split - kt0;  // this CTA's slices
 
   griddep_launch_dependents();
   trace_start(p.trace);
@@ -230,11 +296,11 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
       for (int i = 0; i < pre; ++i) {
         const uint32_t st = sbase + i * STAGE_BYTES;
         mbar_arrive_expect_tx(smem_u32(&full_bar[i]), STAGE_BYTES);
-        tma_load_2d(st + A_BYTES, &tmW, i * (128 / ESZ), ch0, smem_u32(&full_bar[i]));
+        tma_load_2d(st + A_BYTES, &tmW, (kt0 + i) * (128 / ESZ), ch0, smem_u32(&full_bar[i]));
       }
       griddep_wait();
       for (int i = 0; i < pre; ++i)
-        tma_load_2d(sbase + i * STAGE_BYTES, &tmX, i * (128 / ESZ), tok0, smem_u32(&full_bar[i]));
+        tma_load_2d(sbase + i * STAGE_BYTES, &tmX, (kt0 + i) * (128 / ESZ), tok0, smem_u32(&full_bar[i]));
       for (int i = pre; i < nkt; ++i) {
         const int s = i % STAGES;
         const uint32_t par = ((i / STAGES) & 1) ^ 1;
@@ -243,12 +309,14 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
           break;
         }
         const uint32_t st = sbase + s * STAGE_BYTES;
-        const int kx = i * (128 / ESZ);  // element coordinate of the K slice
+        const int kx = (kt0 + i) * (128 / ESZ);  // element coordinate of the K slice
         mbar_arrive_expect_tx(smem_u32(&full_bar[s]), STAGE_BYTES);
         tma_load_2d(st + A_BYTES, &tmW, kx, ch0, smem_u32(&full_bar[s]));
         tma_load_2d(st, &tmX, kx, tok0, smem_u32(&full_bar[s]));
       }
     }
+    __syncwarp();
+    if (n_split > 1) cluster_sync_all();  // partial tiles written (splitk epilogue)
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
@@ -269,13 +337,20 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
       }
       tc_commit(smem_u32(&accum_bar));
     }
+    __syncwarp();
+    if (n_split > 1) cluster_sync_all();
   } else {
     // ---------------------------------------------------------------- epilogue (warps 2..5)
     const int q = warp & 3;              // TMEM lane quadrant
     const int et = threadIdx.x - 64;     // 0..127 among epilogue threads
-    const int tl = q * 32 + lane;        // token within the tile (= TMEM lane)
+    // Split-K: cluster CTA z finishes rows z*RP .. z*RP+RP-1 of the tile (RP = 128 / k_splits)
+    // from every CTA's partial; the per-row epilogue (QKV) runs on threads et < RP.
+    const bool split = n_split > 1;
+    const int RP = kUmmaTokens / n_split;
+    const bool row_owner = !split || et < RP;
+    const int tl = split ? static_cast<int>(blockIdx.z) * RP + et % RP : q * 32 + lane;  // token within the tile
     const int tok = tok0 + tl;
-    const bool tok_ok = tok < p.M;
+    const bool tok_ok = tok < p.M && row_owner;
     const int tokc = tok_ok ? tok : p.M - 1;
     const uint32_t trow = tmem + (static_cast<uint32_t>(q * 32) << 16);
     griddep_wait();  // positions, scales and the residual come from earlier kernels
@@ -323,11 +398,62 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
     tc_fence_after();
     epi_bar();  // s_bsc / s_nw visible to all epilogue threads
 
+    // Split-K partial tiles: each CTA's accumulator rows, TMEM lane = token, are written to its
+    // idle stage ring (pitch PP floats); after the cluster barrier a row's chunk is the sum of the
+    // CTAs' partials in rank order (int32 exactly, fp32 rounded to nearest at each addition).
+    constexpr int PP = BN + 4;
+    const uint32_t part_s = sbase;
+    const uint32_t red_s = sbase + kUmmaTokens * PP * 4;  // this CTA's summed rows (split-K)
+    if (split) {
+      if (STAGES * STAGE_BYTES < (kUmmaTokens + RP) * PP * 4) {  // the host sizes the ring for this
+        if (p.err) atomicExch(p.err, kDevWaitTimeout);
+        ok = false;
+      }
+      const int tr = q * 32 + lane;  // this thread's TMEM lane
+      for (int c = 0; c < NCH && ok; ++c) {
+        uint32_t r[32];
+        tmem_ld32(trow + c * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+          if (c * 32 + j < BN)
+            asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};\n" ::"r"(part_s + (tr * PP + c * 32 + j) * 4),
+                         "r"(r[j]), "r"(r[j + 1]), "r"(r[j + 2]), "r"(r[j + 3])
+                         : "memory");
+      }
+      cluster_sync_all();
+      const int row0 = static_cast<int>(blockIdx.z) * RP;
+      if (ok) {
+        if (n_split == 2) splitk_reduce<2, I8, PP>(part_s, red_s, row0, RP, BN / 4, et);
+        else if (n_split == 4) splitk_reduce<4, I8, PP>(part_s, red_s, row0, RP, BN / 4, et);
+        else splitk_reduce<8, I8, PP>(part_s, red_s, row0, RP, BN / 4, et);
+      }
+      epi_bar();  // the summed rows are visible to every epilogue thread
+    }
+    // the summed partials of columns col..col+3 of tile row `row` of this CTA (split-K only)
+    auto split_sum4 = [&](int row, int col, uint32_t (&r)[4]) {
+      uint4 v;
+      asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];\n"
+                   : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                   : "r"(red_s + ((row - static_cast<int>(blockIdx.z) * RP) * PP + col) * 4)
+                   : "memory");
+      r[0] = v.x; r[1] = v.y; r[2] = v.z; r[3] = v.w;
+    };
+
     // dequantised chunk c (columns 32c..32c+31 of this token's row)
     auto load_chunk = [&](int c, float (&v)[32]) {
       uint32_t r[32];
-      tmem_ld32(trow + c * 32, r);
-      tmem_wait_ld();
+      if (split) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          uint32_t r4[4] = {0u, 0u, 0u, 0u};
+          if (c * 32 + j < BN && row_owner) split_sum4(tl, c * 32 + j, r4);
+          r[j] = r4[0]; r[j + 1] = r4[1]; r[j + 2] = r4[2]; r[j + 3] = r4[3];
+        }
+      } else {
+        tmem_ld32(trow + c * 32, r);
+        tmem_wait_ld();
+      }
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         if constexpr (I8) v[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), a_s), s_bsc[(c * 32 + j) % BN]);
@@ -349,7 +475,54 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
       *reinterpret_cast<float4*>(stg + tl * SP + col) = make_float4(a, b, c_, d);
     };
 
-    if (staged && (EPI == EPI_RESID || EPI == EPI_F32 || EPI == EPI_S32)) {
+    if (split && (EPI == EPI_RESID || EPI == EPI_SWIGLU || EPI == EPI_F32 || EPI == EPI_S32)) {
+      // Split-K residual / SwiGLU / plain outputs: elementwise over this CTA's RP rows, four
+      // consecutive channels per item (consecutive threads on consecutive channels: coalesced).
+      if constexpr (EPI == EPI_RESID || EPI == EPI_SWIGLU || EPI == EPI_F32 || EPI == EPI_S32) {
+        constexpr int C4 = BN / 4;
+        const int F = p.N / 2;
+        for (int idx = et; idx < RP * C4; idx += 128) {
+          const int row = static_cast<int>(blockIdx.z) * RP + idx / C4, col = 4 * (idx % C4);
+          const int t = tok0 + row, ch = ch0 + col;
+          if (t >= p.M || ch >= p.N) continue;
+          uint32_t r[4];
+          split_sum4(row, col, r);
+          if constexpr (EPI == EPI_S32) {  // the int32 accumulators
+            *reinterpret_cast<uint4*>(reinterpret_cast<int*>(p.out) + static_cast<size_t>(t) * p.ldo + ch) =
+                ok ? make_uint4(r[0], r[1], r[2], r[3]) : make_uint4(0u, 0u, 0u, 0u);
+            continue;
+          }
+          float v[4];
+          const float as = I8 ? p.a_scale[t] : 1.0f;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if constexpr (I8) v[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), as), s_bsc[col + j]);
+            else v[j] = __uint_as_float(r[j]);
+            if (!ok) v[j] = 0.f;
+          }
+          if constexpr (EPI == EPI_F32) {
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + static_cast<size_t>(t) * p.ldo + ch) =
+                make_float4(v[0], v[1], v[2], v[3]);
+          } else if constexpr (EPI == EPI_RESID) {
+            float* dst = reinterpret_cast<float*>(p.out) + static_cast<size_t>(t) * p.ldo + ch;
+            const float4 rv = *reinterpret_cast<const float4*>(p.resid + static_cast<size_t>(t) * p.ldo + ch);
+            *reinterpret_cast<float4*>(dst) =
+                make_float4(resid_add(v[0], rv.x, p.resid_scale), resid_add(v[1], rv.y, p.resid_scale),
+                            resid_add(v[2], rv.z, p.resid_scale), resid_add(v[3], rv.w, p.resid_scale));
+          } else {
+            // interleaved rows: channel 2i is W1 row i (gate), 2i+1 is W3 row i (up)
+            const float g0 = swiglu_pair(v[0], v[1], p.silu_form), g1 = swiglu_pair(v[2], v[3], p.silu_form);
+            const int j0 = ch / 2;
+            if (p.swiglu_f32) {
+              *reinterpret_cast<float2*>(reinterpret_cast<float*>(p.out) + static_cast<size_t>(t) * F + j0) = make_float2(g0, g1);
+            } else {
+              *reinterpret_cast<uint32_t*>(reinterpret_cast<OutT*>(p.out) + static_cast<size_t>(t) * F + j0) =
+                  ActTraits<OutT>::pack2(g0, g1);
+            }
+          }
+        }
+      }
+    } else if (staged && (EPI == EPI_RESID || EPI == EPI_F32 || EPI == EPI_S32)) {
       for (int c = 0; c < NCH; ++c) {
         float v[32];
         if constexpr (EPI == EPI_S32) {
@@ -621,6 +794,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
     }
   }
   if (failed && p.err) atomicExch(p.err, kDevWaitTimeout);
+  // split-K: no CTA leaves while another may still read its partial tile
+  if (n_split > 1) cluster_sync_all();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

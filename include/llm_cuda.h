@@ -244,6 +244,11 @@ int llm_debug_sample(int device, const float *logits, int rows, int vocab, float
                                    0 = the mma.sync tile kernel (default 1)                   */
 #define LLM_OPT_PREFILL_PERSIST 16  /* projections of >= 1024-row chunks on the persistent tcgen05
                                        kernel (double-buffered TMEM accumulators; default 1) */
+#define LLM_OPT_DECODE_SPLITK 17 /* decode steps' projections split K over a cluster of CTAs whose
+                                    partial tiles are summed in rank order through distributed
+                                    shared memory (default 1; the split per projection is fixed
+                                    by its shape, so results do not depend on the batch; fp16 /
+                                    bf16 rounding differs from 0, int8 results do not) */
 #define LLM_OPT_ATTN_CHAIN 7   /* overlap mode: a micro-batch's attention launch starts once every CTA of
                                   the other's has started (1, default) or once it completed (0)  */
 /* Set an execution option (0/1 switches; sizes and counts where noted).  Results do not depend
@@ -356,7 +361,10 @@ int llm_gemm_i8_splitk_noalloc(int device, const int8_t *A, const int8_t *B, int
  * model kernel (w NULL: quantise only). */
 int llm_debug_norm_quant(int device, const float *x, const float *w, int rows, int cols, double eps,
                          int8_t *q, float *scales);
-/* int8 GEMM C = A . B^T with the model's GEMM kernel; splits forces split-K (0 = auto). */
+/* int8 GEMM C = A . B^T with the model's GEMM kernels.  splits >= 0: the warp-level kernel with
+ * that split-K (0 = auto); -1: the tcgen05 kernel at the model's channel tile, -bn: tile width
+ * bn; -(1000 + S): the tcgen05 kernel split over clusters of S = 2, 4 or 8 CTAs (the decode
+ * projections' form).  The same for llm_debug_gemm_f16. */
 int llm_debug_gemm_i8(int device, const int8_t *A, const int8_t *B, int M, int N, int K, int splits,
                       int32_t *C);
 /* 16-bit GEMM (dtype LLM_DTYPE_F16 / BF16; inputs given as fp32 and rounded) -> fp32 C. */

@@ -395,6 +395,23 @@ void oracle_gemm_mma(const float *A, const float *B, int M, int N, int K, int ac
   free(am); free(ae); free(bm); free(be);
 }
 
+/* The split-K form of oracle_gemm_mma (umma.cuh split-K clusters): S contiguous ranges of
+ * 64-element K slices, one chain each, summed in rank order (mma_dot16_split). */
+static float mma_dot16_split(const int16_t *am, const int16_t *ae, const int16_t *bm, const int16_t *be, int K,
+                             int mb2, int S);
+void oracle_gemm_mma_splitk(const float *A, const float *B, int M, int N, int K, int act, int S, float *Cout) {
+  const int mb = act == 1 ? 10 : 7;
+  int16_t *am, *ae, *bm, *be;
+  split_rows(A, (size_t)M * K, mb, &am, &ae);
+  split_rows(B, (size_t)N * K, mb, &bm, &be);
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int m = 0; m < M; m++)
+    for (int n = 0; n < N; n++)
+      Cout[(size_t)m * N + n] =
+          mma_dot16_split(am + (size_t)m * K, ae + (size_t)m * K, bm + (size_t)n * K, be + (size_t)n * K, K, 2 * mb, S);
+  free(am); free(ae); free(bm); free(be);
+}
+
 /* ane/stories/cpu.go:41-72 EmbedLookup: channel-first out[d][t] = embed[tokens[t]][d], a
  * token outside [0, vocab) zeroes its column (vocab = the table's rows). */
 void oracle_embed_lookup_cf(float *out, const float *embed, int vocab, const int32_t *tokens, int dim, int seq) {
@@ -438,6 +455,7 @@ struct oracle_model {
   float resid_scale; /* 0: x + branch (stories); else x + resid_scale * branch (storiesane) */
   int silu_form;     /* 0: h1 / (1 + exp(-h1)); 1: h1 * f32(1 / (1 + exp(-h1))) (storiesane) */
   int gpu;           /* 1: the CUDA path's order of operations (see oracle_model_set_gpu_order) */
+  int decode_splitk; /* GPU order: decode rows' projections split K (LLM_OPT_DECODE_SPLITK, default 1) */
   int16_t *lm_sm, *lm_se; /* GPU order: lm_head split for the MMA model */
 };
 
@@ -458,6 +476,8 @@ static void split_rows(const float *src, size_t n, int mb, int16_t **pm, int16_t
 static void mat_split(mat_t *mt, int mb) {
   if (mt->fp && !mt->sm) split_rows(mt->fp, (size_t)mt->rows * mt->cols, mb, &mt->sm, &mt->se);
 }
+
+void oracle_model_set_decode_splitk(oracle_model *m, int on) { m->decode_splitk = on ? 1 : 0; }
 
 void oracle_model_set_gpu_order(oracle_model *m, int on) {
   m->gpu = on && m->act ? 1 : 0;
@@ -525,6 +545,7 @@ oracle_model *oracle_model_new(const oracle_config *cfg, const oracle_weights_f3
   m->i8 = mode_int8(c->mode);
   m->q_dim = c->n_heads * c->head_dim;
   m->kv_dim = c->n_kv_heads * c->head_dim;
+  m->decode_splitk = 1;
   m->group = c->n_heads / c->n_kv_heads;
   size_t ne = (size_t)c->vocab * c->dim;
   if (m->act) {
@@ -735,40 +756,72 @@ static void matvec_i8(float *out, const mat_t *mt, const int8_t *qa, float sa) {
   }
 }
 
+/* Split-K plan of a decode step's projection (llm_cuda.cu decode_splits): the power of two
+ * <= min(4, K slices / 2, 128 / channel tiles at the widest tile), where a K slice is 128 bytes
+ * of the operand type and the widest tile is bnmax channels. */
+int oracle_decode_splits(int in8, int n, int k, int bnmax) {
+  const int nkt = k * (in8 ? 1 : 2) / 128;
+  const int tiles = (n + bnmax - 1) / bnmax;
+  int lim = 4;
+  if (nkt / 2 < lim) lim = nkt / 2;
+  if (128 / (tiles > 0 ? tiles : 1) < lim) lim = 128 / (tiles > 0 ? tiles : 1);
+  int sk = 1;
+  while (sk * 2 <= lim) sk *= 2;
+  return sk;
+}
+
+/* The MMA chain split over S contiguous ranges of 64-element (128-byte) K slices, CTA z taking
+ * slices [z*n/S, (z+1)*n/S), each range its own chain; the partial sums added in rank order,
+ * each addition rounded to nearest (umma.cuh split-K epilogue). */
+static float mma_dot16_split(const int16_t *am, const int16_t *ae, const int16_t *bm, const int16_t *be, int K,
+                             int mb2, int S) {
+  if (S <= 1) return mma_dot16(am, ae, bm, be, K, mb2);
+  const int nkt = K / 64;
+  float acc = 0.0f;
+  for (int z = 0; z < S; z++) {
+    const int k0 = z * nkt / S * 64, k1 = (z + 1) * nkt / S * 64;
+    const float pz = mma_dot16(am + k0, ae + k0, bm + k0, be + k0, k1 - k0, mb2);
+    acc = z == 0 ? pz : acc + pz;
+  }
+  return acc;
+}
+
 /* GPU order of a 16-bit matVec: every output row is the tensor-core MMA chain over the row
- * (instructions of 16 columns in order); rows pre-split, the input split once. */
-static void matvec_mma(float *out, const int16_t *wm, const int16_t *we, const float *in, int rows, int cols, int act) {
+ * (instructions of 16 columns in order), split over S ranges of K as above; rows pre-split, the
+ * input split once. */
+static void matvec_mma(float *out, const int16_t *wm, const int16_t *we, const float *in, int rows, int cols, int act,
+                       int S) {
   const int mb = act == 1 ? 10 : 7;
   int16_t *im = (int16_t *)malloc(sizeof(int16_t) * (size_t)cols), *ie = (int16_t *)malloc(sizeof(int16_t) * (size_t)cols);
   split16(in, cols, mb, im, ie);
 #pragma omp parallel for schedule(static)
   for (int r = 0; r < rows; r++)
-    out[r] = mma_dot16(wm + (size_t)r * cols, we + (size_t)r * cols, im, ie, cols, 2 * mb);
+    out[r] = mma_dot16_split(wm + (size_t)r * cols, we + (size_t)r * cols, im, ie, cols, 2 * mb, S);
   free(im);
   free(ie);
 }
 
-static void matvec_act(const oracle_model *m, float *out, const mat_t *mt, const float *in) {
-  if (m->gpu) matvec_mma(out, mt->sm, mt->se, in, mt->rows, mt->cols, m->act);
+static void matvec_act(const oracle_model *m, float *out, const mat_t *mt, const float *in, int S) {
+  if (m->gpu) matvec_mma(out, mt->sm, mt->se, in, mt->rows, mt->cols, m->act, S);
   else matvec_f32(out, mt->fp, in, mt->rows, mt->cols);
 }
 
 /* Linear layer on an activation vector that is already normalised (f32):
  * F32 mode: matVec as the reference; fp16/bf16: round the input, matVec on rounded weights;
  * W8A8: quantise the input per token, int8 matVec. `in` is rounded in place. */
-static void linear(oracle_seq *s, float *out, const mat_t *mt, float *in) {
+static void linear(oracle_seq *s, float *out, const mat_t *mt, float *in, int S) {
   const oracle_model *m = s->m;
   if (m->i8) {
     float sa = quant_row(in, mt->cols, s->qa);
     matvec_i8(out, mt, s->qa, sa);
   } else {
     round_vec(m->act, in, mt->cols);
-    matvec_act(m, out, mt, in);
+    matvec_act(m, out, mt, in, S);
   }
 }
 
 /* Two linears sharing the same (normalised) input, quantised/rounded once. */
-static void linear2(oracle_seq *s, float *o1, const mat_t *m1, float *o2, const mat_t *m2, float *in) {
+static void linear2(oracle_seq *s, float *o1, const mat_t *m1, float *o2, const mat_t *m2, float *in, int S) {
   const oracle_model *m = s->m;
   if (m->i8) {
     float sa = quant_row(in, m1->cols, s->qa);
@@ -776,8 +829,8 @@ static void linear2(oracle_seq *s, float *o1, const mat_t *m1, float *o2, const 
     matvec_i8(o2, m2, s->qa, sa);
   } else {
     round_vec(m->act, in, m1->cols);
-    matvec_act(m, o1, m1, in);
-    matvec_act(m, o2, m2, in);
+    matvec_act(m, o1, m1, in, S);
+    matvec_act(m, o2, m2, in, S);
   }
 }
 
@@ -1069,6 +1122,12 @@ int oracle_forward(const oracle_model *m, oracle_seq *s, int token, int pos, flo
 
   if (token < 0 || token >= c->vocab) memset(s->x, 0, sizeof(float) * (size_t)D);
   else memcpy(s->x, m->embed + (size_t)token * D, sizeof(float) * (size_t)D);
+  /* GPU order: a decode step's 16-bit residual projections (Wo, W2) split K
+   * (oracle_decode_splits); QKV, W1/W3, prefill rows and int8 (exact either way) do not */
+  const int dec = m->gpu && m->decode_splitk && !m->i8 && pos >= s->n_prefill;
+  const int sp_qkv = 1, sp_w13 = 1;
+  const int sp_wo = dec ? oracle_decode_splits(m->i8, D, m->q_dim, 256) : 1;
+  const int sp_w2 = dec ? oracle_decode_splits(m->i8, D, F, 256) : 1;
   for (int l = 0; l < c->n_layers; l++) {
     const layer_t *L = &m->layers[l];
     norm_vec(m, s->xn, s->x, L->rms_att, D);
@@ -1079,9 +1138,9 @@ int oracle_forward(const oracle_model *m, oracle_seq *s, int token, int pos, flo
       matvec_i8(s->v, &L->wv, s->qa, sa);
     } else {
       round_vec(m->act, s->xn, D);
-      matvec_act(m, s->q, &L->wq, s->xn);
-      matvec_act(m, s->k, &L->wk, s->xn);
-      matvec_act(m, s->v, &L->wv, s->xn);
+      matvec_act(m, s->q, &L->wq, s->xn, sp_qkv);
+      matvec_act(m, s->k, &L->wk, s->xn, sp_qkv);
+      matvec_act(m, s->v, &L->wv, s->xn, sp_qkv);
     }
     if (c->qk_norm) {
       for (int h = 0; h < c->n_heads; h++) qk_norm_head(m, s->q + (size_t)h * hd, L->q_norm);
@@ -1107,14 +1166,14 @@ int oracle_forward(const oracle_model *m, oracle_seq *s, int token, int pos, flo
     }
     if (m->gpu) attend_gpu(s, l, pos);
     else attend(s, l, pos);
-    linear(s, s->x2, &L->wo, s->att);
+    linear(s, s->x2, &L->wo, s->att, sp_wo);
     if (m->resid_scale != 0.0f) /* ane/storiesane/accel_other.go:60-64: base + scale*branch */
       for (int i = 0; i < D; i++) s->x2[i] = s->x[i] + m->resid_scale * s->x2[i];
     else
       for (int i = 0; i < D; i++) s->x2[i] += s->x[i];
 
     norm_vec(m, s->xn, s->x2, L->rms_ffn, D);
-    linear2(s, s->h1, &L->w1, s->h3, &L->w3, s->xn);
+    linear2(s, s->h1, &L->w1, s->h3, &L->w3, s->xn, sp_w13);
     if (m->gpu)
       for (int i = 0; i < F; i++) s->g[i] = gate_gpu(s->h1[i], s->h3[i], m->silu_form);
     else if (m->silu_form) /* ane/storiesane/accel_other.go:66-71 */
@@ -1124,7 +1183,7 @@ int oracle_forward(const oracle_model *m, oracle_seq *s, int token, int pos, flo
       }
     else
       for (int i = 0; i < F; i++) s->g[i] = oracle_silu(s->h1[i]) * s->h3[i];
-    linear(s, s->y, &L->w2, s->g);
+    linear(s, s->y, &L->w2, s->g, sp_w2);
     if (m->resid_scale != 0.0f)
       for (int i = 0; i < D; i++) s->x[i] = s->x2[i] + m->resid_scale * s->y[i];
     else
@@ -1137,7 +1196,7 @@ int oracle_forward(const oracle_model *m, oracle_seq *s, int token, int pos, flo
   }
   norm_vec(m, s->xn, s->x, m->rms_final, D);
   round_vec(m->act, s->xn, D);
-  if (m->gpu) matvec_mma(s->logits, m->lm_sm, m->lm_se, s->xn, c->vocab, D, m->act);
+  if (m->gpu) matvec_mma(s->logits, m->lm_sm, m->lm_se, s->xn, c->vocab, D, m->act, 1);
   else matvec_f32(s->logits, m->lm_head, s->xn, c->vocab, D);
   if (logits_out) memcpy(logits_out, s->logits, sizeof(float) * (size_t)c->vocab);
   return ORACLE_OK;

@@ -106,6 +106,14 @@ void oracle_model_set_storiesane(oracle_model *m, int on);
  *     order (64-position tiles, lazy reference max), later positions in the decode kernel's
  *     (32-page segments, 4 warps, fixed fold order). */
 void oracle_model_set_gpu_order(oracle_model *m, int on);
+/* GPU order: whether a decode step's 16-bit residual projections (Wo, W2) split K over
+ * clusters (the library's LLM_OPT_DECODE_SPLITK, default on), and the split of such a
+ * projection: out channels n, input k, widest channel tile bnmax (256). */
+void oracle_model_set_decode_splitk(oracle_model *m, int on);
+int oracle_decode_splits(int in8, int n, int k, int bnmax);
+/* C[m][n] of oracle_gemm_mma with K split into S ranges of 64-element slices (one MMA chain
+ * each, partials added in range order, each addition rounded to nearest). */
+void oracle_gemm_mma_splitk(const float *A, const float *B, int M, int N, int K, int act, int S, float *Cout);
 void oracle_model_free(oracle_model *m);
 oracle_seq *oracle_seq_new(const oracle_model *m);
 void oracle_seq_free(oracle_seq *s);

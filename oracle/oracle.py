@@ -70,6 +70,10 @@ def lib() -> C.CDLL:
         "oracle_model_free": (None, [C.c_void_p]),
         "oracle_model_set_storiesane": (None, [C.c_void_p, C.c_int]),
         "oracle_model_set_gpu_order": (None, [C.c_void_p, C.c_int]),
+        "oracle_model_set_decode_splitk": (None, [C.c_void_p, C.c_int]),
+        "oracle_decode_splits": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int]),
+        "oracle_gemm_mma_splitk": (None, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                          C.c_void_p]),
         "oracle_seq_set_prefill": (None, [C.c_void_p, C.c_int]),
         "oracle_seq_set_logits_from": (None, [C.c_void_p, C.c_int]),
         "oracle_exp2_det": (C.c_float, [C.c_float]),
@@ -122,7 +126,8 @@ def f32(a):
 class Model:
     """oracle_model over fp32 weights given as a dict or as ane.stories.ModelWeights."""
 
-    def __init__(self, cfg: dict, weights, mode: str = "fp32", storiesane: bool = False, gpu_order: bool = False):
+    def __init__(self, cfg: dict, weights, mode: str = "fp32", storiesane: bool = False, gpu_order: bool = False,
+                 decode_splitk: bool = True):
         """gpu_order: restate the CUDA path's order of operations (bit-identical results in
         the emulation modes); default: the reference's arithmetic at the mode's precision."""
         self.cfg = dict(cfg)
@@ -154,6 +159,8 @@ class Model:
         self.gpu_order = bool(gpu_order) and mode != "fp32"
         if self.gpu_order:
             lib().oracle_model_set_gpu_order(self.h, 1)
+            # decode rows' projections split K as the library's default (LLM_OPT_DECODE_SPLITK)
+            lib().oracle_model_set_decode_splitk(self.h, 1 if decode_splitk else 0)
 
     def eval_window(self, tokens) -> np.ndarray:
         """ane/storiesane/engine.go:804-842: logits of every window position, channel-first
@@ -284,6 +291,23 @@ def gemm_mma(A, B, act: int):
     Cm = np.zeros((A.shape[0], B.shape[0]), np.float32)
     lib().oracle_gemm_mma(_p(A), _p(B), A.shape[0], B.shape[0], A.shape[1], act, _p(Cm))
     return Cm
+
+
+def gemm_mma_splitk(A, B, act: int, splits: int):
+    """oracle_gemm_mma_splitk: the MMA chains of gemm_mma over `splits` contiguous ranges of
+    64-element K slices, summed in range order."""
+    A = f32(A)
+    B = f32(B)
+    M, K = A.shape
+    N = B.shape[0]
+    out = np.zeros((M, N), np.float32)
+    lib().oracle_gemm_mma_splitk(_p(A), _p(B), M, N, K, act, splits, _p(out))
+    return out
+
+
+def decode_splits(in8: bool, n: int, k: int, bnmax: int) -> int:
+    """Split-K of a decode step's projection (oracle_decode_splits)."""
+    return int(lib().oracle_decode_splits(1 if in8 else 0, n, k, bnmax))
 
 
 def embed_lookup_cf(embed, tokens, dim: int, seq: int):

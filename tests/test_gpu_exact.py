@@ -47,6 +47,37 @@ def test_gemm_kernels_follow_the_tensor_core_model(act, path, kind):
     assert bad == 0, f"{bad} of {C.size} outputs differ from the model"
 
 
+@pytest.mark.parametrize("act,M,N,K,S", [(1, 64, 768, 2048, 8), (2, 128, 1024, 3072, 8), (2, 37, 256, 1024, 4),
+                                         (1, 128, 2304, 768, 4), (2, 5, 512, 384, 2), (1, 100, 96, 512, 4)])
+def test_split_k_gemm_follows_the_model(act, M, N, K, S):
+    """Decode projections split K over clusters of S CTAs (contiguous ranges of 64-element
+    slices, one MMA chain each, the partial tiles summed in rank order through distributed
+    shared memory): every output bit-identical to O.gemm_mma_splitk."""
+    rng = np.random.default_rng(M + N + K + S + act)
+    A = _act_values(rng, (M, K), act, "normal")
+    B = _act_values(rng, (N, K), act, "wide")
+    C = np.zeros((M, N), np.float32)
+    _abi.check(_abi.lib().llm_debug_gemm_f16(0, act, _abi.ptr(A), _abi.ptr(B), M, N, K, -(1000 + S), _abi.ptr(C)))
+    want = O.gemm_mma_splitk(A, B, act, S)
+    bad = np.count_nonzero(C.view(np.uint32) != want.view(np.uint32))
+    assert bad == 0, f"{bad} of {C.size} outputs differ from the model"
+    if S > 1:  # the split changes the rounding (the model tells which)
+        assert np.count_nonzero(want.view(np.uint32) != O.gemm_mma(A, B, act).view(np.uint32)) > 0
+
+
+@pytest.mark.parametrize("M,N,K,S", [(64, 768, 2048, 8), (256, 1024, 3072, 8), (7, 384, 768, 2), (130, 512, 1024, 4)])
+def test_split_k_int8_gemm_exact(M, N, K, S):
+    """int8 split-K partials are int32 sums: the result is the exact product."""
+    import ctypes as C_
+    rng = np.random.default_rng(M * 3 + S)
+    A = rng.integers(-128, 128, (M, K), dtype=np.int8)
+    B = rng.integers(-128, 128, (N, K), dtype=np.int8)
+    out = np.zeros((M, N), np.int32)
+    _abi.check(_abi.lib().llm_debug_gemm_i8(0, _abi.ptr(A, C_.c_int8), _abi.ptr(B, C_.c_int8), M, N, K, -(1000 + S),
+                                            _abi.ptr(out, C_.c_int32)))
+    np.testing.assert_array_equal(out, A.astype(np.int64) @ B.astype(np.int64).T)
+
+
 def test_device_exp2_equals_oracle():
     rng = np.random.default_rng(3)
     x = np.concatenate([np.linspace(-130, 130, 20001), rng.uniform(-30, 1, 20000), [-np.inf, np.inf, 0.0, -126.0,
