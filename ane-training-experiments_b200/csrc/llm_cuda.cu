@@ -385,7 +385,21 @@ cudaError_t umma_launch_t(const CUtensorMap& tx, const CUtensorMap& tw, const Ge
                           bool prepare) {
   constexpr int smem = umma_smem_bytes<BN>();
   static_assert(smem <= 200 * 1024, "stage ring exceeds the shared-memory budget");
-  auto k = umma_gemm_kernel<InT, OutT, BN, EPI>;
+  // split-K clusters (k_splits > 1) run their own instantiation: residual and plain outputs
+  constexpr bool kSplittable = EPI == EPI_RESID || EPI == EPI_F32 || EPI == EPI_S32;
+  auto k = umma_gemm_kernel<InT, OutT, BN, EPI, false>;
+  if constexpr (kSplittable) {
+    auto ks = umma_gemm_kernel<InT, OutT, BN, EPI, true>;
+    if (prepare) {
+      const cudaError_t e = cudaFuncSetAttribute(ks, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return e;
+    } else if (p.k_splits > 1) {
+      (void)cudaGetLastError();
+      return launch_pdl(ks, grid, dim3(kUmmaThreads), umma_smem_bytes_for<BN>(p.stages), s, tx, tw, p);
+    }
+  } else {
+    if (!prepare && p.k_splits > 1) return cudaErrorInvalidValue;
+  }
   if (prepare) return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   (void)cudaGetLastError();  // launch errors below must be this launch's own
   return launch_pdl(k, grid, dim3(kUmmaThreads), umma_smem_bytes_for<BN>(p.stages), s, tx, tw, p);
@@ -1374,7 +1388,7 @@ int gemm(llm_ctx* c, bool in8, int epi, GemmParams p, cudaStream_t stream = null
     }
     // split-K over a cluster of k_splits CTAs (decode rows): the narrowest channel tile whose
     // grid, times the splits, still fits one CTA per SM
-    const int ksplit = p.k_splits > 1 && (epi == EPI_QKV || epi == EPI_RESID || epi == EPI_SWIGLU) ? p.k_splits : 1;
+    const int ksplit = p.k_splits > 1 && epi == EPI_RESID ? p.k_splits : 1;
     // (two splits: tiles up to 128 channels, so the partial and summed tiles fit the ring)
     // (one wave: clusters of two pack 144 of the 148 SMs, larger ones 128)
     const int wave = ksplit == 1 ? c->n_sm : std::min(c->n_sm, ksplit == 2 ? 144 : kSplitPlanSMs);
@@ -1600,7 +1614,6 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
     p.trace = tr("qkv", l, P);
     t_prio = prio;
     t_use_pdl = chain_pdl;
-    p.k_splits = decode_rows ? decode_splits(c, EPI_QKV, p.N, p.K, overlap) : 1;
     return gemm(c, i8, EPI_QKV, p, P.s, ring_kb);
   };
 
@@ -1721,7 +1734,6 @@ int enqueue_forward(llm_ctx* c, const RowsSpec& rs) {
       p.trace = tr("w13", l, P);
       t_prio = prio;
       t_use_pdl = chain_pdl;
-      p.k_splits = decode_rows ? decode_splits(c, EPI_SWIGLU, p.N, p.K, overlap) : 1;
       RC(gemm(c, i8, EPI_SWIGLU, p, P.s, ring_kb));
       RC(mark("w13_gemm+swiglu"));
     }

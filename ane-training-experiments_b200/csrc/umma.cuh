@@ -234,7 +234,9 @@ __device__ __forceinline__ void splitk_reduce(uint32_t part_s, uint32_t red_s, i
   }
 }
 
-template <typename InT, typename OutT, int BN, int EPI>
+// SPLIT: the split-K cluster form (k_splits > 1); a separate instantiation, so the whole-K
+// kernels carry none of its registers.
+template <typename InT, typename OutT, int BN, int EPI, bool SPLIT = false>
 __global__ void __launch_bounds__(kUmmaThreads, 2)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, GemmParams p) {
   constexpr bool I8 = sizeof(InT) == 1;
@@ -260,7 +262,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
   // Split-K (k_splits > 1): the CTAs blockIdx.z = 0 .. k_splits-1 of one cluster take
   // contiguous ranges of the 128-byte K slices and exchange their partial tiles through
   // distributed shared memory (splitk_epilogue below).
-  const int n_split = p.k_splits > 1 ? p.k_splits : 1;
+  const int n_split = SPLIT && p.k_splits > 1 ? p.k_splits : 1;
   const int nkt_all = p.K * ESZ / 128;
   const int kt0 = static_cast<int>(blockIdx.z) * nkt_all / n_split;
   const int nkt = (static_cast<int>(blockIdx.z) + 1) * nkt_all / n_split - kt0;  // this CTA's slices
@@ -316,7 +318,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
       }
     }
     __syncwarp();
-    if (n_split > 1) cluster_sync_all();  // partial tiles written (splitk epilogue)
+    if (SPLIT && n_split > 1) cluster_sync_all();  // partial tiles written (splitk epilogue)
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
@@ -338,14 +340,14 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
       tc_commit(smem_u32(&accum_bar));
     }
     __syncwarp();
-    if (n_split > 1) cluster_sync_all();
+    if (SPLIT && n_split > 1) cluster_sync_all();
   } else {
     // ---------------------------------------------------------------- epilogue (warps 2..5)
     const int q = warp & 3;              // TMEM lane quadrant
     const int et = threadIdx.x - 64;     // 0..127 among epilogue threads
     // Split-K: cluster CTA z finishes rows z*RP .. z*RP+RP-1 of the tile (RP = 128 / k_splits)
     // from every CTA's partial; the per-row epilogue (QKV) runs on threads et < RP.
-    const bool split = n_split > 1;
+    const bool split = SPLIT && n_split > 1;
     const int RP = kUmmaTokens / n_split;
     const bool row_owner = !split || et < RP;
     const int tl = split ? static_cast<int>(blockIdx.z) * RP + et % RP : q * 32 + lane;  // token within the tile
@@ -423,10 +425,12 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
       }
       cluster_sync_all();
       const int row0 = static_cast<int>(blockIdx.z) * RP;
-      if (ok) {
-        if (n_split == 2) splitk_reduce<2, I8, PP>(part_s, red_s, row0, RP, BN / 4, et);
-        else if (n_split == 4) splitk_reduce<4, I8, PP>(part_s, red_s, row0, RP, BN / 4, et);
-        else splitk_reduce<8, I8, PP>(part_s, red_s, row0, RP, BN / 4, et);
+      if constexpr (SPLIT) {
+        if (ok) {
+          if (n_split == 2) splitk_reduce<2, I8, PP>(part_s, red_s, row0, RP, BN / 4, et);
+          else if (n_split == 4) splitk_reduce<4, I8, PP>(part_s, red_s, row0, RP, BN / 4, et);
+          else splitk_reduce<8, I8, PP>(part_s, red_s, row0, RP, BN / 4, et);
+        }
       }
       epi_bar();  // the summed rows are visible to every epilogue thread
     }
@@ -795,7 +799,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
   }
   if (failed && p.err) atomicExch(p.err, kDevWaitTimeout);
   // split-K: no CTA leaves while another may still read its partial tile
-  if (n_split > 1) cluster_sync_all();
+  if (SPLIT && n_split > 1) cluster_sync_all();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
