@@ -240,6 +240,7 @@ template <typename InT, typename OutT, int BN, int EPI, bool SPLIT = false>
 __global__ void __launch_bounds__(kUmmaThreads, 2)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, GemmParams p) {
   constexpr bool I8 = sizeof(InT) == 1;
+  static_assert(!SPLIT || EPI == EPI_RESID || EPI == EPI_F32 || EPI == EPI_S32, "split-K: elementwise epilogues");
   constexpr int MAX_STAGES = umma_stages<BN>();
   const int STAGES = p.stages > 0 && p.stages < MAX_STAGES ? p.stages : MAX_STAGES;
   constexpr int A_BYTES = kUmmaTokens * 128;
@@ -346,13 +347,12 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
     const int q = warp & 3;              // TMEM lane quadrant
     const int et = threadIdx.x - 64;     // 0..127 among epilogue threads
     // Split-K: cluster CTA z finishes rows z*RP .. z*RP+RP-1 of the tile (RP = 128 / k_splits)
-    // from every CTA's partial; the per-row epilogue (QKV) runs on threads et < RP.
+    // from every CTA's partial.
     const bool split = SPLIT && n_split > 1;
     const int RP = kUmmaTokens / n_split;
-    const bool row_owner = !split || et < RP;
-    const int tl = split ? static_cast<int>(blockIdx.z) * RP + et % RP : q * 32 + lane;  // token within the tile
+    const int tl = q * 32 + lane;        // token within the tile (= TMEM lane)
     const int tok = tok0 + tl;
-    const bool tok_ok = tok < p.M && row_owner;
+    const bool tok_ok = tok < p.M;
     const int tokc = tok_ok ? tok : p.M - 1;
     const uint32_t trow = tmem + (static_cast<uint32_t>(q * 32) << 16);
     griddep_wait();  // positions, scales and the residual come from earlier kernels
@@ -434,7 +434,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
       }
       epi_bar();  // the summed rows are visible to every epilogue thread
     }
-    // the summed partials of columns col..col+3 of tile row `row` of this CTA (split-K only)
+    // the summed partials of columns col..col+3 of tile row `row` of this CTA (split-K)
     auto split_sum4 = [&](int row, int col, uint32_t (&r)[4]) {
       uint4 v;
       asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];\n"
@@ -447,17 +447,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
     // dequantised chunk c (columns 32c..32c+31 of this token's row)
     auto load_chunk = [&](int c, float (&v)[32]) {
       uint32_t r[32];
-      if (split) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          uint32_t r4[4] = {0u, 0u, 0u, 0u};
-          if (c * 32 + j < BN && row_owner) split_sum4(tl, c * 32 + j, r4);
-          r[j] = r4[0]; r[j + 1] = r4[1]; r[j + 2] = r4[2]; r[j + 3] = r4[3];
-        }
-      } else {
-        tmem_ld32(trow + c * 32, r);
-        tmem_wait_ld();
-      }
+      tmem_ld32(trow + c * 32, r);
+      tmem_wait_ld();
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         if constexpr (I8) v[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), a_s), s_bsc[(c * 32 + j) % BN]);
@@ -479,12 +470,11 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
       *reinterpret_cast<float4*>(stg + tl * SP + col) = make_float4(a, b, c_, d);
     };
 
-    if (split && (EPI == EPI_RESID || EPI == EPI_SWIGLU || EPI == EPI_F32 || EPI == EPI_S32)) {
-      // Split-K residual / SwiGLU / plain outputs: elementwise over this CTA's RP rows, four
-      // consecutive channels per item (consecutive threads on consecutive channels: coalesced).
-      if constexpr (EPI == EPI_RESID || EPI == EPI_SWIGLU || EPI == EPI_F32 || EPI == EPI_S32) {
+    if (split) {
+      // Split-K residual / plain outputs: elementwise over this CTA's RP rows, four consecutive
+      // channels per item (consecutive threads on consecutive channels: coalesced).
+      if constexpr (SPLIT) {
         constexpr int C4 = BN / 4;
-        const int F = p.N / 2;
         for (int idx = et; idx < RP * C4; idx += 128) {
           const int row = static_cast<int>(blockIdx.z) * RP + idx / C4, col = 4 * (idx % C4);
           const int t = tok0 + row, ch = ch0 + col;
@@ -513,16 +503,6 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
             *reinterpret_cast<float4*>(dst) =
                 make_float4(resid_add(v[0], rv.x, p.resid_scale), resid_add(v[1], rv.y, p.resid_scale),
                             resid_add(v[2], rv.z, p.resid_scale), resid_add(v[3], rv.w, p.resid_scale));
-          } else {
-            // interleaved rows: channel 2i is W1 row i (gate), 2i+1 is W3 row i (up)
-            const float g0 = swiglu_pair(v[0], v[1], p.silu_form), g1 = swiglu_pair(v[2], v[3], p.silu_form);
-            const int j0 = ch / 2;
-            if (p.swiglu_f32) {
-              *reinterpret_cast<float2*>(reinterpret_cast<float*>(p.out) + static_cast<size_t>(t) * F + j0) = make_float2(g0, g1);
-            } else {
-              *reinterpret_cast<uint32_t*>(reinterpret_cast<OutT*>(p.out) + static_cast<size_t>(t) * F + j0) =
-                  ActTraits<OutT>::pack2(g0, g1);
-            }
           }
         }
       }
