@@ -93,7 +93,8 @@ constexpr int attn_min_blocks() { return HD >= 128 ? 3 : LLM_ATTN_MINB_HD64; }
 #define LLM_ATTN_STAGES_HD128 2
 #endif
 // head_dim 64: two pages as well (32 KB per CTA): 28.4 vs 36.3 us per Stories110M layer at 256
-// sequences x ~160 positions against four pages (short contexts want more CTAs per SM).
+// sequences x ~160 positions against four pages (short contexts want more CTAs per SM); three
+// pages at four CTAs per SM measured slower too (Stories W8A8 decode step 0.925 vs 0.904 ms).
 #ifndef LLM_ATTN_STAGES_HD64
 #define LLM_ATTN_STAGES_HD64 2
 #endif
