@@ -69,7 +69,7 @@ def _run(world, n_total, steps, tmp_path, skip=()):
 
 
 two_gpus = pytest.mark.skipif(
-    __import__("torch").cuda.device_count() < 2, reason="needs two GPUs on the box (gpurun --gpus 2)")
+    __import__("torch").cuda.device_count() < 2, reason="needs two GPUs")
 
 
 @two_gpus
