@@ -14,7 +14,12 @@
 // that the grid is about one CTA per SM and every CTA streams its share of W through a
 // ~192 KB stage ring (4..11 stages) with all stages in flight.  Grid x = token tile (fastest,
 // so the CTAs that share a weight tile run side by side and the second one reads it from
-// L2), y = channel tile.
+// L2), y = channel tile.  One SM streams only ~50 GB/s into shared memory, and a decode CTA
+// loads the whole activation tile for its few channels, so the long-K narrow-N residual
+// projections of the 16-bit models split K over a thread-block cluster (z = split, SPLIT
+// instantiation): each CTA runs its own MMA chain over a contiguous range of K slices, and after
+// a cluster barrier finishes 128/S rows of the tile by adding the S partial tiles, read from
+// the CTAs' shared memory through the cluster, in rank order (splitk_reduce).
 //
 // Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM allocator + MMA issuer
 // (one elected thread), warps 2..5 = epilogue.  Epilogue warp w reads TMEM lanes
@@ -262,7 +267,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
   const int tok0 = blockIdx.x * kUmmaTokens, ch0 = blockIdx.y * BN;
   // Split-K (k_splits > 1): the CTAs blockIdx.z = 0 .. k_splits-1 of one cluster take
   // contiguous ranges of the 128-byte K slices and exchange their partial tiles through
-  // distributed shared memory (splitk_epilogue below).
+  // distributed shared memory (splitk_reduce and the split epilogue below).
   const int n_split = SPLIT && p.k_splits > 1 ? p.k_splits : 1;
   const int nkt_all = p.K * ESZ / 128;
   const int kt0 = static_cast<int>(blockIdx.z) * nkt_all / n_split;
