@@ -244,11 +244,12 @@ int llm_debug_sample(int device, const float *logits, int rows, int vocab, float
                                    0 = the mma.sync tile kernel (default 1)                   */
 #define LLM_OPT_PREFILL_PERSIST 16  /* projections of >= 1024-row chunks on the persistent tcgen05
                                        kernel (double-buffered TMEM accumulators; default 1) */
-#define LLM_OPT_DECODE_SPLITK 17 /* decode steps' projections split K over a cluster of CTAs whose
-                                    partial tiles are summed in rank order through distributed
-                                    shared memory (default 1; the split per projection is fixed
-                                    by its shape, so results do not depend on the batch; fp16 /
-                                    bf16 rounding differs from 0, int8 results do not) */
+#define LLM_OPT_DECODE_SPLITK 17 /* fp16 / bf16 models: a decode step's residual projections (Wo,
+                                    W2) split K over a cluster of 2-4 CTAs whose partial tiles
+                                    are summed in rank order through distributed shared memory
+                                    (default 1; the split per projection is fixed by its shape,
+                                    so results do not depend on the batch; the rounding differs
+                                    from 0; int8 models never split) */
 #define LLM_OPT_ATTN_CHAIN 7   /* overlap mode: a micro-batch's attention launch starts once every CTA of
                                   the other's has started (1, default) or once it completed (0)  */
 /* Set an execution option (0/1 switches; sizes and counts where noted).  Results do not depend
