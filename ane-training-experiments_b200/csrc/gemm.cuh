@@ -67,6 +67,8 @@ struct GemmParams {
   // tcgen05 GEMM: stage-ring depth (0 = the kernel's maximum); fewer stages need less shared
   // memory, which lets a GEMM CTA share an SM with an attention CTA
   int stages;
+  // tcgen05 QKV: token rows per tile (64 or 0 = 128)
+  int a_rows;
   TraceRec* trace;  // llm_trace_step (tcgen05 GEMM only)
   // storiesane arithmetic (ane/storiesane/residual.go:9, accel_other.go:60-71):
   // EPI_RESID out = resid + resid_scale * y when resid_scale != 0 (0 = out = y + resid);

@@ -561,6 +561,9 @@ struct LayerW {
   float *rms_att = nullptr, *rms_ffn = nullptr, *q_norm = nullptr, *k_norm = nullptr;
 };
 
+#ifndef LLM_QKV_TILE64_DEFAULT
+#define LLM_QKV_TILE64_DEFAULT 1
+#endif
 struct GraphKey {
   int n, splits, mode;  // mode: 0 = step, 1 = step + logits, 2 = generate
   bool operator<(const GraphKey& o) const { return std::tie(n, splits, mode) < std::tie(o.n, o.splits, o.mode); }
@@ -643,6 +646,7 @@ struct llm_ctx {
   int overlap_ring_kb = 64;   // tcgen05 stage ring in overlap mode: fits beside two attention CTAs
   int attn_splits = 0;        // decode attention splits per sequence (0 = chosen per batch)
   bool decode_splitk = true;  // LLM_OPT_DECODE_SPLITK
+  bool qkv_tile64 = LLM_QKV_TILE64_DEFAULT;  // 64-token QKV tiles when the grid allows
   bool null_tokens = false;   // llm_eval_window: token id -1 = a zero embedding row
   // how one micro-batch's attention launch waits for the other's: 0 = its completion,
   // 1 = all of its CTAs having started (launch-completion event)
@@ -1413,13 +1417,17 @@ int gemm(llm_ctx* c, bool in8, int epi, GemmParams p, cudaStream_t stream = null
       const int want = std::max(need, p.stages > 0 ? std::min(p.stages, slices) : slices);
       p.stages = std::max(2, want);
     }
-    const CUtensorMap* tx = tmap(c, p.A, esz, p.K, p.M, kUmmaTokens);
+    // QKV of more than 64 tokens: 64-token tiles when twice the grid still fits one CTA per
+    // SM (each CTA then loads half the activation bytes per K slice)
+    const long long tiles_n = (p.N + bn - 1) / bn;
+    p.a_rows = epi == EPI_QKV && c->qkv_tile64 && p.M > 64 && (p.M + 63) / 64 * tiles_n <= c->n_sm ? 64 : kUmmaTokens;
+    const CUtensorMap* tx = tmap(c, p.A, esz, p.K, p.M, p.a_rows);
     const CUtensorMap* tw = tmap(c, p.B, esz, p.K, p.N, bn);
     if (!tw || !tx) return LLM_ERR_CUDA;
     p.k_splits = ksplit;
     p.k_tiles_per_split = p.K * esz / 128 / ksplit;
     p.err = c->d_err;
-    dim3 grid((p.M + kUmmaTokens - 1) / kUmmaTokens, (p.N + bn - 1) / bn, ksplit);
+    dim3 grid((p.M + p.a_rows - 1) / p.a_rows, (p.N + bn - 1) / bn, ksplit);
     t_cluster_z = ksplit;
     const cudaError_t e = umma_any(c->act, in8, *tx, *tw, p, epi, bn, grid, stream, false);
     t_cluster_z = 1;

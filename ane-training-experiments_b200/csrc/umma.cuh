@@ -264,7 +264,12 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
 
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tok0 = blockIdx.x * kUmmaTokens, ch0 = blockIdx.y * BN;
+  // QKV tiles of 64 tokens (a_rows == 64, chosen when the grid has SMs to spare): the CTA loads
+  // only its 64 activation rows per K slice (a 64-row box), the MMA still forms 128 rows, and
+  // rows 64..127 of the accumulator are never read.
+  const int TR = EPI == EPI_QKV && p.a_rows == 64 ? 64 : kUmmaTokens;
+  const uint32_t LOAD_BYTES = TR * 128 + BN * 128;
+  const int tok0 = blockIdx.x * TR, ch0 = blockIdx.y * BN;
   // Split-K (k_splits > 1): the CTAs blockIdx.z = 0 .. k_splits-1 of one cluster take
   // contiguous ranges of the 128-byte K slices and exchange their partial tiles through
   // distributed shared memory (splitk_reduce and the split epilogue below).
@@ -303,7 +308,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
       const int pre = min(nkt, STAGES);
       for (int i = 0; i < pre; ++i) {
         const uint32_t st = sbase + i * STAGE_BYTES;
-        mbar_arrive_expect_tx(smem_u32(&full_bar[i]), STAGE_BYTES);
+        mbar_arrive_expect_tx(smem_u32(&full_bar[i]), LOAD_BYTES);
         tma_load_2d(st + A_BYTES, &tmW, (kt0 + i) * (128 / ESZ), ch0, smem_u32(&full_bar[i]));
       }
       griddep_wait();
@@ -318,7 +323,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
         }
         const uint32_t st = sbase + s * STAGE_BYTES;
         const int kx = (kt0 + i) * (128 / ESZ);  // element coordinate of the K slice
-        mbar_arrive_expect_tx(smem_u32(&full_bar[s]), STAGE_BYTES);
+        mbar_arrive_expect_tx(smem_u32(&full_bar[s]), LOAD_BYTES);
         tma_load_2d(st + A_BYTES, &tmW, kx, ch0, smem_u32(&full_bar[s]));
         tma_load_2d(st, &tmX, kx, tok0, smem_u32(&full_bar[s]));
       }
@@ -357,7 +362,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
     const int RP = kUmmaTokens / n_split;
     const int tl = q * 32 + lane;        // token within the tile (= TMEM lane)
     const int tok = tok0 + tl;
-    const bool tok_ok = tok < p.M;
+    const bool tok_ok = tl < TR && tok < p.M;
     const int tokc = tok_ok ? tok : p.M - 1;
     const uint32_t trow = tmem + (static_cast<uint32_t>(q * 32) << 16);
     griddep_wait();  // positions, scales and the residual come from earlier kernels
